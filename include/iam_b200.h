@@ -1,0 +1,114 @@
+/*
+ * iam_b200.h -- C ABI of libiamb200.so, the B200 (sm_100a) implementation of the
+ * Effort-style dynamic-sparse decode path of Guziuk/Input-Adaptive-Matrix-Inference-
+ * Optimization.
+ *
+ * Conventions (all entry points):
+ *   - every function returns an int status (IAM_OK = 0, else an IAM_ERR_* code);
+ *     iam_last_error() returns a message for the calling thread's last failure;
+ *   - pointers named *_dev are device pointers owned by the caller; nothing here
+ *     frees or keeps them beyond the documented lifetime;
+ *   - work is enqueued on the given cudaStream_t (passed as void*, 0 = legacy default)
+ *     and is asynchronous; nothing synchronises unless documented;
+ *   - a handle (iam_bucketmul_t, iam_model_t) owns its scratch memory, so one handle per
+ *     stream is safe; a single handle is not re-entrant across streams (the reference's
+ *     singleton BucketMul::shared is not re-entrant either, bucket_mul.hpp:119-122).
+ *
+ * Bucket weight layout (the reference's on-disk contract, preprocess_layer_fixed_gpu.py:
+ * 110-282): for W[out_dim][in_dim] fp16, C = out_dim/16 bucket columns and R = 16*in_dim
+ * bucket rows; buckets[R][C] u16 where row i*16+r holds the rank-r (|w| descending) value
+ * of each 16-output bucket with its original slot in the low 4 mantissa bits; stats[R][4]
+ * u16 fp16 mean |value| per bucket row (channel 3 is used, bucketMul.cl:372); probes[in_dim]
+ * u16 fp16 mean |W[:,i]|.  stats_stride = 4 reads that file layout directly, 1 reads a
+ * packed channel-3 array (iam_stats_pack).
+ */
+#ifndef IAM_B200_H
+#define IAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    IAM_OK = 0,
+    IAM_ERR_ARG = 1,      /* invalid argument */
+    IAM_ERR_IO = 2,       /* missing / truncated / malformed weight file */
+    IAM_ERR_CUDA = 3,     /* CUDA runtime or launch error */
+    IAM_ERR_NCCL = 4,     /* NCCL error */
+    IAM_ERR_TIMEOUT = 5,  /* a bounded device-side wait gave up */
+    IAM_ERR_UNSUPPORTED = 6,
+    IAM_ERR_NOMEM = 7
+};
+
+#define IAM_PROBES_COUNT 4096 /* bucket_mul.hpp:101, bucketMul.cl:18 */
+
+/* Library identity and last error of the calling host thread. */
+const char* iam_version(void);
+const char* iam_last_error(void);
+/* Number of SMs and the sm_XY of `device`; fails with IAM_ERR_UNSUPPORTED off sm_100. */
+int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
+
+/* ------------------------------------------------------------------ bucketMul operator */
+/* Replaces the BucketMul singleton (bucket_mul.hpp:99-268).  The handle owns what the
+ * singleton owned (dispatch list, cutoff, counts), sized on demand. */
+typedef struct iam_bucketmul_s* iam_bucketmul_t;
+
+/* BucketMul::shared (bucket_mul.hpp:119-136). */
+int iam_bucketmul_create(iam_bucketmul_t* out, int device);
+int iam_bucketmul_destroy(iam_bucketmul_t h);
+
+/* findCutoffBinarySearch alone (bucketMul.cl:68-214 with the quantile of bucket_mul.hpp:164):
+ * writes the cutoff (fp32) to cutoff_dev[0] and the number of bisection steps to
+ * iters_dev[0] (iters_dev may be NULL).  Uses x[0:min(in_dim,4096)] and
+ * probes[expert_no*4096 + i]. */
+int iam_bucketmul_cutoff(iam_bucketmul_t h, const float* x_dev, const uint16_t* probes_dev,
+                         int expert_no, int in_dim, float effort, float* cutoff_dev,
+                         int* iters_dev, void* stream);
+
+/* BucketMul::calcDispatch (bucket_mul.hpp:147-191): cutoff + prepareDispatch
+ * (bucketMul.cl:351-386) into the handle's dispatch list.  Rows are kept in ascending
+ * row order (the reference's order is its atomic counter's; the selected SET is equal).
+ * stats_stride is 4 for the file layout, 1 for a packed channel-3 array. */
+int iam_bucketmul_calc_dispatch(iam_bucketmul_t h, const float* x_dev, const uint16_t* stats_dev,
+                                int stats_stride, const uint16_t* probes_dev, int expert_no,
+                                int in_dim, int bucket_cols, int expert_size, float effort,
+                                void* stream);
+
+/* Copies the current dispatch list out of the handle: rows_dev (capacity >= expert_size)
+ * receives the selected bucket-row indices in ascending order, count_dev[0] their number,
+ * cutoff_dev[0] the cutoff.  Any pointer may be NULL. */
+int iam_bucketmul_read_dispatch(iam_bucketmul_t h, int32_t* rows_dev, int* count_dev,
+                                float* cutoff_dev, void* stream);
+
+/* BucketMul::mul (bucket_mul.hpp:193-252): bucketMul (bucketMul.cl:392-447) + integrate
+ * (:453-497) over the handle's dispatch list.  out_dev receives 16*bucket_cols floats
+ * (overwritten, not accumulated).  bucket_rows = rows of the full buckets tensor. */
+int iam_bucketmul_mul(iam_bucketmul_t h, const uint16_t* buckets_dev, int bucket_rows,
+                      int bucket_cols, float* out_dev, void* stream);
+
+/* BucketMul::fullMul (bucket_mul.hpp:254-267) as ONE fused launch: cutoff, selection and
+ * accumulation in the same kernel.  count_dev (may be NULL) receives the number of
+ * selected bucket rows, cutoff_dev (may be NULL) the cutoff. */
+int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* stats_dev,
+                       int stats_stride, const uint16_t* probes_dev, const uint16_t* buckets_dev,
+                       int expert_no, int in_dim, int bucket_cols, int expert_size, float effort,
+                       float* out_dev, int* count_dev, float* cutoff_dev, void* stream);
+
+/* Packs channel 3 of a [rows][4] stats array into [rows] (stats_stride = 1 layout). */
+int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_dev, void* stream);
+
+/* Bucketize W[out_dim][in_dim] (fp16 bits, row-major, device) into the reference layout,
+ * on the GPU: same result as preprocess_layer_fixed_gpu.py:110-242 (ties in |w| ordered
+ * by lower original slot first).  buckets_dev [16*in_dim][out_dim/16], stats4_dev
+ * [16*in_dim][4] (may be NULL), stats1_dev [16*in_dim] (may be NULL), probes_dev [in_dim]. */
+int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buckets_dev,
+                  uint16_t* stats4_dev, uint16_t* stats1_dev, uint16_t* probes_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IAM_B200_H */

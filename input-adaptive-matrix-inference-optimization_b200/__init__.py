@@ -1,0 +1,148 @@
+"""iam_b200 -- Python host mirror of the reference's C++ host API over libiamb200.so.
+
+The product is the C ABI in include/iam_b200.h (and the C++ shim include/iam_b200.hpp);
+this module binds it with ctypes for tests and bench.py.  Device memory and streams come
+from torch (plumbing only).  There is no CPU path: if libiamb200.so is missing or the GPU
+is not an sm_100 part, every call raises.
+
+Load it by path (the directory name is not a Python identifier):
+
+    spec = importlib.util.spec_from_file_location(
+        "iam_b200", "<repo>/input-adaptive-matrix-inference-optimization_b200/__init__.py",
+        submodule_search_locations=["<repo>/input-adaptive-matrix-inference-optimization_b200"])
+"""
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libiamb200.so")
+
+IAM_OK, IAM_ERR_ARG, IAM_ERR_IO, IAM_ERR_CUDA, IAM_ERR_NCCL, IAM_ERR_TIMEOUT, IAM_ERR_UNSUPPORTED, \
+    IAM_ERR_NOMEM = range(8)
+PROBES_COUNT = 4096
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_longlong
+_f32 = ctypes.c_float
+
+# name -> argtypes (all return int unless listed in _RESTYPES)
+_SIGNATURES = {
+    "iam_version": [],
+    "iam_last_error": [],
+    "iam_device_info": [_i32, _vp, _vp, _vp],
+    "iam_bucketmul_create": [_vp, _i32],
+    "iam_bucketmul_destroy": [_vp],
+    "iam_bucketmul_cutoff": [_vp, _vp, _vp, _i32, _i32, _f32, _vp, _vp, _vp],
+    "iam_bucketmul_calc_dispatch": [_vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32, _vp],
+    "iam_bucketmul_read_dispatch": [_vp, _vp, _vp, _vp, _vp],
+    "iam_bucketmul_mul": [_vp, _vp, _i32, _i32, _vp, _vp],
+    "iam_bucketmul_full": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
+    "iam_stats_pack": [_vp, _i64, _vp, _vp],
+    "iam_bucketize": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
+}
+_RESTYPES = {"iam_version": ctypes.c_char_p, "iam_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+class IamError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"iam error {code}: {msg}")
+        self.code = code
+
+
+def load_library(path=LIB_PATH):
+    """Load libiamb200.so (fails loudly: there is no fallback path)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise IamError(IAM_ERR_UNSUPPORTED, f"{path} not built; run build.py")
+    lib = ctypes.CDLL(path)
+    for name, args in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
+    _lib = lib
+    return lib
+
+
+def exported_symbols():
+    return list(_SIGNATURES)
+
+
+def check(rc):
+    if rc != IAM_OK:
+        raise IamError(rc, load_library().iam_last_error().decode(errors="replace"))
+    return rc
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class BucketMul:
+    """Mirror of BucketMul (bucket_mul.hpp:99-268) on one device; arguments are torch
+    tensors on that device.  stats may be the file layout [R][4] (stats_stride=4) or the
+    packed channel 3 [R] (stats_stride=1)."""
+
+    def __init__(self, device=0):
+        self.lib = load_library()
+        self.h = ctypes.c_void_p()
+        check(self.lib.iam_bucketmul_create(ctypes.byref(self.h), device))
+
+    def close(self):
+        if self.h:
+            self.lib.iam_bucketmul_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def cutoff(self, x, probes, in_dim, effort, out, iters=None, expert_no=0, stream=None):
+        check(self.lib.iam_bucketmul_cutoff(self.h, _ptr(x), _ptr(probes), expert_no, in_dim, effort,
+                                            _ptr(out), _ptr(iters), _stream(stream)))
+
+    def calc_dispatch(self, x, stats, probes, expert_no, in_size, bucket_cols, expert_size, effort,
+                      stats_stride=4, stream=None):
+        check(self.lib.iam_bucketmul_calc_dispatch(self.h, _ptr(x), _ptr(stats), stats_stride, _ptr(probes),
+                                                   expert_no, in_size, bucket_cols, expert_size, effort,
+                                                   _stream(stream)))
+
+    def read_dispatch(self, rows=None, count=None, cutoff=None, stream=None):
+        check(self.lib.iam_bucketmul_read_dispatch(self.h, _ptr(rows), _ptr(count), _ptr(cutoff),
+                                                   _stream(stream)))
+
+    def mul(self, buckets, out, bucket_rows=None, bucket_cols=None, stream=None):
+        rows = buckets.shape[0] if bucket_rows is None else bucket_rows
+        cols = buckets.shape[1] if bucket_cols is None else bucket_cols
+        check(self.lib.iam_bucketmul_mul(self.h, _ptr(buckets), rows, cols, _ptr(out), _stream(stream)))
+
+    def full_mul(self, x, stats, probes, buckets, expert_no, in_size, bucket_cols, expert_size, effort, out,
+                 stats_stride=4, count=None, cutoff=None, stream=None):
+        check(self.lib.iam_bucketmul_full(self.h, _ptr(x), _ptr(stats), stats_stride, _ptr(probes),
+                                          _ptr(buckets), expert_no, in_size, bucket_cols, expert_size, effort,
+                                          _ptr(out), _ptr(count), _ptr(cutoff), _stream(stream)))
+
+
+def stats_pack(stats4, stats1, stream=None):
+    check(load_library().iam_stats_pack(_ptr(stats4), stats4.numel() // 4, _ptr(stats1), _stream(stream)))
+
+
+def bucketize(w, buckets, stats4=None, stats1=None, probes=None, stream=None):
+    """GPU bucketize of W[out][in] (torch uint16/int16/float16 tensor holding fp16 bits)."""
+    out_dim, in_dim = w.shape
+    check(load_library().iam_bucketize(_ptr(w), out_dim, in_dim, _ptr(buckets), _ptr(stats4), _ptr(stats1),
+                                       _ptr(probes), _stream(stream)))

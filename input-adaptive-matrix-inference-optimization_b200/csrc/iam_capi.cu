@@ -1,0 +1,252 @@
+// iam_capi.cu -- C ABI entry points of libiamb200.so for the bucketMul operator.
+// Declarations and the reference interface each one replaces: include/iam_b200.h.
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "iam_bucketmul_launch.h"
+#include "iam_common.cuh"
+
+namespace iam {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? IAM_ERR_NOMEM : IAM_ERR_CUDA;
+}
+
+}  // namespace iam
+
+using namespace iam;
+
+struct iam_bucketmul_s {
+    int device = 0;
+    int32_t* list = nullptr;  // dispatch list scratch
+    size_t list_cap = 0;      // capacity in rows
+    int* seg_counts = nullptr;
+    float* cutoff = nullptr;  // device scalar
+    int* ints = nullptr;      // device scalars: [0] count, [1] iters
+    // dispatch recorded by iam_bucketmul_calc_dispatch (consumed by iam_bucketmul_mul)
+    bool have_dispatch = false;
+    BMProblem disp{};
+    int disp_G = 8;
+    int disp_bucket_cols = 0;
+};
+
+namespace {
+
+int ensure_list(iam_bucketmul_s* h, size_t rows) {
+    if (rows <= h->list_cap) return IAM_OK;
+    if (h->list) {
+        IAM_CUDA_TRY(cudaFree(h->list));
+        h->list = nullptr;
+        h->list_cap = 0;
+    }
+    IAM_CUDA_TRY(cudaMalloc(&h->list, rows * sizeof(int32_t)));
+    h->list_cap = rows;
+    return IAM_OK;
+}
+
+bool effort_ok(float e) { return std::isfinite(e) && e > 0.0f && e <= 1.0f; }
+
+// Fills the selection part of a problem (shared by calc_dispatch and full).
+int fill_problem(iam_bucketmul_s* h, BMProblem& p, int G, const float* x, const uint16_t* stats,
+                 int stats_stride, const uint16_t* probes, int expert_no, int in_dim, int bucket_cols,
+                 int expert_size, float effort) {
+    if (!x || !stats || !probes) return fail(IAM_ERR_ARG, "bucketmul: null input/stats/probes pointer");
+    if (in_dim <= 0 || bucket_cols <= 0 || expert_size <= 0 || expert_no < 0)
+        return fail(IAM_ERR_ARG, "bucketmul: in_dim, bucket_cols, expert_size must be > 0, expert_no >= 0");
+    if (stats_stride != 1 && stats_stride != 4)
+        return fail(IAM_ERR_ARG, "bucketmul: stats_stride must be 1 (packed) or 4 (file layout)");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "bucketmul: effort must be in (0, 1]");
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.stats = stats;
+    p.stats_stride = stats_stride;
+    p.probes = probes + (size_t)expert_no * IAM_PROBES_COUNT;  // bucketMul.cl:103
+    p.row0 = (long long)expert_size * expert_no;               // bucketMul.cl:363
+    p.n_rows_valid = expert_size < 16 * in_dim ? expert_size : 16 * in_dim;
+    p.n_inputs = (p.n_rows_valid + 15) / 16;
+    p.cols = bucket_cols;
+    p.P = in_dim < IAM_PROBES_COUNT ? in_dim : IAM_PROBES_COUNT;
+    p.target = bm_target(effort, p.P);
+    p.seg_inputs = (p.n_inputs + G - 1) / G;
+    int rc = ensure_list(h, (size_t)p.seg_inputs * 16 * G);
+    if (rc) return rc;
+    p.list = h->list;
+    p.seg_counts = h->seg_counts;
+    return IAM_OK;
+}
+
+int pick_vec(const BMBatch& b) {
+    for (int i = 0; i < b.nprob; ++i) {
+        const BMProblem& p = b.p[i];
+        if (p.cols % 8 != 0 || (reinterpret_cast<uintptr_t>(p.buckets) & 15u) != 0) return 1;
+    }
+    return 8;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* iam_version(void) { return "iam-b200 0.1 (sm_100a)"; }
+
+const char* iam_last_error(void) { return g_last_error.c_str(); }
+
+int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor) {
+    cudaDeviceProp prop;
+    IAM_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (sm_count) *sm_count = prop.multiProcessorCount;
+    if (cc_major) *cc_major = prop.major;
+    if (cc_minor) *cc_minor = prop.minor;
+    if (prop.major != 10) return fail(IAM_ERR_UNSUPPORTED, "libiamb200 is built for sm_100a only");
+    return IAM_OK;
+}
+
+int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
+    if (!out) return fail(IAM_ERR_ARG, "iam_bucketmul_create: null out");
+    *out = nullptr;
+    int rc = iam_device_info(device, nullptr, nullptr, nullptr);
+    if (rc) return rc;
+    IAM_CUDA_TRY(cudaSetDevice(device));
+    iam_bucketmul_s* h = new iam_bucketmul_s();
+    h->device = device;
+    cudaError_t e = cudaMalloc(&h->seg_counts, sizeof(int) * kMaxCluster);
+    if (e == cudaSuccess) e = cudaMalloc(&h->cutoff, sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * 2);
+    if (e != cudaSuccess) {
+        iam_bucketmul_destroy(h);
+        return cuda_fail(e, "iam_bucketmul_create: cudaMalloc");
+    }
+    *out = h;
+    return IAM_OK;
+}
+
+int iam_bucketmul_destroy(iam_bucketmul_t h) {
+    if (!h) return IAM_OK;
+    cudaFree(h->list);
+    cudaFree(h->seg_counts);
+    cudaFree(h->cutoff);
+    cudaFree(h->ints);
+    delete h;
+    return IAM_OK;
+}
+
+int iam_bucketmul_cutoff(iam_bucketmul_t h, const float* x_dev, const uint16_t* probes_dev, int expert_no,
+                         int in_dim, float effort, float* cutoff_dev, int* iters_dev, void* stream) {
+    if (!h || !x_dev || !probes_dev || !cutoff_dev) return fail(IAM_ERR_ARG, "iam_bucketmul_cutoff: null pointer");
+    if (in_dim <= 0 || expert_no < 0) return fail(IAM_ERR_ARG, "iam_bucketmul_cutoff: bad in_dim/expert_no");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_bucketmul_cutoff: effort must be in (0, 1]");
+    const int P = in_dim < IAM_PROBES_COUNT ? in_dim : IAM_PROBES_COUNT;
+    return bm_launch_cutoff(x_dev, probes_dev + (size_t)expert_no * IAM_PROBES_COUNT, P, bm_target(effort, P),
+                            cutoff_dev, iters_dev, (cudaStream_t)stream);
+}
+
+int iam_bucketmul_calc_dispatch(iam_bucketmul_t h, const float* x_dev, const uint16_t* stats_dev, int stats_stride,
+                                const uint16_t* probes_dev, int expert_no, int in_dim, int bucket_cols,
+                                int expert_size, float effort, void* stream) {
+    if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_calc_dispatch: null handle");
+    h->have_dispatch = false;
+    const int G = bm_default_cluster();
+    BMBatch b;
+    memset(&b, 0, sizeof(b));
+    int rc = fill_problem(h, b.p[0], G, x_dev, stats_dev, stats_stride, probes_dev, expert_no, in_dim,
+                          bucket_cols, expert_size, effort);
+    if (rc) return rc;
+    b.p[0].cutoff_out = h->cutoff;
+    b.p[0].count_out = h->ints;
+    b.p[0].iters_out = h->ints + 1;
+    b.p[0].n_tiles = 1;
+    b.nprob = 1;
+    b.mode = kModeSelectOnly;
+    rc = bm_launch(b, 1, G, (cudaStream_t)stream);
+    if (rc) return rc;
+    h->disp = b.p[0];
+    h->disp_G = G;
+    h->disp_bucket_cols = bucket_cols;
+    h->have_dispatch = true;
+    return IAM_OK;
+}
+
+int iam_bucketmul_read_dispatch(iam_bucketmul_t h, int32_t* rows_dev, int* count_dev, float* cutoff_dev,
+                                void* stream) {
+    if (!h || !h->have_dispatch) return fail(IAM_ERR_ARG, "iam_bucketmul_read_dispatch: no dispatch recorded");
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc = bm_launch_gather(h->list, h->seg_counts, h->disp_G, h->disp.seg_inputs * 16, rows_dev, count_dev, s);
+    if (rc) return rc;
+    if (cutoff_dev) IAM_CUDA_TRY(cudaMemcpyAsync(cutoff_dev, h->cutoff, sizeof(float), cudaMemcpyDeviceToDevice, s));
+    return IAM_OK;
+}
+
+int iam_bucketmul_mul(iam_bucketmul_t h, const uint16_t* buckets_dev, int bucket_rows, int bucket_cols,
+                      float* out_dev, void* stream) {
+    if (!h || !h->have_dispatch) return fail(IAM_ERR_ARG, "iam_bucketmul_mul: call iam_bucketmul_calc_dispatch first");
+    if (!buckets_dev || !out_dev) return fail(IAM_ERR_ARG, "iam_bucketmul_mul: null buckets/out");
+    if (bucket_cols != h->disp_bucket_cols)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_mul: bucket_cols differs from the dispatch's bucketCols");
+    if ((long long)bucket_rows < h->disp.row0 + h->disp.n_rows_valid)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_mul: buckets tensor has fewer rows than the dispatch covers");
+    BMBatch b;
+    memset(&b, 0, sizeof(b));
+    b.p[0] = h->disp;
+    b.p[0].buckets = buckets_dev;
+    b.p[0].out = out_dev;
+    b.p[0].cutoff_out = nullptr;
+    b.p[0].count_out = nullptr;
+    b.p[0].iters_out = nullptr;
+    b.nprob = 1;
+    b.mode = kModeMulOnly;
+    const int G = h->disp_G;
+    const int vec = pick_vec(b);
+    bm_plan_tiles(b, vec, G, bm_max_active_clusters(vec, G));
+    return bm_launch(b, vec, G, (cudaStream_t)stream);
+}
+
+int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* stats_dev, int stats_stride,
+                       const uint16_t* probes_dev, const uint16_t* buckets_dev, int expert_no, int in_dim,
+                       int bucket_cols, int expert_size, float effort, float* out_dev, int* count_dev,
+                       float* cutoff_dev, void* stream) {
+    if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_full: null handle");
+    if (!buckets_dev || !out_dev) return fail(IAM_ERR_ARG, "iam_bucketmul_full: null buckets/out");
+    const int G = bm_default_cluster();
+    BMBatch b;
+    memset(&b, 0, sizeof(b));
+    int rc = fill_problem(h, b.p[0], G, x_dev, stats_dev, stats_stride, probes_dev, expert_no, in_dim,
+                          bucket_cols, expert_size, effort);
+    if (rc) return rc;
+    b.p[0].buckets = buckets_dev;
+    b.p[0].out = out_dev;
+    b.p[0].count_out = count_dev;
+    b.p[0].cutoff_out = cutoff_dev;
+    b.nprob = 1;
+    b.mode = kModeFused;
+    const int vec = pick_vec(b);
+    bm_plan_tiles(b, vec, G, bm_max_active_clusters(vec, G));
+    return bm_launch(b, vec, G, (cudaStream_t)stream);
+}
+
+int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_dev, void* stream) {
+    if (!stats4_dev || !stats1_dev || rows < 0) return fail(IAM_ERR_ARG, "iam_stats_pack: bad arguments");
+    if (rows == 0) return IAM_OK;
+    return bm_launch_stats_pack(stats4_dev, rows, stats1_dev, (cudaStream_t)stream);
+}
+
+int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buckets_dev, uint16_t* stats4_dev,
+                  uint16_t* stats1_dev, uint16_t* probes_dev, void* stream) {
+    if (!w_dev || !buckets_dev) return fail(IAM_ERR_ARG, "iam_bucketize: null W/buckets");
+    if (out_dim <= 0 || in_dim <= 0 || out_dim % 16 != 0)
+        return fail(IAM_ERR_ARG, "iam_bucketize: out_dim must be a positive multiple of 16");
+    return bucketize_launch(w_dev, out_dim, in_dim, buckets_dev, stats4_dev, stats1_dev, probes_dev,
+                            (cudaStream_t)stream);
+}
+
+}  // extern "C"
