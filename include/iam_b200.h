@@ -51,6 +51,12 @@ const char* iam_last_error(void);
 /* Number of SMs and the sm_XY of `device`; fails with IAM_ERR_UNSUPPORTED off sm_100. */
 int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
 
+/* Diagnostics: resident clusters of `cluster_size` CTAs for the fused bucketMul kernel with
+ * vec-wide loads (8 or 1) on the current device, and the tiling chosen for one bucketMul of
+ * bucket_cols columns and in_dim inputs (log2 of lanes per row, column tiles). */
+int iam_bucketmul_plan_info(int vec, int cluster_size, int bucket_cols, int in_dim,
+                            int* max_active_clusters, int* log2_lanes, int* n_tiles);
+
 /* ------------------------------------------------------------------ bucketMul operator */
 /* Replaces the BucketMul singleton (bucket_mul.hpp:99-268).  The handle owns what the
  * singleton owned (dispatch list, cutoff, counts), sized on demand. */
@@ -96,6 +102,11 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
                        int stats_stride, const uint16_t* probes_dev, const uint16_t* buckets_dev,
                        int expert_no, int in_dim, int bucket_cols, int expert_size, float effort,
                        float* out_dev, int* count_dev, float* cutoff_dev, void* stream);
+
+/* Diagnostics: every later launch of `h` writes 7 globaltimer stamps (ns) of its first CTA
+ * to times_dev[0..6]: start, cutoff done, masks done, list done, accumulation done,
+ * partial tile done, end.  NULL turns it off. */
+int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev);
 
 /* Packs channel 3 of a [rows][4] stats array into [rows] (stats_stride = 1 layout). */
 int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_dev, void* stream);

@@ -31,6 +31,7 @@ _SIGNATURES = {
     "iam_version": [],
     "iam_last_error": [],
     "iam_device_info": [_i32, _vp, _vp, _vp],
+    "iam_bucketmul_plan_info": [_i32, _i32, _i32, _i32, _vp, _vp, _vp],
     "iam_bucketmul_create": [_vp, _i32],
     "iam_bucketmul_destroy": [_vp],
     "iam_bucketmul_cutoff": [_vp, _vp, _vp, _i32, _i32, _f32, _vp, _vp, _vp],
@@ -38,6 +39,7 @@ _SIGNATURES = {
     "iam_bucketmul_read_dispatch": [_vp, _vp, _vp, _vp, _vp],
     "iam_bucketmul_mul": [_vp, _vp, _i32, _i32, _vp, _vp],
     "iam_bucketmul_full": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
+    "iam_bucketmul_phase_times": [_vp, _vp],
     "iam_stats_pack": [_vp, _i64, _vp, _vp],
     "iam_bucketize": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
 }
@@ -111,6 +113,10 @@ class BucketMul:
         except Exception:
             pass
 
+    def phase_times(self, times):
+        """Diagnostics: later launches write 7 int64 globaltimer stamps into `times`."""
+        check(self.lib.iam_bucketmul_phase_times(self.h, _ptr(times)))
+
     def cutoff(self, x, probes, in_dim, effort, out, iters=None, expert_no=0, stream=None):
         check(self.lib.iam_bucketmul_cutoff(self.h, _ptr(x), _ptr(probes), expert_no, in_dim, effort,
                                             _ptr(out), _ptr(iters), _stream(stream)))
@@ -135,6 +141,14 @@ class BucketMul:
         check(self.lib.iam_bucketmul_full(self.h, _ptr(x), _ptr(stats), stats_stride, _ptr(probes),
                                           _ptr(buckets), expert_no, in_size, bucket_cols, expert_size, effort,
                                           _ptr(out), _ptr(count), _ptr(cutoff), _stream(stream)))
+
+
+def plan_info(vec, cluster, bucket_cols, in_dim):
+    """-> (max_active_clusters, log2_lanes_per_row, n_tiles) of the fused bucketMul tiling."""
+    a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(load_library().iam_bucketmul_plan_info(vec, cluster, bucket_cols, in_dim, ctypes.byref(a),
+                                                 ctypes.byref(b), ctypes.byref(c)))
+    return a.value, b.value, c.value
 
 
 def stats_pack(stats4, stats1, stream=None):

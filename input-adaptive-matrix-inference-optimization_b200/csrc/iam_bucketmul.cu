@@ -1,39 +1,100 @@
-// iam_bucketmul.cu -- fused bucketMul kernels and the bucketMul C ABI.
+// iam_bucketmul.cu -- fused bucketMul kernel (sm_100a) and its launch planning.
 //
 // Reference operator: BucketMul (bucket_mul.hpp:99-268) over bucketMul.cl:68-497.
+//
+// One launch runs up to kMaxProblems bucketMuls.  Grid = clusters of G CTAs; cluster ci
+// owns one column tile of one problem.  Per CTA (rank g of its cluster):
+//   1. cutoff: block_find_cutoff over x[0:P] (every CTA, identical result);
+//   2. selection masks for input segment g (block_masks), cluster barrier, prefix over the
+//      G segment counts read through DSMEM, then the selected rows are written COMPACT and
+//      ascending into the dispatch list (every cluster writes the same values), cluster
+//      barrier -- position p of the selection is list[p] for every CTA;
+//   3. the CTA takes positions [S*g/G, S*(g+1)/G): it stages {row*C, x(row)} for 512 rows
+//      at a time in shared memory (next chunk prefetched during the current one), and each
+//      lane streams VEC-wide slices of its rows with register double-buffered loads,
+//      adding x*w into lane-private per-slot accumulators in shared memory;
+//   4. lane accumulators -> one partial tile per CTA -> fixed-order DSMEM sum across the
+//      cluster -> out (+ residual).  No global atomics; results are bitwise deterministic.
 #include <algorithm>
-#include <cstdio>
 #include <cstdlib>
+#include <map>
 #include <mutex>
-#include <vector>
+#include <tuple>
 
 #include "iam_bucketmul.cuh"
 #include "iam_bucketmul_launch.h"
 
 namespace iam {
 
-// ------------------------------------------------------------------ fused kernel
+constexpr int kCH = 2048;  // rows per staged chunk
+constexpr int kU = 8;      // rows per lane per load group (two groups in flight)
+
+// Threads per CTA for a vector width: the lane accumulators (16 slots x VEC floats per
+// lane) fill 128 KB of shared memory either way; narrower loads buy more warps.
+template <int VEC>
+struct Threads {
+    static constexpr int value = VEC == 4 ? 512 : 256;
+};
 
 template <int NT>
 struct FusedHeader {
     CutoffShared<NT> cut;
     ScanShared<NT> scan;
+    float red[256];
     int my_count;
     int pre[kMaxCluster + 1];
 };
 
-template <int VEC, int NT>
-constexpr size_t fused_smem_bytes() {
-    return ((sizeof(FusedHeader<NT>) + 15) / 16) * 16     // header
-           + sizeof(float) * 16 * VEC * 32                // part: one column tile, 16 slots
-           + sizeof(float) * (NT / 32) * 32 * VEC * 16;   // per-warp lane-private accumulators
+constexpr size_t align16(size_t n) { return (n + 15) / 16 * 16; }
+
+template <int VEC>
+constexpr size_t fixed_smem_bytes() {
+    constexpr int NT = Threads<VEC>::value;
+    return align16(sizeof(FusedHeader<NT>)) + 2 * kCH * sizeof(uint2)  // header, staging
+           + sizeof(float) * 16 * VEC * 32                             // partial tile
+           + sizeof(float) * NT * VEC * 16;                            // lane accumulators
 }
 
-// One launch = up to kMaxProblems independent bucketMuls (e.g. q/k/v sharing x).
-// Cluster ci belongs to problem p and covers column tile (ci - p.cluster_begin).
-template <int VEC, int NT, int U>
-__global__ void __launch_bounds__(NT, 1) bm_fused_kernel(const __grid_constant__ BMBatch batch) {
-    constexpr int NW = NT / 32;
+size_t bm_smem_bytes(int vec, int seg_inputs) {
+    const size_t masks = align16((size_t)seg_inputs * sizeof(uint16_t));
+    if (vec == 8) return fixed_smem_bytes<8>() + masks;
+    if (vec == 4) return fixed_smem_bytes<4>() + masks;
+    return fixed_smem_bytes<1>() + masks;
+}
+
+IAM_DEV void stamp(long long* dbg, int k) {
+    if (dbg) {
+        long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        dbg[k] = t;
+    }
+}
+
+template <int XM, int NT>
+struct Provider;
+template <int NT>
+struct Provider<kXPlain, NT> {
+    using T = XPlain;
+    static IAM_DEV T make(const BMProblem& p, float*) { return XPlain{p.x}; }
+};
+template <int NT>
+struct Provider<kXRms, NT> {
+    using T = XRms;
+    static IAM_DEV T make(const BMProblem& p, float* red) {
+        return XRms{p.x, p.gain, block_rms_scale<NT>(p.x, p.norm_n, p.norm_eps, red)};
+    }
+};
+template <int NT>
+struct Provider<kXSilu, NT> {
+    using T = XSilu;
+    static IAM_DEV T make(const BMProblem& p, float*) { return XSilu{p.x, p.x2}; }
+};
+
+template <int VEC, int XM>
+__global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const __grid_constant__ BMBatch batch) {
+    constexpr int NT = Threads<VEC>::value, NW = NT / 32, U = kU;
+    using VL = VecLoad<VEC>;
+    using VT = typename VL::T;
     cg::cluster_group cluster = cg::this_cluster();
     const int G = (int)cluster.num_blocks();
     const int g = (int)cluster.block_rank();
@@ -42,112 +103,153 @@ __global__ void __launch_bounds__(NT, 1) bm_fused_kernel(const __grid_constant__
     while (pi + 1 < batch.nprob && ci >= batch.p[pi + 1].cluster_begin) ++pi;
     const BMProblem& pr = batch.p[pi];
     const int tile = ci - pr.cluster_begin;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    long long* dbg = (ci == 0 && g == 0 && tid == 0) ? pr.dbg : nullptr;
+    stamp(dbg, 0);
 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FusedHeader<NT>& hdr = *reinterpret_cast<FusedHeader<NT>*>(smem_raw);
-    float* part = reinterpret_cast<float*>(smem_raw + ((sizeof(FusedHeader<NT>) + 15) / 16) * 16);
+    uint2* stage = reinterpret_cast<uint2*>(smem_raw + align16(sizeof(FusedHeader<NT>)));
+    float* part = reinterpret_cast<float*>(stage + 2 * kCH);
     float* acc = part + 16 * VEC * 32;
+    uint16_t* masks = reinterpret_cast<uint16_t*>(acc + NT * VEC * 16);
 
-    const int seg_cap = pr.seg_inputs * 16;
-    const int i0 = min(g * pr.seg_inputs, pr.n_inputs);
-    const int i1 = min(i0 + pr.seg_inputs, pr.n_inputs);
+    const auto xp = Provider<XM, NT>::make(pr, hdr.red);
+    const long long row0 = pr.row0;
 
-    // ---- phase 1+2: cutoff and selection of this CTA's input segment
+    // ---- phases 1-2: cutoff, selection masks, compact dispatch list
+    int S;
     if (batch.mode != kModeMulOnly) {
         int iters = 0;
-        const float cutoff = block_find_cutoff<NT>(pr.x, pr.probes, pr.P, pr.target, hdr.cut, &iters);
-        const int n = block_select<NT>(pr.x, pr.stats, pr.stats_stride, pr.row0, pr.n_rows_valid,
-                                       i0, i1, cutoff, pr.list + (size_t)g * seg_cap, hdr.scan);
-        if (threadIdx.x == 0) {
-            hdr.my_count = n;
-            if (batch.mode == kModeSelectOnly) pr.seg_counts[g] = n;
-            if (tile == 0 && g == 0) {
-                if (pr.cutoff_out) *pr.cutoff_out = cutoff;
-                if (pr.iters_out) *pr.iters_out = iters;
+        const float cutoff = block_find_cutoff<NT>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters);
+        stamp(dbg, 1);
+        const int i0 = min(pr.in_begin + g * pr.seg_inputs, pr.n_inputs);
+        const int i1 = min(i0 + pr.seg_inputs, pr.n_inputs);
+        const int n = block_masks<NT>(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i0, i1, cutoff,
+                                      masks, hdr.scan);
+        if (tid == 0) hdr.my_count = n;
+        stamp(dbg, 2);
+        cluster.sync();
+        if (warp == 0) {  // all G peer counts read in parallel, then a warp scan
+            const int c = lane < G ? *cluster.map_shared_rank(&hdr.my_count, lane) : 0;
+            int inc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += t;
             }
+            if (lane <= G) hdr.pre[lane] = inc - c;
         }
-    } else if (threadIdx.x == 0) {
-        hdr.my_count = __ldcg(pr.seg_counts + g);
-    }
-    cluster.sync();  // segment lists (global) and counts (smem) visible cluster-wide
-
-    if (threadIdx.x == 0) {
-        int s = 0;
-        for (int r = 0; r < G; ++r) {
-            hdr.pre[r] = s;
-            s += *cluster.map_shared_rank(&hdr.my_count, r);
+        __syncthreads();
+        block_write_rows<NT>(masks, row0, i0, i1, pr.list + hdr.pre[g], hdr.scan);
+        S = hdr.pre[G];
+        if (tile == 0 && g == 0 && tid == 0) {
+            if (pr.cutoff_out) *pr.cutoff_out = cutoff;
+            if (pr.iters_out) *pr.iters_out = iters;
+            if (pr.count_out) *pr.count_out = S;
+            if (batch.mode == kModeSelectOnly && pr.sel_total) *pr.sel_total = S;
         }
-        hdr.pre[G] = s;
-        if (batch.mode != kModeMulOnly && tile == 0 && g == 0 && pr.count_out) *pr.count_out = s;
-    }
-    __syncthreads();
-    if (batch.mode == kModeSelectOnly) {
-        cluster.sync();  // peers may still read my_count
-        return;
+        cluster.sync();  // compact list complete; peers done reading my_count
+        stamp(dbg, 3);
+        if (batch.mode == kModeSelectOnly) return;
+    } else {
+        S = __ldcg(pr.sel_total);
     }
 
-    // ---- phase 3: accumulate this CTA's balanced share of the cluster's selected rows
-    const int S = hdr.pre[G];
+    // ---- phase 3: accumulate positions [a, b) of the selection
     const int a = (int)(((long long)S * g) / G);
     const int b = (int)(((long long)S * (g + 1)) / G);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int log2L = pr.log2L;
     const int L = 1 << log2L, P = 32 >> log2L;
     const int rg = lane >> log2L, q = lane & (L - 1);
     const int TW = VEC * L;
     const int c0 = tile * TW + q * VEC;
     const bool col_ok = c0 < pr.cols;
+    const uint16_t* __restrict__ wbase = pr.buckets + (col_ok ? c0 : 0);
+    const int cols = pr.cols;
+    const int32_t bucket_row0 = (int32_t)pr.bucket_row0;
+    const int32_t* __restrict__ list = pr.list;
 
     float* my_acc = acc + (size_t)warp * 16 * VEC * 32 + lane;
 #pragma unroll 4
     for (int j = 0; j < 16 * VEC; ++j) my_acc[j * 32] = 0.0f;
 
-    const int32_t* list = pr.list;
-    auto row_at = [&](int p) -> int32_t {
-        int gs = 0;
-        while (gs + 1 < G && p >= hdr.pre[gs + 1]) ++gs;
-        return __ldcg(list + (size_t)gs * seg_cap + (p - hdr.pre[gs]));
-    };
-
-    const int stride_u = NW * P;
-    const int step = stride_u * U;
-    const uint16_t* __restrict__ wb = pr.buckets + c0;
-    const float* __restrict__ xv_base = pr.x;
-    const long long row0 = pr.row0;
-    const size_t cols = (size_t)pr.cols;
-
-    int rows[U];
-    const int first = a + warp * P;
+    constexpr int SPT = kCH / NT;  // staged rows per thread per chunk
+    auto stage_fetch = [&](int p0, int n, int32_t* rr, float* xx) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int p = first + u * stride_u + rg;
-        rows[u] = (p < b) ? row_at(p) : -1;
-    }
-    for (int s0 = first; s0 < b; s0 += step) {
-        typename VecLoad<VEC>::T w[U];
-        float xv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (rows[u] >= 0 && col_ok) {
-                w[u] = VecLoad<VEC>::load(wb + (size_t)rows[u] * cols);
-                xv[u] = __ldg(xv_base + ((rows[u] - row0) >> 4));
+        for (int k = 0; k < SPT; ++k) {
+            const int j = tid + k * NT;
+            if (j < n) {
+                const int32_t row = __ldcg(list + p0 + j);
+                rr[k] = row;
+                xx[k] = xp((int)((row - row0) >> 4));
             }
         }
-        int next[U];
+    };
+    auto stage_store = [&](uint2* st, int n, const int32_t* rr, const float* xx) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int p = s0 + step + u * stride_u + rg;
-            next[u] = (p < b) ? row_at(p) : -1;
+        for (int k = 0; k < SPT; ++k) {
+            const int j = tid + k * NT;
+            if (j < n)
+                st[j] = make_uint2((uint32_t)(rr[k] - bucket_row0) * (uint32_t)cols, __float_as_uint(xx[k]));
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (rows[u] >= 0 && col_ok) accumulate<VEC>(my_acc, w[u], xv[u]);
-#pragma unroll
-        for (int u = 0; u < U; ++u) rows[u] = next[u];
+    };
+
+    int32_t rr[SPT];
+    float xx[SPT];
+    {
+        const int n0 = min(kCH, b - a);
+        stage_fetch(a, n0, rr, xx);
+        stage_store(stage, n0, rr, xx);
     }
     __syncthreads();
 
-    // ---- reduce the lane-private accumulators into this CTA's tile partial
+    int buf = 0;
+    for (int cstart = a; cstart < b; cstart += kCH, buf ^= 1) {
+        const int n = min(kCH, b - cstart);
+        const int nn = min(kCH, b - (cstart + kCH));
+        stage_fetch(cstart + kCH, nn, rr, xx);  // next chunk, overlapped with this one
+
+        const uint2* st = stage + buf * kCH;
+        const int first = P * warp;
+        const int mw = n > first ? (n - first + P * NW - 1) / (P * NW) : 0;
+        const int ng = (mw + U - 1) / U;
+        VT wA[U], wB[U];
+        float xA[U], xB[U];
+        auto load_group = [&](int grp, VT* w, float* xs) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int j = rg + P * (warp + NW * (grp * U + u));
+                if (j < n && col_ok) {
+                    const uint2 e = st[j];
+                    w[u] = VL::load(wbase + e.x);
+                    xs[u] = __uint_as_float(e.y);
+                } else {
+                    w[u] = VL::zero();
+                    xs[u] = 0.0f;
+                }
+            }
+        };
+        auto acc_group = [&](const VT* w, const float* xs) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) accumulate<VEC>(my_acc, w[u], xs[u]);
+        };
+        if (ng > 0) load_group(0, wA, xA);
+        int gi = 0;
+        for (; gi + 1 < ng; gi += 2) {
+            load_group(gi + 1, wB, xB);
+            acc_group(wA, xA);
+            if (gi + 2 < ng) load_group(gi + 2, wA, xA);
+            acc_group(wB, xB);
+        }
+        if (gi < ng) acc_group(wA, xA);
+
+        stage_store(stage + (buf ^ 1) * kCH, nn, rr, xx);
+        __syncthreads();
+    }
+    stamp(dbg, 4);
+
+    // ---- phase 4: lane accumulators -> CTA partial tile -> cluster sum
     for (int sk = warp; sk < 16 * VEC; sk += NW) {
         float v = 0.0f;
 #pragma unroll
@@ -159,57 +261,43 @@ __global__ void __launch_bounds__(NT, 1) bm_fused_kernel(const __grid_constant__
         }
     }
     cluster.sync();
-
-    // ---- cluster reduction of the G partial tiles, fixed order (deterministic)
+    stamp(dbg, 5);
     const int nout = 16 * TW;
     const int per = (nout + G - 1) / G;
-    const int o0 = g * per, o1 = min(nout, o0 + per);
-    for (int o = o0 + (int)threadIdx.x; o < o1; o += NT) {
+    const int o0 = min(nout, g * per), o1 = min(nout, o0 + per);
+    const int n_own = o1 - o0;
+    float* gathered = acc;  // [n_own][G]; the accumulators are dead, peers only read `part`
+    for (int k = tid; k < n_own * G; k += NT) {  // all remote loads in flight at once
+        const int oo = k / G, r = k - oo * G;
+        gathered[k] = cluster.map_shared_rank(part, r)[o0 + oo];
+    }
+    __syncthreads();
+    for (int oo = tid; oo < n_own; oo += NT) {
         float s = 0.0f;
-        for (int r = 0; r < G; ++r) s += cluster.map_shared_rank(part, r)[o];
+        for (int r = 0; r < G; ++r) s += gathered[oo * G + r];  // fixed order: deterministic
+        const int o = o0 + oo;
         const int col = tile * TW + o / 16;
-        if (col < pr.cols) {
+        if (col < cols) {
             const size_t j = (size_t)tile * TW * 16 + o;  // = col*16 + slot
-            if (pr.residual) s = pr.residual[j] + s;      // add32 fused (bucketMul.cl:517-520)
+            if (pr.residual) s = pr.residual[j] + s;      // add32 (bucketMul.cl:517-520)
             pr.out[j] = s;
         }
     }
     cluster.sync();  // keep `part` alive until every peer has read it
+    stamp(dbg, 6);
 }
 
-// ------------------------------------------------------------------ standalone cutoff
+// ------------------------------------------------------------------ standalone kernels
 
 template <int NT>
 __global__ void __launch_bounds__(NT) bm_cutoff_kernel(const float* x, const uint16_t* probes, int P,
                                                        int target, float* out, int* iters) {
     __shared__ CutoffShared<NT> sm;
     int it = 0;
-    const float c = block_find_cutoff<NT>(x, probes, P, target, sm, &it);
+    const float c = block_find_cutoff<NT>(XPlain{x}, probes, P, target, sm, &it);
     if (threadIdx.x == 0) {
         out[0] = c;
         if (iters) iters[0] = it;
-    }
-}
-
-// Concatenates the G segments of a dispatch list (ascending rows).
-__global__ void bm_gather_dispatch_kernel(const int32_t* list, const int* seg_counts, int G,
-                                          int seg_cap, int32_t* rows_out, int* count_out) {
-    __shared__ int pre[kMaxCluster + 1];
-    if (threadIdx.x == 0) {
-        int s = 0;
-        for (int r = 0; r < G; ++r) {
-            pre[r] = s;
-            s += seg_counts[r];
-        }
-        pre[G] = s;
-        if (count_out) *count_out = s;
-    }
-    __syncthreads();
-    if (!rows_out) return;
-    for (int r = 0; r < G; ++r) {
-        const int n = pre[r + 1] - pre[r];
-        for (int k = threadIdx.x; k < n; k += blockDim.x)
-            rows_out[pre[r] + k] = list[(size_t)r * seg_cap + k];
     }
 }
 
@@ -223,24 +311,31 @@ __global__ void stats_pack_kernel(const uint16_t* s4, long long rows, uint16_t* 
 
 namespace {
 
-constexpr int kNT = 256;
-constexpr int kU = 8;
+int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return (v && *v) ? atoi(v) : dflt;
+}
 
-template <int VEC>
-int launch_fused(const BMBatch& b, int G, int n_clusters, cudaStream_t s) {
-    auto kern = bm_fused_kernel<VEC, kNT, kU>;
-    const size_t smem = fused_smem_bytes<VEC, kNT>();
+template <int VEC, int XM>
+cudaError_t set_attrs() {
     static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        auto kern = bm_fused_kernel<VEC, XM>;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (err == cudaSuccess) err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     });
-    if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(bm_fused)");
+    return err;
+}
+
+template <int VEC, int XM>
+int launch_one(const BMBatch& b, int G, int n_clusters, size_t smem, cudaStream_t s) {
+    auto kern = bm_fused_kernel<VEC, XM>;
+    cudaError_t e = set_attrs<VEC, XM>();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bm_fused)");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(n_clusters * G));
-    cfg.blockDim = dim3(kNT);
+    cfg.blockDim = dim3(Threads<VEC>::value);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -254,19 +349,19 @@ int launch_fused(const BMBatch& b, int G, int n_clusters, cudaStream_t s) {
     return IAM_OK;
 }
 
-int env_int(const char* name, int dflt) {
-    const char* v = getenv(name);
-    return (v && *v) ? atoi(v) : dflt;
+template <int VEC>
+int launch_vec(const BMBatch& b, int G, int n, size_t smem, cudaStream_t s) {
+    switch (b.xmode) {
+        case kXRms: return launch_one<VEC, kXRms>(b, G, n, smem, s);
+        case kXSilu: return launch_one<VEC, kXSilu>(b, G, n, smem, s);
+        default: return launch_one<VEC, kXPlain>(b, G, n, smem, s);
+    }
 }
 
-}  // namespace
-
-int bm_max_active_clusters(int vec, int G) {
-    static std::mutex mu;
-    static int cache[2][kMaxCluster + 1] = {};
-    std::lock_guard<std::mutex> lk(mu);
-    const int vi = vec == 8 ? 0 : 1;
-    if (cache[vi][G]) return cache[vi][G];
+template <int VEC>
+int occupancy_clusters(int G, size_t smem) {
+    auto kern = bm_fused_kernel<VEC, kXPlain>;
+    if (set_attrs<VEC, kXPlain>() != cudaSuccess) return 1;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -275,61 +370,82 @@ int bm_max_active_clusters(int vec, int G) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cfg.blockDim = dim3(kNT);
+    cfg.blockDim = dim3(Threads<VEC>::value);
     cfg.gridDim = dim3((unsigned)(G * 64));
+    cfg.dynamicSmemBytes = smem;
     int n = 0;
-    cudaError_t e;
-    if (vec == 8) {
-        auto kern = bm_fused_kernel<8, kNT, kU>;
-        cfg.dynamicSmemBytes = fused_smem_bytes<8, kNT>();
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    } else {
-        auto kern = bm_fused_kernel<1, kNT, kU>;
-        cfg.dynamicSmemBytes = fused_smem_bytes<1, kNT>();
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    }
-    if (e != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();
         n = 1;
     }
-    cache[vi][G] = n;
+    return n;
+}
+
+int seg_inputs_max(const BMBatch& b) {
+    int m = 1;
+    for (int i = 0; i < b.nprob; ++i) m = std::max(m, b.p[i].seg_inputs);
+    return m;
+}
+
+}  // namespace
+
+int bm_max_active_clusters(int vec, int G) {
+    // occupancy with the fixed part of shared memory plus 8 KB of masks (4096 inputs)
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_pair(vec * 64 + G, dev);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    const size_t smem = bm_smem_bytes(vec, 4096);
+    const int n = vec == 8 ? occupancy_clusters<8>(G, smem) : vec == 4 ? occupancy_clusters<4>(G, smem)
+                                                                       : occupancy_clusters<1>(G, smem);
+    cache[key] = n;
     return n;
 }
 
 int bm_default_cluster() {
     const int g = env_int("IAM_BM_CLUSTER", 8);
-    return (g == 2 || g == 4 || g == 8 || g == 16) ? g : 8;
+    return (g == 1 || g == 2 || g == 4 || g == 8 || g == 16) ? g : 8;
 }
 
-// Fills the tiling of each problem (log2L, n_tiles, cluster_begin) so the whole batch is
-// about one wave of resident clusters, giving wider tiles to problems with more work.
+// Column tiling: start every problem at the widest tile (32 lanes x VEC columns) and keep
+// halving the tile of the problem with the most work per cluster while the batch still
+// fits in one wave of resident clusters and the row segment stays >= 32 bytes.
 void bm_plan_tiles(BMBatch& b, int vec, int G, int max_clusters) {
-    double work_total = 0.0;
-    for (int i = 0; i < b.nprob; ++i) work_total += (double)b.p[i].cols * b.p[i].n_rows_valid;
+    (void)G;
     const int forced = env_int("IAM_BM_LOG2L", -1);
+    int l2[kMaxProblems];
+    for (int i = 0; i < b.nprob; ++i) l2[i] = (forced >= 0 && forced <= 5) ? forced : 5;
+    auto tiles = [&](int i, int l) { return (b.p[i].cols + (vec << l) - 1) / (vec << l); };
+    if (forced < 0) {
+        for (;;) {
+            int total = 0;
+            for (int i = 0; i < b.nprob; ++i) total += tiles(i, l2[i]);
+            int best = -1;
+            double best_work = 0.0;
+            for (int i = 0; i < b.nprob; ++i) {
+                if (l2[i] == 0 || (vec << (l2[i] - 1)) < 16) continue;     // keep >= 32 B per row
+                if (tiles(i, l2[i] - 1) == tiles(i, l2[i])) continue;        // no gain
+                const int extra = tiles(i, l2[i] - 1) - tiles(i, l2[i]);
+                if (total + extra > max_clusters) continue;
+                const double work = (double)b.p[i].n_rows_valid * std::min(b.p[i].cols, vec << l2[i]);
+                if (work > best_work) {
+                    best_work = work;
+                    best = i;
+                }
+            }
+            if (best < 0) break;
+            --l2[best];
+        }
+    }
     int begin = 0;
     for (int i = 0; i < b.nprob; ++i) {
         BMProblem& p = b.p[i];
-        const double share = work_total > 0 ? max_clusters * ((double)p.cols * p.n_rows_valid) / work_total : 1.0;
-        int best = 5;
-        if (forced >= 0 && forced <= 5) {
-            best = forced;
-        } else {
-            for (int l2 = 5; l2 >= 0; --l2) {
-                const int tw = vec << l2;
-                const int tiles = (p.cols + tw - 1) / tw;
-                best = l2;
-                if (tiles >= share) break;  // first (widest) tiling that fills its share
-            }
-            // never narrower than needed to cover >1 lane group per row when cols is tiny
-        }
-        const int tw = vec << best;
-        p.log2L = best;
-        p.n_tiles = (p.cols + tw - 1) / tw;
+        p.log2L = l2[i];
+        p.n_tiles = tiles(i, l2[i]);
         p.cluster_begin = begin;
         begin += p.n_tiles;
     }
@@ -343,20 +459,16 @@ int bm_total_clusters(const BMBatch& b) {
 
 int bm_launch(const BMBatch& b, int vec, int G, cudaStream_t s) {
     const int n = b.mode == kModeSelectOnly ? b.nprob : bm_total_clusters(b);
-    if (vec == 8) return launch_fused<8>(b, G, n, s);
-    return launch_fused<1>(b, G, n, s);
+    const size_t smem = bm_smem_bytes(vec, seg_inputs_max(b));
+    if (smem > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "bucketmul: segment too large for shared memory");
+    if (vec == 8) return launch_vec<8>(b, G, n, smem, s);
+    if (vec == 4) return launch_vec<4>(b, G, n, smem, s);
+    return launch_vec<1>(b, G, n, smem, s);
 }
 
 int bm_launch_cutoff(const float* x, const uint16_t* probes, int P, int target, float* out, int* iters,
                      cudaStream_t s) {
     bm_cutoff_kernel<256><<<1, 256, 0, s>>>(x, probes, P, target, out, iters);
-    IAM_CUDA_TRY(cudaGetLastError());
-    return IAM_OK;
-}
-
-int bm_launch_gather(const int32_t* list, const int* seg_counts, int G, int seg_cap, int32_t* rows_out,
-                     int* count_out, cudaStream_t s) {
-    bm_gather_dispatch_kernel<<<1, 256, 0, s>>>(list, seg_counts, G, seg_cap, rows_out, count_out);
     IAM_CUDA_TRY(cudaGetLastError());
     return IAM_OK;
 }

@@ -1,14 +1,8 @@
-// iam_bucketmul.cuh -- device building blocks of the bucketMul sparse GEMV on sm_100a.
-//
-// One bucketMul = cutoff search -> row selection -> accumulation (bucketMul.cl:68-497).
-// On B200 the three phases run in ONE launch of thread-block clusters (iam_bucketmul.cu):
-//   * every CTA recomputes the cutoff for its own use (4096 importance values held in
-//     registers, one barrier per bisection step) -- no cutoff launch, no global round trip;
-//   * the G CTAs of a cluster split the bucket rows into G input segments, select and
-//     compact their segment (ascending row order -> deterministic), then rebalance the
-//     selected rows evenly across the cluster through distributed shared memory counts;
-//   * each cluster owns one column tile, so clusters never exchange data; the G partial
-//     tiles of a cluster are summed through DSMEM in a fixed order (no global atomics).
+// iam_bucketmul.cuh -- device building blocks of the bucketMul sparse GEMV on sm_100a:
+// the cutoff search (bucketMul.cl:68-214), the row-selection predicate (:351-386) with a
+// compacting scan, input providers that fuse the layer glue into the matmul prologue, and
+// the per-slot accumulation of bucketMul (:392-447).  The fused kernel that strings them
+// together is in iam_bucketmul.cu.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -32,9 +26,9 @@ struct CutoffShared {
 // the block must call it; all receive the same cutoff.  The counts are exact integers and
 // min/max are order independent, so any thread layout reproduces the reference's result
 // bit for bit.  `target` = P - quantile (bucketMul.cl:81, bucket_mul.hpp:164).
-template <int NT>
-__device__ float block_find_cutoff(const float* __restrict__ x, const uint16_t* __restrict__ probes,
-                                   int P, int target, CutoffShared<NT>& sm, int* iters_out) {
+template <int NT, class XP>
+__device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ probes, int P,
+                                   int target, CutoffShared<NT>& sm, int* iters_out) {
     constexpr int NW = NT / 32;
     constexpr int VPT = (kProbes + NT - 1) / NT;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -45,7 +39,7 @@ __device__ float block_find_cutoff(const float* __restrict__ x, const uint16_t* 
     for (int k = 0; k < VPT; ++k) {
         const int i = tid + k * NT;
         if (i < P) {
-            const float imp = importance(x[i], h2f(probes[i]));
+            const float imp = importance(xp(i), h2f(__ldg(probes + i)));
             v[k] = imp;
             mn = fminf(mn, imp);
             mx = fmaxf(mx, imp);
@@ -110,6 +104,76 @@ __device__ float block_find_cutoff(const float* __restrict__ x, const uint16_t* 
     return result;
 }
 
+// ------------------------------------------------------------------ input providers
+// The bucketMul input x is read through a provider so layer glue runs inside the matmul's
+// prologue: every CTA evaluates the same function of the same bits, so all CTAs see
+// bit-identical x and therefore compute the same cutoff and selection.
+
+// x = a plain fp32 vector.
+struct XPlain {
+    const float* x;
+    IAM_DEV float operator()(int i) const { return __ldg(x + i); }
+};
+
+// x = rmsNorm32fast(src) * gain (aux.cl:156-196 then mul16x32 aux.cl:434-440): the scale is
+// computed once per CTA by block_rms_scale.
+struct XRms {
+    const float* src;
+    const uint16_t* gain;
+    float scale;
+    IAM_DEV float operator()(int i) const {
+        return __fmul_rn(h2f(__ldg(gain + i)), __fmul_rn(__ldg(src + i), scale));
+    }
+};
+
+// x = silu32(gate, up) = up * gate / (1 + exp(-gate)) (matrix.cl:27-32).
+struct XSilu {
+    const float* gate;
+    const float* up;
+    IAM_DEV float operator()(int i) const {
+        const float gv = __ldg(gate + i), uv = __ldg(up + i);
+        return __fdiv_rn(__fmul_rn(uv, gv), __fadd_rn(1.0f, expf(-gv)));
+    }
+};
+
+// rsqrt(sum(x^2)/n + eps) with the reduction order of rmsNorm32fast (aux.cl:165-190) when
+// n is a multiple of 256 (256 contiguous runs, then a halving tree), else sequential.
+// Every thread returns the same value.  red must hold 256 floats.
+template <int NT>
+__device__ float block_rms_scale(const float* __restrict__ x, int n, float eps, float* red) {
+    static_assert(NT >= 256, "rms scale needs >= 256 threads");
+    const int tid = threadIdx.x;
+    if (n >= 256 && n % 256 == 0) {
+        if (tid < 256) {
+            const int e = n / 256;
+            float s = 0.0f;
+            for (int i = tid * e; i < tid * e + e; ++i) {
+                const float v = __ldg(x + i);
+                s = __fadd_rn(s, __fmul_rn(v, v));
+            }
+            red[tid] = s;
+        }
+        __syncthreads();
+        for (int s = 128; s > 0; s >>= 1) {
+            if (tid < s) red[tid] = __fadd_rn(red[tid], red[tid + s]);
+            __syncthreads();
+        }
+    } else {
+        if (tid == 0) {
+            float s = 0.0f;
+            for (int i = 0; i < n; ++i) {
+                const float v = __ldg(x + i);
+                s = __fadd_rn(s, __fmul_rn(v, v));
+            }
+            red[0] = s;
+        }
+        __syncthreads();
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)n), eps)));
+    __syncthreads();
+    return scale;
+}
+
 // ------------------------------------------------------------------ row selection
 
 template <int NT>
@@ -117,37 +181,59 @@ struct ScanShared {
     int tot[2][NT / 32];
 };
 
-// prepareDispatch (bucketMul.cl:351-386) for inputs [i0, i1) of one expert: row
-// row0 + 16*i + r is selected iff 1e5*|x[i]*stats[row][stride-1]| >= cutoff.  Selected
-// rows are written to rows_out[0..n) in ascending order; returns n (same in all threads).
+// prepareDispatch predicate (bucketMul.cl:351-386) for inputs [i0, i1) of one expert: bit r
+// of masks[i - i0] is set iff row row0 + 16*i + r is selected, i.e.
+// 1e5*|x[i]*stats[row][stride-1]| >= cutoff.  Returns the number of selected rows (same in
+// all threads).
+template <int NT, class XP>
+__device__ int block_masks(const XP& xp, const uint16_t* __restrict__ stats, int stride,
+                           long long row0, int n_rows_valid, int i0, int i1, float cutoff,
+                           uint16_t* __restrict__ masks, ScanShared<NT>& sm) {
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int cnt = 0;
+    for (int i = i0 + tid; i < i1; i += NT) {
+        const float xi = xp(i);
+        const int rmax = min(16, n_rows_valid - i * 16);
+        const uint16_t* sp = stats + (row0 + (long long)i * 16) * stride + (stride - 1);
+        unsigned mask = 0u;
+        if (stride == 1 && rmax == 16 && ((reinterpret_cast<uintptr_t>(sp) & 15u) == 0)) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(sp));
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(sp + 8));
+            const uint32_t wds[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const uint32_t hb = (r & 1) ? (wds[r >> 1] >> 16) : (wds[r >> 1] & 0xffffu);
+                if (importance(xi, h2f(hb)) >= cutoff) mask |= 1u << r;  // ">=" (:380)
+            }
+        } else {
+            for (int r = 0; r < rmax; ++r)
+                if (importance(xi, h2f(__ldg(sp + r * stride))) >= cutoff) mask |= 1u << r;
+        }
+        masks[i - i0] = (uint16_t)mask;
+        cnt += __popc(mask);
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (lane == 0) sm.tot[0][warp] = cnt;
+    __syncthreads();
+    int total = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) total += sm.tot[0][w];
+    __syncthreads();
+    return total;
+}
+
+// Writes the selected rows of inputs [i0, i1) (masks from block_masks) to rows_out in
+// ascending row order.
 template <int NT>
-__device__ int block_select(const float* __restrict__ x, const uint16_t* __restrict__ stats,
-                            int stride, long long row0, int n_rows_valid, int i0, int i1,
-                            float cutoff, int32_t* __restrict__ rows_out, ScanShared<NT>& sm) {
+__device__ void block_write_rows(const uint16_t* __restrict__ masks, long long row0, int i0,
+                                 int i1, int32_t* __restrict__ rows_out, ScanShared<NT>& sm) {
     constexpr int NW = NT / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int base = 0, round = 0;
     for (int ib = i0; ib < i1; ib += NT, ++round) {
         const int i = ib + tid;
-        unsigned mask = 0u;
-        if (i < i1) {
-            const float xi = x[i];
-            const int rmax = min(16, n_rows_valid - i * 16);
-            const uint16_t* sp = stats + (row0 + (long long)i * 16) * stride + (stride - 1);
-            if (stride == 1 && rmax == 16 && ((reinterpret_cast<uintptr_t>(sp) & 15u) == 0)) {
-                const uint4 a = *reinterpret_cast<const uint4*>(sp);
-                const uint4 b = *reinterpret_cast<const uint4*>(sp + 8);
-                const uint32_t wds[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int r = 0; r < 16; ++r) {
-                    const uint32_t hb = (r & 1) ? (wds[r >> 1] >> 16) : (wds[r >> 1] & 0xffffu);
-                    if (importance(xi, h2f(hb)) >= cutoff) mask |= 1u << r;  // ">=" (:380)
-                }
-            } else {
-                for (int r = 0; r < rmax; ++r)
-                    if (importance(xi, h2f(sp[r * stride])) >= cutoff) mask |= 1u << r;
-            }
-        }
+        unsigned mask = (i < i1) ? masks[i - i0] : 0u;
         const int n = __popc(mask);
         int inc = n;
 #pragma unroll
@@ -175,7 +261,6 @@ __device__ int block_select(const float* __restrict__ x, const uint16_t* __restr
         base += total;
     }
     __syncthreads();
-    return base;
 }
 
 // ------------------------------------------------------------------ accumulation
@@ -186,6 +271,7 @@ template <>
 struct VecLoad<8> {
     using T = uint4;
     static IAM_DEV T load(const uint16_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+    static IAM_DEV T zero() { return make_uint4(0u, 0u, 0u, 0u); }
     static IAM_DEV uint32_t bits(const T& v, int k) {
         const uint32_t w = (k >> 1) == 0 ? v.x : (k >> 1) == 1 ? v.y : (k >> 1) == 2 ? v.z : v.w;
         return (k & 1) ? (w >> 16) : (w & 0xffffu);
@@ -195,6 +281,7 @@ template <>
 struct VecLoad<4> {
     using T = uint2;
     static IAM_DEV T load(const uint16_t* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+    static IAM_DEV T zero() { return make_uint2(0u, 0u); }
     static IAM_DEV uint32_t bits(const T& v, int k) {
         const uint32_t w = (k >> 1) == 0 ? v.x : v.y;
         return (k & 1) ? (w >> 16) : (w & 0xffffu);
@@ -204,6 +291,7 @@ template <>
 struct VecLoad<1> {
     using T = uint32_t;
     static IAM_DEV T load(const uint16_t* p) { return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p)); }
+    static IAM_DEV T zero() { return 0u; }
     static IAM_DEV uint32_t bits(const T& v, int) { return v; }
 };
 

@@ -11,27 +11,41 @@ constexpr int kMaxCluster = 16;
 
 enum BMMode { kModeFused = 0, kModeSelectOnly = 1, kModeMulOnly = 2 };
 
+// How the bucketMul input x is produced (all CTAs derive bit-identical x).
+enum BMXMode {
+    kXPlain = 0,  // x = x[i]
+    kXRms = 1,    // x = rmsNorm32fast(x)[i] * gain[i]        (aux.cl:156-196, :434-440)
+    kXSilu = 2    // x = up[i] * x[i] / (1 + exp(-x[i])), x = gate  (matrix.cl:27-32)
+};
+
 // One bucketMul (one weight matrix times one input vector).
 struct BMProblem {
-    const uint16_t* buckets;  // [R_total][cols] (full tensor; rows are absolute)
+    const uint16_t* buckets;  // [R_total][cols]; rows are absolute indices (may be a virtual base)
     const uint16_t* stats;    // [R_total][stats_stride]
     const uint16_t* probes;   // already offset by expert_no * 4096
-    const float* x;           // [in_dim]
+    const float* x;           // input (plain), RMS source (kXRms) or gate (kXSilu)
+    const float* x2;          // up (kXSilu)
+    const uint16_t* gain;     // RMS gain (kXRms)
+    float norm_eps;           // kXRms
+    int norm_n;               // kXRms: length of the normalised vector
     float* out;               // [16 * cols]
-    const float* residual;    // optional: out = residual + result
-    int32_t* list;            // dispatch list scratch: G segments of seg_inputs*16 rows
-    int* seg_counts;          // [G] segment counts (select-only writes, mul-only reads)
+    const float* residual;    // optional: out = residual + result (add32, bucketMul.cl:517-520)
+    int32_t* list;            // compact dispatch list scratch (>= n_rows_valid rows)
+    int* sel_total;           // selected-row total (select-only writes, mul-only reads)
     float* cutoff_out;        // optional
     int* count_out;           // optional
     int* iters_out;           // optional
+    long long* dbg;           // optional per-phase globaltimer stamps (cluster 0, CTA 0)
     long long row0;           // expert row offset (expertSize * expertNo)
-    int n_rows_valid;         // rows considered: min(expert_size, 16*in_dim)
-    int n_inputs;             // ceil(n_rows_valid / 16)
-    int cols;                 // bucket columns C
+    long long bucket_row0;    // absolute row held by buckets[0] (0, or the first row of a shard)
+    int in_begin;             // first input of this shard (row-parallel tensor parallelism)
+    int n_rows_valid;         // rows of the expert considered: min(expert_size, 16*in_dim)
+    int n_inputs;             // inputs end: ceil(n_rows_valid / 16)
+    int cols;                 // bucket columns C of the buckets tensor
     int stats_stride;         // 4 (file layout) or 1 (packed channel 3)
     int P;                    // probes used by the cutoff: min(in_dim, 4096)
     int target;               // P - quantile
-    int seg_inputs;           // inputs per cluster segment
+    int seg_inputs;           // inputs per CTA segment of the cluster
     int log2L;                // lanes per row segment = 1 << log2L
     int n_tiles;              // column tiles (clusters) of this problem
     int cluster_begin;        // index of its first cluster in the launch
@@ -41,17 +55,17 @@ struct BMBatch {
     BMProblem p[kMaxProblems];
     int nprob;
     int mode;
+    int xmode;
 };
 
 int bm_default_cluster();
 int bm_max_active_clusters(int vec, int G);
+size_t bm_smem_bytes(int vec, int seg_inputs);
 void bm_plan_tiles(BMBatch& b, int vec, int G, int max_clusters);
 int bm_total_clusters(const BMBatch& b);
 int bm_launch(const BMBatch& b, int vec, int G, cudaStream_t s);
 int bm_launch_cutoff(const float* x, const uint16_t* probes, int P, int target, float* out, int* iters,
                      cudaStream_t s);
-int bm_launch_gather(const int32_t* list, const int* seg_counts, int G, int seg_cap, int32_t* rows_out,
-                     int* count_out, cudaStream_t s);
 int bm_launch_stats_pack(const uint16_t* s4, long long rows, uint16_t* s1, cudaStream_t s);
 int bucketize_launch(const uint16_t* w, int out_dim, int in_dim, uint16_t* buckets, uint16_t* stats4,
                      uint16_t* stats1, uint16_t* probes, cudaStream_t s);

@@ -1,6 +1,7 @@
 // iam_capi.cu -- C ABI entry points of libiamb200.so for the bucketMul operator.
 // Declarations and the reference interface each one replaces: include/iam_b200.h.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -29,16 +30,16 @@ using namespace iam;
 
 struct iam_bucketmul_s {
     int device = 0;
-    int32_t* list = nullptr;  // dispatch list scratch
+    int32_t* list = nullptr;  // compact dispatch list scratch
     size_t list_cap = 0;      // capacity in rows
-    int* seg_counts = nullptr;
     float* cutoff = nullptr;  // device scalar
-    int* ints = nullptr;      // device scalars: [0] count, [1] iters
+    int* ints = nullptr;      // device scalars: [0] count, [1] iters, [2] selected total
     // dispatch recorded by iam_bucketmul_calc_dispatch (consumed by iam_bucketmul_mul)
     bool have_dispatch = false;
     BMProblem disp{};
     int disp_G = 8;
     int disp_bucket_cols = 0;
+    long long* dbg = nullptr;  // optional phase stamps
 };
 
 namespace {
@@ -79,19 +80,27 @@ int fill_problem(iam_bucketmul_s* h, BMProblem& p, int G, const float* x, const 
     p.P = in_dim < IAM_PROBES_COUNT ? in_dim : IAM_PROBES_COUNT;
     p.target = bm_target(effort, p.P);
     p.seg_inputs = (p.n_inputs + G - 1) / G;
-    int rc = ensure_list(h, (size_t)p.seg_inputs * 16 * G);
+    if ((p.row0 + p.n_rows_valid) * (long long)bucket_cols >= (1LL << 31))
+        return fail(IAM_ERR_UNSUPPORTED, "bucketmul: rows * bucket_cols must stay below 2^31 elements");
+    int rc = ensure_list(h, (size_t)p.n_rows_valid);
     if (rc) return rc;
     p.list = h->list;
-    p.seg_counts = h->seg_counts;
+    p.sel_total = h->ints + 2;
+    p.dbg = h->dbg;
     return IAM_OK;
 }
 
+// Widest vector load every problem of the batch supports (IAM_BM_VEC may lower it).
 int pick_vec(const BMBatch& b) {
+    int vec = 8;
+    const char* env = getenv("IAM_BM_VEC");
+    if (env && (atoi(env) == 4 || atoi(env) == 1)) vec = atoi(env);
     for (int i = 0; i < b.nprob; ++i) {
         const BMProblem& p = b.p[i];
-        if (p.cols % 8 != 0 || (reinterpret_cast<uintptr_t>(p.buckets) & 15u) != 0) return 1;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(p.buckets);
+        while (vec > 1 && (p.cols % vec != 0 || (a & (uintptr_t)(2 * vec - 1)) != 0)) vec = vec == 8 ? 4 : 1;
     }
-    return 8;
+    return vec;
 }
 
 }  // namespace
@@ -112,6 +121,23 @@ int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor) {
     return IAM_OK;
 }
 
+int iam_bucketmul_plan_info(int vec, int cluster_size, int bucket_cols, int in_dim, int* max_active_clusters,
+                            int* log2_lanes, int* n_tiles) {
+    if ((vec != 8 && vec != 4 && vec != 1) || cluster_size < 1 || cluster_size > kMaxCluster || bucket_cols <= 0 || in_dim <= 0)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_plan_info: bad arguments");
+    const int mac = bm_max_active_clusters(vec, cluster_size);
+    BMBatch b;
+    memset(&b, 0, sizeof(b));
+    b.nprob = 1;
+    b.p[0].cols = bucket_cols;
+    b.p[0].n_rows_valid = 16 * in_dim;
+    bm_plan_tiles(b, vec, cluster_size, mac);
+    if (max_active_clusters) *max_active_clusters = mac;
+    if (log2_lanes) *log2_lanes = b.p[0].log2L;
+    if (n_tiles) *n_tiles = b.p[0].n_tiles;
+    return IAM_OK;
+}
+
 int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
     if (!out) return fail(IAM_ERR_ARG, "iam_bucketmul_create: null out");
     *out = nullptr;
@@ -120,9 +146,8 @@ int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
     IAM_CUDA_TRY(cudaSetDevice(device));
     iam_bucketmul_s* h = new iam_bucketmul_s();
     h->device = device;
-    cudaError_t e = cudaMalloc(&h->seg_counts, sizeof(int) * kMaxCluster);
-    if (e == cudaSuccess) e = cudaMalloc(&h->cutoff, sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * 2);
+    cudaError_t e = cudaMalloc(&h->cutoff, sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * 4);
     if (e != cudaSuccess) {
         iam_bucketmul_destroy(h);
         return cuda_fail(e, "iam_bucketmul_create: cudaMalloc");
@@ -134,7 +159,6 @@ int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
 int iam_bucketmul_destroy(iam_bucketmul_t h) {
     if (!h) return IAM_OK;
     cudaFree(h->list);
-    cudaFree(h->seg_counts);
     cudaFree(h->cutoff);
     cudaFree(h->ints);
     delete h;
@@ -181,8 +205,10 @@ int iam_bucketmul_read_dispatch(iam_bucketmul_t h, int32_t* rows_dev, int* count
                                 void* stream) {
     if (!h || !h->have_dispatch) return fail(IAM_ERR_ARG, "iam_bucketmul_read_dispatch: no dispatch recorded");
     cudaStream_t s = (cudaStream_t)stream;
-    int rc = bm_launch_gather(h->list, h->seg_counts, h->disp_G, h->disp.seg_inputs * 16, rows_dev, count_dev, s);
-    if (rc) return rc;
+    if (rows_dev)
+        IAM_CUDA_TRY(cudaMemcpyAsync(rows_dev, h->list, sizeof(int32_t) * (size_t)h->disp.n_rows_valid,
+                                     cudaMemcpyDeviceToDevice, s));
+    if (count_dev) IAM_CUDA_TRY(cudaMemcpyAsync(count_dev, h->ints, sizeof(int), cudaMemcpyDeviceToDevice, s));
     if (cutoff_dev) IAM_CUDA_TRY(cudaMemcpyAsync(cutoff_dev, h->cutoff, sizeof(float), cudaMemcpyDeviceToDevice, s));
     return IAM_OK;
 }
@@ -232,6 +258,12 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
     const int vec = pick_vec(b);
     bm_plan_tiles(b, vec, G, bm_max_active_clusters(vec, G));
     return bm_launch(b, vec, G, (cudaStream_t)stream);
+}
+
+int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev) {
+    if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_phase_times: null handle");
+    h->dbg = times_dev;
+    return IAM_OK;
 }
 
 int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_dev, void* stream) {
