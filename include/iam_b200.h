@@ -52,10 +52,12 @@ const char* iam_last_error(void);
 int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
 
 /* Diagnostics: resident clusters of `cluster_size` CTAs for the fused bucketMul kernel with
- * vec-wide loads (8 or 1) on the current device, and the tiling chosen for one bucketMul of
- * bucket_cols columns and in_dim inputs (log2 of lanes per row, column tiles). */
+ * vec-wide loads (8, 4 or 1) on the current device, and the plan chosen for one bucketMul of
+ * bucket_cols columns and in_dim inputs: log2 of lanes per row slice, column tiles, and input
+ * splits (clusters per column tile). */
 int iam_bucketmul_plan_info(int vec, int cluster_size, int bucket_cols, int in_dim,
-                            int* max_active_clusters, int* log2_lanes, int* n_tiles);
+                            int* max_active_clusters, int* log2_lanes, int* n_tiles,
+                            int* n_splits);
 
 /* ------------------------------------------------------------------ bucketMul operator */
 /* Replaces the BucketMul singleton (bucket_mul.hpp:99-268).  The handle owns what the
@@ -103,9 +105,10 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
                        int expert_no, int in_dim, int bucket_cols, int expert_size, float effort,
                        float* out_dev, int* count_dev, float* cutoff_dev, void* stream);
 
-/* Diagnostics: every later launch of `h` writes 7 globaltimer stamps (ns) of its first CTA
- * to times_dev[0..6]: start, cutoff done, masks done, list done, accumulation done,
- * partial tile done, end.  NULL turns it off. */
+/* Diagnostics: every later launch of `h` writes globaltimer stamps (ns) of its first CTA
+ * to times_dev[0..9] (16 slots): [0] start, [1] cutoff done, [2] row lists done, [3] cluster
+ * numbering done, [4] accumulation done, [5] partial tile done, [6] end, [8] cutoff loads
+ * and min/max done, [9] bisection done.  NULL turns it off. */
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev);
 
 /* Packs channel 3 of a [rows][4] stats array into [rows] (stats_stride = 1 layout). */

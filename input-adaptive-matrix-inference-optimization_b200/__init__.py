@@ -31,7 +31,7 @@ _SIGNATURES = {
     "iam_version": [],
     "iam_last_error": [],
     "iam_device_info": [_i32, _vp, _vp, _vp],
-    "iam_bucketmul_plan_info": [_i32, _i32, _i32, _i32, _vp, _vp, _vp],
+    "iam_bucketmul_plan_info": [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp],
     "iam_bucketmul_create": [_vp, _i32],
     "iam_bucketmul_destroy": [_vp],
     "iam_bucketmul_cutoff": [_vp, _vp, _vp, _i32, _i32, _f32, _vp, _vp, _vp],
@@ -144,11 +144,11 @@ class BucketMul:
 
 
 def plan_info(vec, cluster, bucket_cols, in_dim):
-    """-> (max_active_clusters, log2_lanes_per_row, n_tiles) of the fused bucketMul tiling."""
-    a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    """-> (max_active_clusters, log2_lanes_per_row, n_tiles, n_splits) of the fused bucketMul plan."""
+    a, b, c, d = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     check(load_library().iam_bucketmul_plan_info(vec, cluster, bucket_cols, in_dim, ctypes.byref(a),
-                                                 ctypes.byref(b), ctypes.byref(c)))
-    return a.value, b.value, c.value
+                                                 ctypes.byref(b), ctypes.byref(c), ctypes.byref(d)))
+    return a.value, b.value, c.value, d.value
 
 
 def stats_pack(stats4, stats1, stream=None):

@@ -2,19 +2,21 @@
 //
 // Reference operator: BucketMul (bucket_mul.hpp:99-268) over bucketMul.cl:68-497.
 //
-// One launch runs up to kMaxProblems bucketMuls.  Grid = clusters of G CTAs; cluster ci
-// owns one column tile of one problem.  Per CTA (rank g of its cluster):
+// One launch runs up to kMaxProblems bucketMuls.  Grid = clusters of G CTAs; a cluster owns
+// one column tile of one problem and one of n_split input ranges.  Per CTA (rank g):
 //   1. cutoff: block_find_cutoff over x[0:P] (every CTA, identical result);
-//   2. selection masks for input segment g (block_masks), cluster barrier, prefix over the
-//      G segment counts read through DSMEM, then the selected rows are written COMPACT and
-//      ascending into the dispatch list (every cluster writes the same values), cluster
-//      barrier -- position p of the selection is list[p] for every CTA;
-//   3. the CTA takes positions [S*g/G, S*(g+1)/G): it stages {row*C, x(row)} for 512 rows
-//      at a time in shared memory (next chunk prefetched during the current one), and each
+//   2. selection masks for its share of the cluster's inputs (block_masks), then its
+//      selected rows as 16-bit offsets in its own shared memory; one cluster barrier; a
+//      prefix over the G counts read through DSMEM numbers the cluster's rows 0..S-1;
+//   3. the CTA takes rows [S*g/G, S*(g+1)/G) of that numbering, wherever they live: it
+//      stages {row*C, x(row)} for 2048 rows at a time (row offsets read from the owner's
+//      shared memory through DSMEM, next chunk fetched during the current one), and each
 //      lane streams VEC-wide slices of its rows with register double-buffered loads,
 //      adding x*w into lane-private per-slot accumulators in shared memory;
-//   4. lane accumulators -> one partial tile per CTA -> fixed-order DSMEM sum across the
-//      cluster -> out (+ residual).  No global atomics; results are bitwise deterministic.
+//   4. lane accumulators -> a partial tile per CTA -> fixed-order DSMEM sum across the
+//      cluster; with n_split > 1 the partial tiles go to global scratch and the last cluster
+//      to arrive at each slice adds them in split order -> out (+ residual).
+// No float atomics anywhere: results are bitwise deterministic.
 #include <algorithm>
 #include <cstdlib>
 #include <map>
@@ -42,7 +44,10 @@ struct FusedHeader {
     ScanShared<NT> scan;
     float red[256];
     int my_count;
+    int my_row_base;
+    int last_flag;
     int pre[kMaxCluster + 1];
+    int row_base[kMaxCluster];
 };
 
 constexpr size_t align16(size_t n) { return (n + 15) / 16 * 16; }
@@ -56,19 +61,14 @@ constexpr size_t fixed_smem_bytes() {
 }
 
 size_t bm_smem_bytes(int vec, int seg_inputs) {
-    const size_t masks = align16((size_t)seg_inputs * sizeof(uint16_t));
-    if (vec == 8) return fixed_smem_bytes<8>() + masks;
-    if (vec == 4) return fixed_smem_bytes<4>() + masks;
-    return fixed_smem_bytes<1>() + masks;
+    const size_t lists = align16((size_t)seg_inputs * sizeof(uint16_t))         // masks
+                         + align16((size_t)seg_inputs * 16 * sizeof(uint16_t));  // local rows
+    if (vec == 8) return fixed_smem_bytes<8>() + lists;
+    if (vec == 4) return fixed_smem_bytes<4>() + lists;
+    return fixed_smem_bytes<1>() + lists;
 }
 
-IAM_DEV void stamp(long long* dbg, int k) {
-    if (dbg) {
-        long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        dbg[k] = t;
-    }
-}
+IAM_DEV void stamp(long long* dbg, int k) { debug_stamp(dbg, k); }
 
 template <int XM, int NT>
 struct Provider;
@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     int pi = 0;
     while (pi + 1 < batch.nprob && ci >= batch.p[pi + 1].cluster_begin) ++pi;
     const BMProblem& pr = batch.p[pi];
-    const int tile = ci - pr.cluster_begin;
+    const int local = ci - pr.cluster_begin;
+    const int tile = local % pr.n_tiles, split = local / pr.n_tiles;
+    const int K = pr.n_split;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     long long* dbg = (ci == 0 && g == 0 && tid == 0) ? pr.dbg : nullptr;
     stamp(dbg, 0);
@@ -113,25 +115,36 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     float* part = reinterpret_cast<float*>(stage + 2 * kCH);
     float* acc = part + 16 * VEC * 32;
     uint16_t* masks = reinterpret_cast<uint16_t*>(acc + NT * VEC * 16);
+    uint16_t* rows16 = masks + align16((size_t)pr.seg_inputs * sizeof(uint16_t)) / sizeof(uint16_t);
 
     const auto xp = Provider<XM, NT>::make(pr, hdr.red);
     const long long row0 = pr.row0;
 
-    // ---- phases 1-2: cutoff, selection masks, compact dispatch list
-    int S;
-    if (batch.mode != kModeMulOnly) {
+    // ---- phases 1-2: cutoff, selection masks, cluster-local row numbering
+    int S, list_lo = 0;
+    const bool from_list = batch.mode == kModeMulOnly;
+    if (!from_list) {
         int iters = 0;
-        const float cutoff = block_find_cutoff<NT>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters);
+        const float cutoff =
+            block_find_cutoff<NT>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters, dbg ? dbg + 8 : nullptr);
         stamp(dbg, 1);
-        const int i0 = min(pr.in_begin + g * pr.seg_inputs, pr.n_inputs);
-        const int i1 = min(i0 + pr.seg_inputs, pr.n_inputs);
+        const int span = (pr.n_inputs - pr.in_begin + K - 1) / K;
+        const int klo = min(pr.in_begin + split * span, pr.n_inputs);
+        const int khi = min(klo + span, pr.n_inputs);
+        const int i0 = min(klo + g * pr.seg_inputs, khi);
+        const int i1 = min(i0 + pr.seg_inputs, khi);
         const int n = block_masks<NT>(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i0, i1, cutoff,
                                       masks, hdr.scan);
-        if (tid == 0) hdr.my_count = n;
+        block_write_rows_local<NT>(masks, i0, i1, rows16, hdr.scan);
+        if (tid == 0) {
+            hdr.my_count = n;
+            hdr.my_row_base = (int)(row0 + 16LL * i0);
+        }
         stamp(dbg, 2);
-        cluster.sync();
+        cluster.sync();  // counts and local row lists visible cluster-wide
         if (warp == 0) {  // all G peer counts read in parallel, then a warp scan
             const int c = lane < G ? *cluster.map_shared_rank(&hdr.my_count, lane) : 0;
+            if (lane < G) hdr.row_base[lane] = *cluster.map_shared_rank(&hdr.my_row_base, lane);
             int inc = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -141,22 +154,33 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
             if (lane <= G) hdr.pre[lane] = inc - c;
         }
         __syncthreads();
-        block_write_rows<NT>(masks, row0, i0, i1, pr.list + hdr.pre[g], hdr.scan);
         S = hdr.pre[G];
-        if (tile == 0 && g == 0 && tid == 0) {
-            if (pr.cutoff_out) *pr.cutoff_out = cutoff;
-            if (pr.iters_out) *pr.iters_out = iters;
-            if (pr.count_out) *pr.count_out = S;
-            if (batch.mode == kModeSelectOnly && pr.sel_total) *pr.sel_total = S;
+        if (batch.mode == kModeSelectOnly) {  // one cluster per problem: publish the compact list
+            const int base = hdr.pre[g];
+            for (int j = tid; j < n; j += NT) pr.list[base + j] = hdr.my_row_base + (int)rows16[j];
+            if (g == 0 && tid == 0) {
+                if (pr.cutoff_out) *pr.cutoff_out = cutoff;
+                if (pr.iters_out) *pr.iters_out = iters;
+                if (pr.count_out) *pr.count_out = S;
+                if (pr.sel_total) *pr.sel_total = S;
+            }
+            cluster.sync();  // peers are done reading my counts
+            return;
         }
-        cluster.sync();  // compact list complete; peers done reading my_count
+        if (tile == 0 && g == 0 && tid == 0) {
+            if (split == 0 && pr.cutoff_out) *pr.cutoff_out = cutoff;
+            if (split == 0 && pr.iters_out) *pr.iters_out = iters;
+            if (K == 1 && pr.count_out) *pr.count_out = S;
+            if (K > 1) pr.split_sel[split] = S;
+        }
         stamp(dbg, 3);
-        if (batch.mode == kModeSelectOnly) return;
     } else {
-        S = __ldcg(pr.sel_total);
+        const int total = __ldcg(pr.sel_total);
+        list_lo = (int)(((long long)total * split) / K);
+        S = (int)(((long long)total * (split + 1)) / K) - list_lo;
     }
 
-    // ---- phase 3: accumulate positions [a, b) of the selection
+    // ---- phase 3: accumulate rows [a, b) of the cluster's numbering
     const int a = (int)(((long long)S * g) / G);
     const int b = (int)(((long long)S * (g + 1)) / G);
     const int log2L = pr.log2L;
@@ -168,7 +192,6 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     const uint16_t* __restrict__ wbase = pr.buckets + (col_ok ? c0 : 0);
     const int cols = pr.cols;
     const int32_t bucket_row0 = (int32_t)pr.bucket_row0;
-    const int32_t* __restrict__ list = pr.list;
 
     float* my_acc = acc + (size_t)warp * 16 * VEC * 32 + lane;
 #pragma unroll 4
@@ -180,7 +203,15 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
         for (int k = 0; k < SPT; ++k) {
             const int j = tid + k * NT;
             if (j < n) {
-                const int32_t row = __ldcg(list + p0 + j);
+                const int p = p0 + j;
+                int32_t row;
+                if (from_list) {
+                    row = __ldcg(pr.list + list_lo + p);
+                } else {
+                    int gs = 0;
+                    while (gs + 1 < G && p >= hdr.pre[gs + 1]) ++gs;
+                    row = hdr.row_base[gs] + (int32_t)cluster.map_shared_rank(rows16, gs)[p - hdr.pre[gs]];
+                }
                 rr[k] = row;
                 xx[k] = xp((int)((row - row0) >> 4));
             }
@@ -190,8 +221,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
 #pragma unroll
         for (int k = 0; k < SPT; ++k) {
             const int j = tid + k * NT;
-            if (j < n)
-                st[j] = make_uint2((uint32_t)(rr[k] - bucket_row0) * (uint32_t)cols, __float_as_uint(xx[k]));
+            if (j < n) st[j] = make_uint2((uint32_t)(rr[k] - bucket_row0) * (uint32_t)cols, __float_as_uint(xx[k]));
         }
     };
 
@@ -249,7 +279,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     }
     stamp(dbg, 4);
 
-    // ---- phase 4: lane accumulators -> CTA partial tile -> cluster sum
+    // ---- phase 4: lane accumulators -> CTA partial tile -> cluster sum -> splits
     for (int sk = warp; sk < 16 * VEC; sk += NW) {
         float v = 0.0f;
 #pragma unroll
@@ -272,18 +302,50 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
         gathered[k] = cluster.map_shared_rank(part, r)[o0 + oo];
     }
     __syncthreads();
+    const size_t tile_out = (size_t)tile * TW * 16;
+    const size_t split_stride = (size_t)16 * cols;
     for (int oo = tid; oo < n_own; oo += NT) {
         float s = 0.0f;
         for (int r = 0; r < G; ++r) s += gathered[oo * G + r];  // fixed order: deterministic
         const int o = o0 + oo;
-        const int col = tile * TW + o / 16;
-        if (col < cols) {
-            const size_t j = (size_t)tile * TW * 16 + o;  // = col*16 + slot
-            if (pr.residual) s = pr.residual[j] + s;      // add32 (bucketMul.cl:517-520)
-            pr.out[j] = s;
+        if (tile * TW + o / 16 < cols) {
+            const size_t j = tile_out + o;  // = col*16 + slot
+            if (K == 1) {
+                if (pr.residual) s = pr.residual[j] + s;  // add32 (bucketMul.cl:517-520)
+                pr.out[j] = s;
+            } else {
+                pr.partials[(size_t)split * split_stride + j] = s;
+            }
         }
     }
-    cluster.sync();  // keep `part` alive until every peer has read it
+    if (K > 1) {  // last cluster to finish this slice adds the splits in order
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) hdr.last_flag = (atomicAdd(pr.slice_ctr + tile * G + g, 1) == K - 1);
+        __syncthreads();
+        if (hdr.last_flag) {
+            __threadfence();
+            for (int oo = tid; oo < n_own; oo += NT) {
+                const int o = o0 + oo;
+                if (tile * TW + o / 16 < cols) {
+                    const size_t j = tile_out + o;
+                    float s = 0.0f;
+                    for (int k = 0; k < K; ++k) s += __ldcg(pr.partials + (size_t)k * split_stride + j);
+                    if (pr.residual) s = pr.residual[j] + s;
+                    pr.out[j] = s;
+                }
+            }
+            if (tid == 0) {
+                pr.slice_ctr[tile * G + g] = 0;  // ready for the next launch
+                if (tile == 0 && g == 0 && pr.count_out) {
+                    int t = 0;
+                    for (int k = 0; k < K; ++k) t += __ldcg(pr.split_sel + k);
+                    *pr.count_out = t;
+                }
+            }
+        }
+    }
+    cluster.sync();  // peers are done reading `part` and my row list
     stamp(dbg, 6);
 }
 
@@ -390,7 +452,7 @@ int seg_inputs_max(const BMBatch& b) {
 }  // namespace
 
 int bm_max_active_clusters(int vec, int G) {
-    // occupancy with the fixed part of shared memory plus 8 KB of masks (4096 inputs)
+    // occupancy with the fixed part of shared memory plus lists for 256 inputs per CTA
     static std::mutex mu;
     static std::map<std::pair<int, int>, int> cache;
     int dev = 0;
@@ -399,7 +461,7 @@ int bm_max_active_clusters(int vec, int G) {
     const auto key = std::make_pair(vec * 64 + G, dev);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
-    const size_t smem = bm_smem_bytes(vec, 4096);
+    const size_t smem = bm_smem_bytes(vec, 256);
     const int n = vec == 8 ? occupancy_clusters<8>(G, smem) : vec == 4 ? occupancy_clusters<4>(G, smem)
                                                                        : occupancy_clusters<1>(G, smem);
     cache[key] = n;
@@ -407,58 +469,61 @@ int bm_max_active_clusters(int vec, int G) {
 }
 
 int bm_default_cluster() {
-    const int g = env_int("IAM_BM_CLUSTER", 8);
-    return (g == 1 || g == 2 || g == 4 || g == 8 || g == 16) ? g : 8;
+    const int g = env_int("IAM_BM_CLUSTER", 4);
+    return (g == 1 || g == 2 || g == 4 || g == 8 || g == 16) ? g : 4;
 }
 
-// Column tiling: start every problem at the widest tile (32 lanes x VEC columns) and keep
-// halving the tile of the problem with the most work per cluster while the batch still
-// fits in one wave of resident clusters and the row segment stays >= 32 bytes.
-void bm_plan_tiles(BMBatch& b, int vec, int G, int max_clusters) {
-    (void)G;
-    const int forced = env_int("IAM_BM_LOG2L", -1);
-    int l2[kMaxProblems];
-    for (int i = 0; i < b.nprob; ++i) l2[i] = (forced >= 0 && forced <= 5) ? forced : 5;
-    auto tiles = [&](int i, int l) { return (b.p[i].cols + (vec << l) - 1) / (vec << l); };
-    if (forced < 0) {
-        for (;;) {
-            int total = 0;
-            for (int i = 0; i < b.nprob; ++i) total += tiles(i, l2[i]);
-            int best = -1;
-            double best_work = 0.0;
-            for (int i = 0; i < b.nprob; ++i) {
-                if (l2[i] == 0 || (vec << (l2[i] - 1)) < 16) continue;     // keep >= 32 B per row
-                if (tiles(i, l2[i] - 1) == tiles(i, l2[i])) continue;        // no gain
-                const int extra = tiles(i, l2[i] - 1) - tiles(i, l2[i]);
-                if (total + extra > max_clusters) continue;
-                const double work = (double)b.p[i].n_rows_valid * std::min(b.p[i].cols, vec << l2[i]);
-                if (work > best_work) {
-                    best_work = work;
-                    best = i;
-                }
-            }
-            if (best < 0) break;
-            --l2[best];
-        }
-    }
+// Launch plan: every problem gets the widest column tiles its row width allows (32 lanes x
+// VEC columns, i.e. 256 or 512 B of each row per tile), then as many input splits as its
+// share of the resident clusters (by selected-row work) allows, so the batch is one full
+// wave; splits are raised further if a CTA's input segment would not fit shared memory.
+void bm_plan(BMBatch& b, int vec, int G, int max_clusters) {
+    const int forced_l2 = env_int("IAM_BM_LOG2L", -1);
+    const int forced_k = env_int("IAM_BM_SPLIT", -1);
+    double work_total = 0.0;
+    for (int i = 0; i < b.nprob; ++i) work_total += (double)b.p[i].cols * b.p[i].n_rows_valid;
     int begin = 0;
     for (int i = 0; i < b.nprob; ++i) {
         BMProblem& p = b.p[i];
-        p.log2L = l2[i];
-        p.n_tiles = tiles(i, l2[i]);
+        int l2 = 0;
+        while (l2 < 5 && (vec << l2) < p.cols) ++l2;
+        if (forced_l2 >= 0 && forced_l2 <= 5) l2 = forced_l2;
+        p.log2L = l2;
+        p.n_tiles = (p.cols + (vec << l2) - 1) / (vec << l2);
+        const int inputs = std::max(1, p.n_inputs - p.in_begin);
+        int K = 1;
+        if (b.mode != kModeSelectOnly) {
+            const double share = work_total > 0 ? max_clusters * ((double)p.cols * p.n_rows_valid) / work_total
+                                                : (double)max_clusters;
+            K = std::max(1, (int)(share / p.n_tiles));
+            if (forced_k > 0) K = forced_k;
+            K = std::min(K, std::max(1, inputs / G));  // at least one input per CTA
+            K = std::min(K, kMaxSplits);
+        }
+        int seg;
+        for (;;) {
+            const int span = (inputs + K - 1) / K;
+            seg = (span + G - 1) / G;
+            if ((seg <= kMaxSegInputs && bm_smem_bytes(vec, seg) <= 227 * 1024) || K >= kMaxSplits) break;
+            ++K;
+        }
+        p.n_split = K;
+        p.seg_inputs = std::max(1, seg);
         p.cluster_begin = begin;
-        begin += p.n_tiles;
+        begin += p.n_tiles * K;
     }
 }
 
 int bm_total_clusters(const BMBatch& b) {
     int n = 0;
-    for (int i = 0; i < b.nprob; ++i) n += b.p[i].n_tiles;
+    for (int i = 0; i < b.nprob; ++i) n += b.p[i].n_tiles * b.p[i].n_split;
     return n;
 }
 
 int bm_launch(const BMBatch& b, int vec, int G, cudaStream_t s) {
     const int n = b.mode == kModeSelectOnly ? b.nprob : bm_total_clusters(b);
+    if (seg_inputs_max(b) > kMaxSegInputs)
+        return fail(IAM_ERR_UNSUPPORTED, "bucketmul: more than 4096 inputs per CTA segment");
     const size_t smem = bm_smem_bytes(vec, seg_inputs_max(b));
     if (smem > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "bucketmul: segment too large for shared memory");
     if (vec == 8) return launch_vec<8>(b, G, n, smem, s);

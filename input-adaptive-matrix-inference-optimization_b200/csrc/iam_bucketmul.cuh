@@ -20,87 +20,133 @@ struct CutoffShared {
     float mn[NT / 32];
     float mx[NT / 32];
     int cnt[2][NT / 32];
+    float result;
+    int steps;
 };
+
+// fp32 (a + b) / 2 exactly as the reference computes its mids (bucketMul.cl:139, :190).
+IAM_DEV float bisect_mid(float a, float b) { return __fmul_rn(__fadd_rn(a, b), 0.5f); }
 
 // Block-wide restatement of findCutoffBinarySearch (bucketMul.cl:68-214).  All threads of
 // the block must call it; all receive the same cutoff.  The counts are exact integers and
 // min/max are order independent, so any thread layout reproduces the reference's result
 // bit for bit.  `target` = P - quantile (bucketMul.cl:81, bucket_mul.hpp:164).
-template <int NT, class XP>
-__device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ probes, int P,
-                                   int target, CutoffShared<NT>& sm, int* iters_out) {
-    constexpr int NW = NT / 32;
-    constexpr int VPT = (kProbes + NT - 1) / NT;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+//
+// NWC warps (one per SM sub-partition by default) hold the 4096 importance values in
+// registers and run the bisection among themselves behind a named barrier: a step costs a
+// handful of compares per lane plus one 32*NWC-thread barrier instead of a full-block one.
+IAM_DEV void debug_stamp(long long* dbg, int k) {
+    if (dbg) {
+        long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        dbg[k] = t;
+    }
+}
 
-    float v[VPT];
-    float mn = INFINITY, mx = -INFINITY;
+template <int NT, int NWC = 4, class XP>
+__device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ probes, int P,
+                                   int target, CutoffShared<NT>& sm, int* iters_out,
+                                   long long* dbg = nullptr) {
+    static_assert(NWC * 32 <= NT, "cutoff warps exceed the block");
+    constexpr int NCT = NWC * 32;
+    constexpr int VPT = (kProbes + NCT - 1) / NCT;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (warp < NWC) {
+        float v[VPT];
+        unsigned mnb = 0x7f800000u, mxb = 0u;  // imp >= 0: float order == bit order
+        // lane t of the NWC warps owns values [t*VPT, t*VPT + VPT): vector loads when the
+        // full 4096 are in use and both arrays are 16-byte aligned
+        const int i_base = tid * VPT;
+        if (XP::kVectorizable && P == kProbes && VPT % 8 == 0 && xp.aligned16() &&
+            ((reinterpret_cast<uintptr_t>(probes) & 15u) == 0)) {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int i = tid + k * NT;
-        if (i < P) {
-            const float imp = importance(xp(i), h2f(__ldg(probes + i)));
-            v[k] = imp;
-            mn = fminf(mn, imp);
-            mx = fmaxf(mx, imp);
+            for (int k = 0; k < VPT; k += 8) {
+                const uint4 pb = __ldg(reinterpret_cast<const uint4*>(probes + i_base + k));
+                float xv[8];
+                xp.load8(i_base + k, xv);
+                const uint32_t pw[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t hb = (e & 1) ? (pw[e >> 1] >> 16) : (pw[e >> 1] & 0xffffu);
+                    v[k + e] = importance(xv[e], h2f(hb));
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                mnb = min(mnb, __float_as_uint(v[k]));
+                mxb = max(mxb, __float_as_uint(v[k]));
+            }
         } else {
-            v[k] = -1.0f;  // never counted: every tested mid is >= 0
-        }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    }
-    if (lane == 0) {
-        sm.mn[warp] = mn;
-        sm.mx[warp] = mx;
+            for (int k = 0; k < VPT; ++k) {
+                const int i = i_base + k;
+                if (i < P) {
+                    v[k] = importance(xp(i), h2f(__ldg(probes + i)));
+                    mnb = min(mnb, __float_as_uint(v[k]));
+                    mxb = max(mxb, __float_as_uint(v[k]));
+                } else {
+                    v[k] = -1.0f;  // never counted: every tested mid is >= 0
+                }
+            }
+        }
+        mnb = __reduce_min_sync(0xffffffffu, mnb);
+        mxb = __reduce_max_sync(0xffffffffu, mxb);
+        if (lane == 0) {
+            sm.mn[warp] = __uint_as_float(mnb);
+            sm.mx[warp] = __uint_as_float(mxb);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NCT));
+        debug_stamp(dbg, 0);
+        float mn = sm.mn[0], mx = sm.mx[0];
+#pragma unroll
+        for (int w = 1; w < NWC; ++w) {
+            mn = fminf(mn, sm.mn[w]);
+            mx = fmaxf(mx, sm.mx[w]);
+        }
+        float lo = mn, hi = mx;
+        float mid = bisect_mid(lo, hi);    // (min+max)/2.0f, :139
+        int min_count = P, max_count = 0;  // :142-143
+        int it = 0;
+        float result;
+        for (;;) {
+            int c4[4] = {0, 0, 0, 0};  // four short chains instead of one VPT-long chain
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) c4[k & 3] += (v[k] > mid) ? 1 : 0;  // ">" (:155)
+            int c = __reduce_add_sync(0xffffffffu, (c4[0] + c4[1]) + (c4[2] + c4[3]));
+            if (lane == 0) sm.cnt[it & 1][warp] = c;
+            asm volatile("bar.sync 1, %0;" ::"n"(NCT));
+            int cnt = 0;
+#pragma unroll
+            for (int w = 0; w < NWC; ++w) cnt += sm.cnt[it & 1][w];
+            if (cnt < target) {
+                hi = mid;
+                max_count = cnt;
+            } else {
+                lo = mid;
+                min_count = cnt;
+            }
+            const float next = bisect_mid(lo, hi);
+            ++it;
+            if (cnt == target || __fsub_rn(hi, lo) < 1e-5f || abs(max_count - min_count) < 3) {
+                result = mid;  // the mid that was tested (:198)
+                break;
+            }
+            mid = next;
+            if (it == kMaxIters) {
+                result = mid;  // bounds[2] after the last update (:211-213)
+                break;
+            }
+        }
+        if (tid == 0) {
+            sm.result = result;
+            sm.steps = it;
+        }
+        debug_stamp(dbg, 1);
     }
     __syncthreads();
-    mn = sm.mn[0];
-    mx = sm.mx[0];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) {
-        mn = fminf(mn, sm.mn[w]);
-        mx = fmaxf(mx, sm.mx[w]);
-    }
-
-    float lo = mn, hi = mx;
-    float mid = __fmul_rn(__fadd_rn(lo, hi), 0.5f);  // (min+max)/2.0f, :139
-    int min_count = P, max_count = 0;                // :142-143
-    int it = 0;
-    float result;
-    for (;;) {
-        int c = 0;
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) c += (v[k] > mid) ? 1 : 0;  // ">" (:155)
-        c = __reduce_add_sync(0xffffffffu, c);
-        if (lane == 0) sm.cnt[it & 1][warp] = c;
-        __syncthreads();
-        int cnt = 0;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) cnt += sm.cnt[it & 1][w];
-        if (cnt < target) {
-            hi = mid;
-            max_count = cnt;
-        } else {
-            lo = mid;
-            min_count = cnt;
-        }
-        const float next = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
-        ++it;
-        if (cnt == target || __fsub_rn(hi, lo) < 1e-5f || abs(max_count - min_count) < 3) {
-            result = mid;  // the mid that was tested (:198)
-            break;
-        }
-        mid = next;
-        if (it == kMaxIters) {
-            result = mid;  // bounds[2] after the last update (:211-213)
-            break;
-        }
-    }
-    __syncthreads();  // sm.cnt may be reused by the caller
-    if (iters_out) *iters_out = it;
+    const float result = sm.result;
+    if (iters_out) *iters_out = sm.steps;
+    __syncthreads();  // the shared state may be reused by the caller
     return result;
 }
 
@@ -109,30 +155,70 @@ __device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ pr
 // prologue: every CTA evaluates the same function of the same bits, so all CTAs see
 // bit-identical x and therefore compute the same cutoff and selection.
 
+// Every provider also offers load8 (8 consecutive values, 16-byte aligned) for the cutoff's
+// vector loads; kVectorizable says whether that path is worth taking.
 // x = a plain fp32 vector.
 struct XPlain {
+    static constexpr bool kVectorizable = true;
     const float* x;
     IAM_DEV float operator()(int i) const { return __ldg(x + i); }
+    IAM_DEV bool aligned16() const { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; }
+    IAM_DEV void load8(int i, float* o) const {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x + i));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(x + i + 4));
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    }
 };
 
 // x = rmsNorm32fast(src) * gain (aux.cl:156-196 then mul16x32 aux.cl:434-440): the scale is
 // computed once per CTA by block_rms_scale.
 struct XRms {
+    static constexpr bool kVectorizable = true;
     const float* src;
     const uint16_t* gain;
     float scale;
     IAM_DEV float operator()(int i) const {
         return __fmul_rn(h2f(__ldg(gain + i)), __fmul_rn(__ldg(src + i), scale));
     }
+    IAM_DEV bool aligned16() const {
+        return ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(gain)) & 15u) == 0;
+    }
+    IAM_DEV void load8(int i, float* o) const {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src + i));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src + i + 4));
+        const uint4 gb = __ldg(reinterpret_cast<const uint4*>(gain + i));
+        const float s8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const uint32_t gw[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t hb = (e & 1) ? (gw[e >> 1] >> 16) : (gw[e >> 1] & 0xffffu);
+            o[e] = __fmul_rn(h2f(hb), __fmul_rn(s8[e], scale));
+        }
+    }
 };
 
 // x = silu32(gate, up) = up * gate / (1 + exp(-gate)) (matrix.cl:27-32).
 struct XSilu {
+    static constexpr bool kVectorizable = true;
     const float* gate;
     const float* up;
     IAM_DEV float operator()(int i) const {
         const float gv = __ldg(gate + i), uv = __ldg(up + i);
         return __fdiv_rn(__fmul_rn(uv, gv), __fadd_rn(1.0f, expf(-gv)));
+    }
+    IAM_DEV bool aligned16() const {
+        return ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up)) & 15u) == 0;
+    }
+    IAM_DEV void load8(int i, float* o) const {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + i));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + i + 4));
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(up + i));
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(up + i + 4));
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __fdiv_rn(__fmul_rn(uv[e], gv[e]), __fadd_rn(1.0f, expf(-gv[e])));
     }
 };
 
@@ -257,6 +343,46 @@ __device__ void block_write_rows(const uint16_t* __restrict__ masks, long long r
             const int r = __ffs(mask) - 1;
             mask &= mask - 1u;
             rows_out[p++] = rbase + r;
+        }
+        base += total;
+    }
+    __syncthreads();
+}
+
+// Writes the selected rows of inputs [i0, i1) as 16-bit offsets from row 16*i0 (ascending)
+// into a shared-memory list (peers of the cluster read it through DSMEM).
+template <int NT>
+__device__ void block_write_rows_local(const uint16_t* __restrict__ masks, int i0, int i1,
+                                       uint16_t* __restrict__ rows_out, ScanShared<NT>& sm) {
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int base = 0, round = 0;
+    for (int ib = i0; ib < i1; ib += NT, ++round) {
+        const int i = ib + tid;
+        unsigned mask = (i < i1) ? masks[i - i0] : 0u;
+        const int n = __popc(mask);
+        int inc = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+        }
+        const int par = round & 1;
+        if (lane == 31) sm.tot[par][warp] = inc;
+        __syncthreads();
+        int pre = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const int t = sm.tot[par][w];
+            pre += (w < warp) ? t : 0;
+            total += t;
+        }
+        int p = base + pre + inc - n;
+        const int rbase = (i - i0) * 16;
+        while (mask) {
+            const int r = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            rows_out[p++] = (uint16_t)(rbase + r);
         }
         base += total;
     }

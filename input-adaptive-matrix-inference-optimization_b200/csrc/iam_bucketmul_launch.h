@@ -8,6 +8,8 @@ namespace iam {
 
 constexpr int kMaxProblems = 4;
 constexpr int kMaxCluster = 16;
+constexpr int kMaxSplits = 64;
+constexpr int kMaxSegInputs = 4096;  // 16-bit local row offsets
 
 enum BMMode { kModeFused = 0, kModeSelectOnly = 1, kModeMulOnly = 2 };
 
@@ -19,8 +21,14 @@ enum BMXMode {
 };
 
 // One bucketMul (one weight matrix times one input vector).
+//
+// Grid layout of a problem: n_tiles column tiles x n_split row splits clusters of G CTAs.
+// Fused mode splits the inputs [in_begin, n_inputs) into n_split ranges; mul-only mode
+// splits the positions of the compact dispatch list.  With n_split > 1 every cluster
+// writes its partial tile to `partials` and the last cluster to finish a slice of the tile
+// (slice_ctr) adds the n_split partials in split order, so results stay deterministic.
 struct BMProblem {
-    const uint16_t* buckets;  // [R_total][cols]; rows are absolute indices (may be a virtual base)
+    const uint16_t* buckets;  // [R_total][cols]; rows are absolute indices minus bucket_row0
     const uint16_t* stats;    // [R_total][stats_stride]
     const uint16_t* probes;   // already offset by expert_no * 4096
     const float* x;           // input (plain), RMS source (kXRms) or gate (kXSilu)
@@ -30,8 +38,11 @@ struct BMProblem {
     int norm_n;               // kXRms: length of the normalised vector
     float* out;               // [16 * cols]
     const float* residual;    // optional: out = residual + result (add32, bucketMul.cl:517-520)
-    int32_t* list;            // compact dispatch list scratch (>= n_rows_valid rows)
+    int32_t* list;            // compact dispatch list (select-only writes, mul-only reads)
     int* sel_total;           // selected-row total (select-only writes, mul-only reads)
+    float* partials;          // [n_split][16 * cols] when n_split > 1
+    int* slice_ctr;           // [n_tiles * G] zero-initialised arrival counters (self-resetting)
+    int* split_sel;           // [n_split] selected rows per split (count_out when n_split > 1)
     float* cutoff_out;        // optional
     int* count_out;           // optional
     int* iters_out;           // optional
@@ -45,9 +56,10 @@ struct BMProblem {
     int stats_stride;         // 4 (file layout) or 1 (packed channel 3)
     int P;                    // probes used by the cutoff: min(in_dim, 4096)
     int target;               // P - quantile
-    int seg_inputs;           // inputs per CTA segment of the cluster
+    int seg_inputs;           // inputs per CTA (fused: per CTA of a split)
     int log2L;                // lanes per row segment = 1 << log2L
-    int n_tiles;              // column tiles (clusters) of this problem
+    int n_tiles;              // column tiles of this problem
+    int n_split;              // row splits (clusters per tile)
     int cluster_begin;        // index of its first cluster in the launch
 };
 
@@ -58,10 +70,19 @@ struct BMBatch {
     int xmode;
 };
 
+// Scratch a problem needs beyond its inputs and outputs (device memory the caller owns).
+struct BMScratch {
+    int32_t* list;     // >= n_rows_valid rows (select-only / mul-only modes)
+    int* sel_total;    // 1 int
+    float* partials;   // >= kMaxSplits * 16 * cols floats
+    int* slice_ctr;    // >= n_tiles * G ints, zero-initialised once
+    int* split_sel;    // >= kMaxSplits ints
+};
+
 int bm_default_cluster();
 int bm_max_active_clusters(int vec, int G);
 size_t bm_smem_bytes(int vec, int seg_inputs);
-void bm_plan_tiles(BMBatch& b, int vec, int G, int max_clusters);
+void bm_plan(BMBatch& b, int vec, int G, int max_clusters);
 int bm_total_clusters(const BMBatch& b);
 int bm_launch(const BMBatch& b, int vec, int G, cudaStream_t s);
 int bm_launch_cutoff(const float* x, const uint16_t* probes, int P, int target, float* out, int* iters,

@@ -32,8 +32,11 @@ struct iam_bucketmul_s {
     int device = 0;
     int32_t* list = nullptr;  // compact dispatch list scratch
     size_t list_cap = 0;      // capacity in rows
-    float* cutoff = nullptr;  // device scalar
-    int* ints = nullptr;      // device scalars: [0] count, [1] iters, [2] selected total
+    float* partials = nullptr;  // split partial tiles
+    size_t partials_cap = 0;    // capacity in floats
+    int* ctr = nullptr;         // slice arrival counters (zeroed once, self-resetting)
+    float* cutoff = nullptr;    // device scalar
+    int* ints = nullptr;        // device scalars: [0] count, [1] iters, [2] selected total, [8..] split counts
     // dispatch recorded by iam_bucketmul_calc_dispatch (consumed by iam_bucketmul_mul)
     bool have_dispatch = false;
     BMProblem disp{};
@@ -86,8 +89,28 @@ int fill_problem(iam_bucketmul_s* h, BMProblem& p, int G, const float* x, const 
     if (rc) return rc;
     p.list = h->list;
     p.sel_total = h->ints + 2;
+    p.split_sel = h->ints + 8;
+    p.slice_ctr = h->ctr;
     p.dbg = h->dbg;
+    const size_t need = (size_t)kMaxSplits * 16 * (size_t)bucket_cols;
+    if (need > h->partials_cap) {
+        if (h->partials) IAM_CUDA_TRY(cudaFree(h->partials));
+        h->partials = nullptr;
+        h->partials_cap = 0;
+        IAM_CUDA_TRY(cudaMalloc(&h->partials, need * sizeof(float)));
+        h->partials_cap = need;
+    }
+    p.partials = h->partials;
     return IAM_OK;
+}
+
+constexpr int kCtrSlots = 4096;
+
+// The slice counters must cover n_tiles * G of the problem.
+bool plan_fits(const BMBatch& b, int G) {
+    for (int i = 0; i < b.nprob; ++i)
+        if (b.p[i].n_tiles * G > kCtrSlots) return false;
+    return true;
 }
 
 // Widest vector load every problem of the batch supports (IAM_BM_VEC may lower it).
@@ -122,7 +145,7 @@ int iam_device_info(int device, int* sm_count, int* cc_major, int* cc_minor) {
 }
 
 int iam_bucketmul_plan_info(int vec, int cluster_size, int bucket_cols, int in_dim, int* max_active_clusters,
-                            int* log2_lanes, int* n_tiles) {
+                            int* log2_lanes, int* n_tiles, int* n_splits) {
     if ((vec != 8 && vec != 4 && vec != 1) || cluster_size < 1 || cluster_size > kMaxCluster || bucket_cols <= 0 || in_dim <= 0)
         return fail(IAM_ERR_ARG, "iam_bucketmul_plan_info: bad arguments");
     const int mac = bm_max_active_clusters(vec, cluster_size);
@@ -131,10 +154,13 @@ int iam_bucketmul_plan_info(int vec, int cluster_size, int bucket_cols, int in_d
     b.nprob = 1;
     b.p[0].cols = bucket_cols;
     b.p[0].n_rows_valid = 16 * in_dim;
-    bm_plan_tiles(b, vec, cluster_size, mac);
+    b.p[0].n_inputs = in_dim;
+    b.mode = kModeFused;
+    bm_plan(b, vec, cluster_size, mac);
     if (max_active_clusters) *max_active_clusters = mac;
     if (log2_lanes) *log2_lanes = b.p[0].log2L;
     if (n_tiles) *n_tiles = b.p[0].n_tiles;
+    if (n_splits) *n_splits = b.p[0].n_split;
     return IAM_OK;
 }
 
@@ -147,7 +173,9 @@ int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
     iam_bucketmul_s* h = new iam_bucketmul_s();
     h->device = device;
     cudaError_t e = cudaMalloc(&h->cutoff, sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * (8 + kMaxSplits));
+    if (e == cudaSuccess) e = cudaMalloc(&h->ctr, sizeof(int) * kCtrSlots);
+    if (e == cudaSuccess) e = cudaMemset(h->ctr, 0, sizeof(int) * kCtrSlots);
     if (e != cudaSuccess) {
         iam_bucketmul_destroy(h);
         return cuda_fail(e, "iam_bucketmul_create: cudaMalloc");
@@ -159,6 +187,8 @@ int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
 int iam_bucketmul_destroy(iam_bucketmul_t h) {
     if (!h) return IAM_OK;
     cudaFree(h->list);
+    cudaFree(h->partials);
+    cudaFree(h->ctr);
     cudaFree(h->cutoff);
     cudaFree(h->ints);
     delete h;
@@ -189,9 +219,9 @@ int iam_bucketmul_calc_dispatch(iam_bucketmul_t h, const float* x_dev, const uin
     b.p[0].cutoff_out = h->cutoff;
     b.p[0].count_out = h->ints;
     b.p[0].iters_out = h->ints + 1;
-    b.p[0].n_tiles = 1;
     b.nprob = 1;
     b.mode = kModeSelectOnly;
+    bm_plan(b, 1, G, 1);
     rc = bm_launch(b, 1, G, (cudaStream_t)stream);
     if (rc) return rc;
     h->disp = b.p[0];
@@ -233,7 +263,8 @@ int iam_bucketmul_mul(iam_bucketmul_t h, const uint16_t* buckets_dev, int bucket
     b.mode = kModeMulOnly;
     const int G = h->disp_G;
     const int vec = pick_vec(b);
-    bm_plan_tiles(b, vec, G, bm_max_active_clusters(vec, G));
+    bm_plan(b, vec, G, bm_max_active_clusters(vec, G));
+    if (!plan_fits(b, G)) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_mul: plan exceeds scratch");
     return bm_launch(b, vec, G, (cudaStream_t)stream);
 }
 
@@ -256,7 +287,8 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
     b.nprob = 1;
     b.mode = kModeFused;
     const int vec = pick_vec(b);
-    bm_plan_tiles(b, vec, G, bm_max_active_clusters(vec, G));
+    bm_plan(b, vec, G, bm_max_active_clusters(vec, G));
+    if (!plan_fits(b, G)) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full: plan exceeds scratch");
     return bm_launch(b, vec, G, (cudaStream_t)stream);
 }
 
