@@ -121,6 +121,67 @@ int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_
 int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buckets_dev,
                   uint16_t* stats4_dev, uint16_t* stats1_dev, uint16_t* probes_dev, void* stream);
 
+/* ------------------------------------------------------------------ decode model */
+/* Replaces MistralModel (model.hpp:84-237), TransformerLayer (transformer_layer.hpp:55-162),
+ * Attention (attention.hpp:71-404) and FeedForward (feedforward.hpp:89-183).  The model
+ * owns its weights (bucket layout with packed stats), an fp16 GQA KV cache
+ * [layer][kv_head][max_ctx][head_dim] (the reference's is fp32 and repeated per query head,
+ * model.hpp:97-98), activations and scratch.  Vocabulary, dims, RoPE theta and RMSNorm eps
+ * are parameters (the reference hard-codes them, model.hpp:25-30, attention.hpp:21-27). */
+typedef struct {
+    int dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_ctx;
+    float norm_eps;         /* 1e-5 in aux.cl:190 */
+    double rope_theta;      /* 1e6 in attention.hpp:27 */
+    int tied_embeddings;    /* LM head = embedding matrix (else a separate lm_head) */
+} iam_model_config;
+
+typedef struct iam_model_s* iam_model_t;
+
+/* Random-init model on `device`: every weight matrix i.i.d. N(0, 0.02) fp16 (a counter-based
+ * generator seeded by `seed`), bucketized on the GPU; RMSNorm gains 1.0; embeddings N(0, 0.02). */
+int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed,
+                            int device);
+/* Loads a model directory in the reference's file layout (MistralModel ctor, model.hpp:84-127):
+ * embed_tokens.npy, norm_weight.npy, [lm_head.npy], layer{L}_input_layernorm.npy,
+ * layer{L}_post_attention_layernorm.npy and layer{L}_{q,k,v,o,gate,up,down}_proj_bucketmul_fp16_
+ * {meta.txt,buckets.bin,stats.bin,probes.bin} (preprocess_layer_fixed_gpu.py:245-333), with the
+ * loader's validation (binary_loader.hpp:96-123): IAM_ERR_IO on missing or mis-sized files. */
+int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device);
+int iam_model_destroy(iam_model_t m);
+/* MistralModel::reset_caches (model.hpp:233-237): zero the KV cache and the position. */
+int iam_model_reset(iam_model_t m, void* stream);
+/* MistralModel::forward (model.hpp:152-231): one decode step of `token` at `pos`; logits_dev
+ * (vocab floats, may be NULL) receives the logits. */
+int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* logits_dev, void* stream);
+/* Greedy generation on the device (the decode loop of test_generation.cpp:239-291 without
+ * host round trips): step 0 decodes first_token at start_pos, every later step decodes the
+ * previous step's argmax; the n_tokens generated ids land in tokens_dev.  Steps after the
+ * first replay one captured CUDA graph. */
+int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort,
+                       int* tokens_dev, void* stream);
+/* KV cache contents of one layer: k/v [n_kv_heads][n_tokens][head_dim] fp16 (post-RoPE k). */
+int iam_model_set_kv(iam_model_t m, int layer, const uint16_t* k_dev, const uint16_t* v_dev,
+                     int n_tokens, void* stream);
+/* Fills positions [0, n_tokens) of every layer's K and V cache with N(0,1) fp16. */
+int iam_model_fill_kv_random(iam_model_t m, int n_tokens, unsigned long long seed, void* stream);
+
+enum {
+    IAM_W_EMBED = 0, IAM_W_FINAL_NORM = 1, IAM_W_LM_HEAD = 2, IAM_W_ATTN_NORM = 3, IAM_W_FFN_NORM = 4,
+    IAM_W_K_CACHE = 5, IAM_W_V_CACHE = 6, /* one layer: [n_kv_heads][max_ctx][head_dim] fp16 */
+    /* IAM_W_MATRIX + 3*m + part: m in q,k,v,o,gate,up,down; part 0 buckets [16*in][cols],
+     * 1 packed stats [16*in] (channel 3), 2 probes [in] */
+    IAM_W_MATRIX = 16
+};
+/* Copies one weight tensor to host memory; *bytes_out receives its size (host_dst may be
+ * NULL to query it). */
+int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, size_t capacity_bytes,
+                          size_t* bytes_out);
+/* Selected bucket rows summed over the 7*n_layers bucketMuls of the last step. */
+int iam_model_selected_rows(iam_model_t m, long long* total);
+/* Algorithmic bytes of the last step at KV length `context`: per bucketMul
+ * 2|S|C + 2R + 4N + 2*min(N,4096) + 4M, plus K/V reads and the dense LM head. */
+int iam_model_step_bytes(iam_model_t m, int context, long long* bytes);
+
 #ifdef __cplusplus
 }
 #endif

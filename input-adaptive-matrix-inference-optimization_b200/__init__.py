@@ -160,3 +160,131 @@ def bucketize(w, buckets, stats4=None, stats1=None, probes=None, stream=None):
     out_dim, in_dim = w.shape
     check(load_library().iam_bucketize(_ptr(w), out_dim, in_dim, _ptr(buckets), _ptr(stats4), _ptr(stats1),
                                        _ptr(probes), _stream(stream)))
+
+
+# ---------------------------------------------------------------- decode model
+
+class ModelConfig(ctypes.Structure):
+    """iam_model_config (include/iam_b200.h)."""
+    _fields_ = [("dim", _i32), ("n_layers", _i32), ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32),
+                ("ffn_dim", _i32), ("vocab", _i32), ("max_ctx", _i32), ("norm_eps", _f32),
+                ("rope_theta", ctypes.c_double), ("tied_embeddings", _i32)]
+
+    @classmethod
+    def make(cls, dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_ctx, norm_eps=1e-5,
+             rope_theta=1e6, tied_embeddings=1):
+        return cls(dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_ctx, norm_eps, rope_theta,
+                   tied_embeddings)
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+MISTRAL_7B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336, vocab=32000)
+
+W_EMBED, W_FINAL_NORM, W_LM_HEAD, W_ATTN_NORM, W_FFN_NORM, W_K_CACHE, W_V_CACHE, W_MATRIX = 0, 1, 2, 3, 4, 5, 6, 16
+MATRIX_NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+_SIGNATURES.update({
+    "iam_model_create_random": [_vp, _vp, ctypes.c_ulonglong, _i32],
+    "iam_model_load": [_vp, ctypes.c_char_p, _vp, _i32],
+    "iam_model_destroy": [_vp],
+    "iam_model_reset": [_vp, _vp],
+    "iam_model_forward": [_vp, _i32, _i32, _f32, _vp, _vp],
+    "iam_model_generate": [_vp, _i32, _i32, _i32, _f32, _vp, _vp],
+    "iam_model_set_kv": [_vp, _i32, _vp, _vp, _i32, _vp],
+    "iam_model_fill_kv_random": [_vp, _i32, ctypes.c_ulonglong, _vp],
+    "iam_model_read_weight": [_vp, _i32, _i32, _vp, ctypes.c_size_t, _vp],
+    "iam_model_selected_rows": [_vp, _vp],
+    "iam_model_step_bytes": [_vp, _i32, _vp],
+})
+
+
+class Model:
+    """Mirror of MistralModel (model.hpp:84-237) on one device."""
+
+    def __init__(self, cfg, h):
+        self.cfg, self.h, self.lib = cfg, h, load_library()
+
+    @classmethod
+    def random(cls, cfg, seed=0, device=0):
+        lib = load_library()
+        h = ctypes.c_void_p()
+        check(lib.iam_model_create_random(ctypes.byref(h), ctypes.byref(cfg), seed, device))
+        return cls(cfg, h)
+
+    @classmethod
+    def load(cls, weights_dir, cfg, device=0):
+        lib = load_library()
+        h = ctypes.c_void_p()
+        check(lib.iam_model_load(ctypes.byref(h), os.fsencode(weights_dir), ctypes.byref(cfg), device))
+        return cls(cfg, h)
+
+    def close(self):
+        if self.h:
+            self.lib.iam_model_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, stream=None):
+        check(self.lib.iam_model_reset(self.h, _stream(stream)))
+
+    def forward(self, token, pos, effort, logits=None, stream=None):
+        check(self.lib.iam_model_forward(self.h, token, pos, effort, _ptr(logits), _stream(stream)))
+
+    def generate(self, first_token, start_pos, n_tokens, effort, tokens, stream=None):
+        check(self.lib.iam_model_generate(self.h, first_token, start_pos, n_tokens, effort, _ptr(tokens),
+                                          _stream(stream)))
+
+    def set_kv(self, layer, k, v, n_tokens, stream=None):
+        check(self.lib.iam_model_set_kv(self.h, layer, _ptr(k), _ptr(v), n_tokens, _stream(stream)))
+
+    def fill_kv_random(self, n_tokens, seed=0, stream=None):
+        check(self.lib.iam_model_fill_kv_random(self.h, n_tokens, seed, _stream(stream)))
+
+    def read_weight(self, which, layer=0):
+        """-> numpy uint16 array with the weight's bits (blocking)."""
+        import numpy as np
+        n = ctypes.c_size_t()
+        check(self.lib.iam_model_read_weight(self.h, layer, which, None, 0, ctypes.byref(n)))
+        out = np.empty(n.value // 2, np.uint16)
+        check(self.lib.iam_model_read_weight(self.h, layer, which, out.ctypes.data_as(ctypes.c_void_p), n.value,
+                                             None))
+        return out
+
+    def selected_rows(self):
+        t = ctypes.c_longlong()
+        check(self.lib.iam_model_selected_rows(self.h, ctypes.byref(t)))
+        return t.value
+
+    def step_bytes(self, context):
+        t = ctypes.c_longlong()
+        check(self.lib.iam_model_step_bytes(self.h, context, ctypes.byref(t)))
+        return t.value
+
+    def export_weights(self):
+        """Host copy of every weight in the oracle's layout (tests use it as the checker's input)."""
+        import importlib
+        weights = importlib.import_module(__name__ + ".weights")
+        c = self.cfg
+        qn, kvn = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+        shapes = {"q": (qn, c.dim), "k": (kvn, c.dim), "v": (kvn, c.dim), "o": (c.dim, qn),
+                  "gate": (c.ffn_dim, c.dim), "up": (c.ffn_dim, c.dim), "down": (c.dim, c.ffn_dim)}
+        layers = []
+        for l in range(c.n_layers):
+            lw = {"attn_norm": self.read_weight(W_ATTN_NORM, l), "ffn_norm": self.read_weight(W_FFN_NORM, l)}
+            for mi, name in enumerate(MATRIX_NAMES):
+                out_dim, in_dim = shapes[name]
+                b = self.read_weight(W_MATRIX + 3 * mi, l).reshape(16 * in_dim, out_dim // 16)
+                s1 = self.read_weight(W_MATRIX + 3 * mi + 1, l)
+                p = self.read_weight(W_MATRIX + 3 * mi + 2, l)
+                lw[name] = weights.BucketWeight(b, s1.reshape(-1, 1), p, in_dim, out_dim)
+            layers.append(lw)
+        embed = self.read_weight(W_EMBED).reshape(c.vocab, c.dim)
+        lm = None if c.tied_embeddings else self.read_weight(W_LM_HEAD).reshape(c.vocab, c.dim)
+        return {"embed": embed, "final_norm": self.read_weight(W_FINAL_NORM), "lm_head": lm, "layers": layers}

@@ -1,0 +1,43 @@
+// iam_layers.h -- launch descriptions of the decode-step kernels in iam_layers.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace iam {
+
+constexpr int kAttnThreads = 128;
+constexpr int kHeadThreads = 256;
+
+struct AttnParams {
+    const float* q;        // [n_heads][head_dim] pre-RoPE (bucketMul output)
+    const float* k;        // [n_kv_heads][head_dim] pre-RoPE
+    const float* v;        // [n_kv_heads][head_dim]
+    uint16_t* k_cache;     // this layer: [n_kv_heads][max_ctx][head_dim] fp16, post-RoPE
+    uint16_t* v_cache;     // this layer: [n_kv_heads][max_ctx][head_dim] fp16
+    const float* rope;     // [max_ctx][head_dim/2][2] cos, sin
+    const int* pos_dev;    // position of the token being decoded (context = pos + 1)
+    float* out;            // [n_heads][head_dim]
+    float* part;           // scratch [n_kv_heads][n_split][gq][head_dim + 2]
+    int* ctr;              // [n_kv_heads] zero-initialised, self-resetting
+    int n_kv_heads, head_dim, max_ctx, n_split, chunk_cap;
+};
+
+struct LMHeadParams {
+    const uint16_t* W;               // [rows][dim] fp16
+    const float* x;                  // [dim] residual stream
+    const uint16_t* gain;            // [dim] final norm gain
+    float eps;
+    int dim, rows;
+    float* logits;                   // [rows] (may be null)
+    unsigned long long* argmax_key;  // greedy argmax (may be null)
+};
+
+int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long long* token_key,
+                 const int* token_dev, float* x, unsigned long long* argmax_key, int* token_used, cudaStream_t s);
+size_t attention_smem(const AttnParams& p, int gq);
+int launch_attention(const AttnParams& p, int gq, cudaStream_t s);
+int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s);
+int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s);
+
+}  // namespace iam

@@ -1,0 +1,756 @@
+// iam_model.cu -- Mistral-style decode runtime over the fused bucketMul kernels.
+//
+// Replaces MistralModel (model.hpp:84-237) + TransformerLayer (transformer_layer.hpp:75-122)
+// + Attention (attention.hpp:135-202) + FeedForward (feedforward.hpp:46-86).  One decode
+// step is 2 + 5*n_layers launches:
+//   embed -> per layer [qkv bucketMuls (RMSNorm*gain fused), attention (RoPE, fp16 KV
+//   append, split-K), o bucketMul (+residual), gate/up bucketMuls (RMSNorm*gain fused),
+//   down bucketMul (SiLU*up fused, +residual)] -> LM head (final RMSNorm*gain, argmax).
+// Position and token live in device memory, so a step can be captured once as a CUDA graph
+// and replayed for every generated token without host round trips.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "iam_bucketmul_launch.h"
+#include "iam_common.cuh"
+#include "iam_layers.h"
+
+namespace iam {
+
+enum { MQ = 0, MK, MV, MO, MG, MU, MD, NMAT };
+static const char* kMatNames[NMAT] = {"q", "k", "v", "o", "gate", "up", "down"};
+
+struct Matrix {
+    uint16_t* buckets = nullptr;  // [16*in][out/16] (column shard for column-parallel TP)
+    uint16_t* stats = nullptr;    // [16*in] channel 3 of the stats (all rows, every rank)
+    uint16_t* probes = nullptr;   // [in]
+    int in_dim = 0, out_dim = 0;  // full matrix shape
+    int cols = 0;                 // bucket columns held (out/16, or a shard of them)
+    int in_begin = 0, in_end = 0; // inputs held (row-parallel shard) -- full range otherwise
+};
+
+struct Layer {
+    uint16_t* attn_norm = nullptr;
+    uint16_t* ffn_norm = nullptr;
+    Matrix m[NMAT];
+};
+
+// splitmix64 -> two uniforms -> Box-Muller: a reproducible N(0,1) per (seed, tensor, index).
+IAM_DEV unsigned long long mix64(unsigned long long z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+__global__ void init_normal_fp16(uint16_t* w, size_t n, unsigned long long seed, unsigned long long tensor,
+                                 float stddev) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const unsigned long long h = mix64(seed ^ mix64(tensor * 0x100000001b3ull + (i >> 1)));
+        const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = ((float)((h >> 16) & 0xffffffull) + 0.5f) * (1.0f / 16777216.0f);
+        const float r = sqrtf(-2.0f * logf(u1));
+        const float z = (i & 1) ? r * sinpif(2.0f * u2) : r * cospif(2.0f * u2);
+        w[i] = __half_as_ushort(__float2half_rn(z * stddev));
+    }
+}
+
+__global__ void fill_u16(uint16_t* w, size_t n, uint16_t v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) w[i] = v;
+}
+
+__global__ void set_int_kernel(int* p, int v) { *p = v; }
+
+// Copies columns [c0, c0+cols_out) of every row of a [rows][cols_in] u16 array.
+__global__ void slice_cols_kernel(const uint16_t* src, int rows, int cols_in, int c0, int cols_out, uint16_t* dst) {
+    const size_t n = (size_t)rows * cols_out;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols_out, c = i % cols_out;
+        dst[i] = src[r * cols_in + c0 + c];
+    }
+}
+
+}  // namespace iam
+
+using namespace iam;
+
+struct iam_model_s {
+    iam_model_config cfg{};
+    int device = 0;
+    int sm_count = 148;
+    int tp_rank = 0, tp_world = 1;
+    uint16_t* embed = nullptr;
+    uint16_t* final_norm = nullptr;
+    uint16_t* lm_head = nullptr;
+    std::vector<Layer> layers;
+    uint16_t* k_cache = nullptr;  // [L][kvh_local][max_ctx][hd]
+    uint16_t* v_cache = nullptr;
+    float* rope = nullptr;
+    float *x = nullptr, *x1 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *g = nullptr, *u = nullptr, *logits = nullptr;
+    int* pos = nullptr;
+    int* token_used = nullptr;
+    int* gen_count = nullptr;
+    unsigned long long* key = nullptr;
+    int* sel = nullptr;  // [L*7] selected rows of the last step
+    // bucketMul scratch, one slot per problem of a batch
+    float* partials[3] = {nullptr, nullptr, nullptr};
+    int* ctr[3] = {nullptr, nullptr, nullptr};
+    int* split_sel[3] = {nullptr, nullptr, nullptr};
+    // attention scratch
+    float* att_part = nullptr;
+    int* att_ctr = nullptr;
+    int att_split = 32, chunk_cap = 0;
+    // launch plans for the current effort
+    std::vector<BMBatch> plans;  // 4 per layer
+    float plan_effort = -1.0f;
+    int vec = 4, G = 4;
+    // generation graph
+    cudaGraphExec_t gen_graph = nullptr;
+    float gen_effort = -1.0f;
+    int gen_steps = 0;
+    int* gen_tokens = nullptr;
+    std::vector<void*> allocs;
+    int n_heads_local = 0, n_kv_local = 0, ffn_local = 0;
+};
+
+namespace {
+
+template <class T>
+int dalloc(iam_model_s* m, T** p, size_t count) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaMalloc(&ptr, count * sizeof(T) + 16);
+    if (e != cudaSuccess) return cuda_fail(e, "model cudaMalloc");
+    m->allocs.push_back(ptr);
+    *p = reinterpret_cast<T*>(ptr);
+    return IAM_OK;
+}
+
+int check_cfg(const iam_model_config* c) {
+    if (!c) return fail(IAM_ERR_ARG, "model: null config");
+    if (c->dim <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 || c->head_dim <= 0 ||
+        c->ffn_dim <= 0 || c->vocab <= 0 || c->max_ctx <= 0)
+        return fail(IAM_ERR_ARG, "model: every dimension must be positive");
+    if (c->n_heads % c->n_kv_heads) return fail(IAM_ERR_ARG, "model: n_heads must be a multiple of n_kv_heads");
+    const int gq = c->n_heads / c->n_kv_heads;
+    if (gq != 1 && gq != 2 && gq != 4 && gq != 8) return fail(IAM_ERR_UNSUPPORTED, "model: GQA group must be 1/2/4/8");
+    if (c->head_dim % 2 || c->head_dim > 1024) return fail(IAM_ERR_ARG, "model: head_dim must be even and <= 1024");
+    if (c->n_heads * c->head_dim % 16 || c->n_kv_heads * c->head_dim % 16 || c->dim % 16 || c->ffn_dim % 16)
+        return fail(IAM_ERR_ARG, "model: every projection width must be a multiple of 16");
+    if (c->dim % 8 || c->ffn_dim % 8) return fail(IAM_ERR_ARG, "model: dim and ffn_dim must be multiples of 8");
+    return IAM_OK;
+}
+
+// RoPE table exactly as precompute_rope_cache (attention.hpp:210-226): freq in double then
+// float, angle = float(pos) * freq, cosf / sinf.
+std::vector<float> rope_table(const iam_model_config& c) {
+    const int half = c.head_dim / 2;
+    std::vector<float> t((size_t)c.max_ctx * c.head_dim);
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; ++i) {
+        const double exponent = (2.0 * i) / c.head_dim;
+        freq[i] = (float)(1.0 / std::pow(c.rope_theta, exponent));
+    }
+    for (int p = 0; p < c.max_ctx; ++p)
+        for (int i = 0; i < half; ++i) {
+            const float angle = (float)p * freq[i];
+            t[(size_t)p * c.head_dim + 2 * i] = std::cos(angle);
+            t[(size_t)p * c.head_dim + 2 * i + 1] = std::sin(angle);
+        }
+    return t;
+}
+
+int alloc_runtime(iam_model_s* m) {
+    const iam_model_config& c = m->cfg;
+    const int hd = c.head_dim;
+    int rc;
+    const size_t kv = (size_t)c.n_layers * m->n_kv_local * c.max_ctx * hd;
+    if ((rc = dalloc(m, &m->k_cache, kv)) || (rc = dalloc(m, &m->v_cache, kv))) return rc;
+    IAM_CUDA_TRY(cudaMemset(m->k_cache, 0, kv * 2));
+    IAM_CUDA_TRY(cudaMemset(m->v_cache, 0, kv * 2));
+    if ((rc = dalloc(m, &m->rope, (size_t)c.max_ctx * hd))) return rc;
+    std::vector<float> rt = rope_table(c);
+    IAM_CUDA_TRY(cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float), cudaMemcpyHostToDevice));
+    const int qn = c.n_heads * hd, kvn = c.n_kv_heads * hd;
+    if ((rc = dalloc(m, &m->x, c.dim)) || (rc = dalloc(m, &m->x1, c.dim)) || (rc = dalloc(m, &m->q, qn)) ||
+        (rc = dalloc(m, &m->k, kvn)) || (rc = dalloc(m, &m->v, kvn)) || (rc = dalloc(m, &m->att, qn)) ||
+        (rc = dalloc(m, &m->g, c.ffn_dim)) || (rc = dalloc(m, &m->u, c.ffn_dim)) ||
+        (rc = dalloc(m, &m->logits, c.vocab)) || (rc = dalloc(m, &m->pos, 4)) || (rc = dalloc(m, &m->token_used, 4)) || (rc = dalloc(m, &m->gen_count, 4)) ||
+        (rc = dalloc(m, &m->key, 2)) || (rc = dalloc(m, &m->sel, (size_t)c.n_layers * NMAT)))
+        return rc;
+    IAM_CUDA_TRY(cudaMemset(m->pos, 0, 16));
+    IAM_CUDA_TRY(cudaMemset(m->key, 0, 16));
+    const int cols_max = std::max(std::max(qn, c.dim), c.ffn_dim) / 16;
+    for (int s = 0; s < 3; ++s) {
+        if ((rc = dalloc(m, &m->partials[s], (size_t)kMaxSplits * 16 * cols_max)) ||
+            (rc = dalloc(m, &m->ctr[s], 4096)) || (rc = dalloc(m, &m->split_sel[s], kMaxSplits)))
+            return rc;
+        IAM_CUDA_TRY(cudaMemset(m->ctr[s], 0, 4096 * sizeof(int)));
+    }
+    const int gq = c.n_heads / c.n_kv_heads;
+    m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, m->n_kv_local)));
+    m->chunk_cap = (c.max_ctx + m->att_split - 1) / m->att_split;
+    if ((rc = dalloc(m, &m->att_part, (size_t)m->n_kv_local * m->att_split * gq * (hd + 2))) ||
+        (rc = dalloc(m, &m->att_ctr, m->n_kv_local)))
+        return rc;
+    IAM_CUDA_TRY(cudaMemset(m->att_ctr, 0, m->n_kv_local * sizeof(int)));
+    return IAM_OK;
+}
+
+void free_model(iam_model_s* m) {
+    if (m->gen_graph) cudaGraphExecDestroy(m->gen_graph);
+    for (void* p : m->allocs) cudaFree(p);
+    delete m;
+}
+
+int make_matrix_random(iam_model_s* m, Matrix& mat, int out_dim, int in_dim, unsigned long long seed,
+                       unsigned long long tensor, uint16_t* wtmp) {
+    mat.in_dim = in_dim;
+    mat.out_dim = out_dim;
+    mat.cols = out_dim / 16;
+    mat.in_begin = 0;
+    mat.in_end = in_dim;
+    int rc;
+    if ((rc = dalloc(m, &mat.buckets, (size_t)16 * in_dim * mat.cols)) || (rc = dalloc(m, &mat.stats, (size_t)16 * in_dim)) ||
+        (rc = dalloc(m, &mat.probes, (size_t)in_dim)))
+        return rc;
+    const size_t n = (size_t)out_dim * in_dim;
+    init_normal_fp16<<<4 * m->sm_count, 256>>>(wtmp, n, seed, tensor, 0.02f);
+    IAM_CUDA_TRY(cudaGetLastError());
+    return bucketize_launch(wtmp, out_dim, in_dim, mat.buckets, nullptr, mat.stats, mat.probes, 0);
+}
+
+// ------------------------------------------------------------------ reference file format
+
+struct Meta {
+    long b0 = 0, b1 = 0, b2 = 0, s0 = 0, s1 = 0, s2 = 0, p0 = 0, p1 = 0, in_dim = 0, out_dim = 0, bsize = 0;
+};
+
+// binary_loader.hpp:59-102
+int read_meta(const std::string& file, Meta& mt) {
+    std::ifstream f(file);
+    if (!f) return fail(IAM_ERR_IO, "Cannot open metadata file: " + file);
+    std::string line;
+    while (std::getline(f, line)) {
+        if (line.empty() || line[0] == '#') continue;
+        std::istringstream is(line);
+        std::string key;
+        is >> key;
+        if (key == "buckets_shape:") is >> mt.b0 >> mt.b1 >> mt.b2;
+        else if (key == "stats_shape:") is >> mt.s0 >> mt.s1 >> mt.s2;
+        else if (key == "probes_shape:") is >> mt.p0 >> mt.p1;
+        else if (key == "in_dim:") is >> mt.in_dim;
+        else if (key == "out_dim:") is >> mt.out_dim;
+        else if (key == "bsize:") is >> mt.bsize;
+    }
+    if (mt.in_dim == 0 || mt.out_dim == 0) return fail(IAM_ERR_IO, "Invalid metadata - missing dimensions: " + file);
+    return IAM_OK;
+}
+
+// binary_loader.hpp:105-134: the file size must equal the metadata size.
+int read_u16(const std::string& file, size_t n, std::vector<uint16_t>& out) {
+    std::ifstream f(file, std::ios::binary | std::ios::ate);
+    if (!f) return fail(IAM_ERR_IO, "Cannot open binary file: " + file);
+    const size_t size = (size_t)f.tellg();
+    if (size != n * 2) {
+        std::ostringstream os;
+        os << "File size mismatch: " << file << " has " << size << " bytes, expected " << n * 2;
+        return fail(IAM_ERR_IO, os.str());
+    }
+    f.seekg(0);
+    out.resize(n);
+    if (!f.read(reinterpret_cast<char*>(out.data()), (std::streamsize)size)) return fail(IAM_ERR_IO, "Failed to read " + file);
+    return IAM_OK;
+}
+
+// model.hpp:54-81: fp16 payload after the .npy header.
+int read_npy_u16(const std::string& file, size_t n, std::vector<uint16_t>& out) {
+    std::ifstream f(file, std::ios::binary | std::ios::ate);
+    if (!f) return fail(IAM_ERR_IO, "Cannot open: " + file);
+    const size_t size = (size_t)f.tellg();
+    f.seekg(0);
+    char hdr[10];
+    if (size < 10 || !f.read(hdr, 10) || std::memcmp(hdr, "\x93NUMPY", 6) != 0) return fail(IAM_ERR_IO, "not a .npy file: " + file);
+    const size_t hlen = (unsigned char)hdr[8] | ((size_t)(unsigned char)hdr[9] << 8);
+    if (size < 10 + hlen || size - 10 - hlen != n * 2) {
+        std::ostringstream os;
+        os << "npy payload mismatch: " << file << " expected " << n << " fp16 values";
+        return fail(IAM_ERR_IO, os.str());
+    }
+    f.seekg((std::streamoff)(10 + hlen));
+    out.resize(n);
+    if (!f.read(reinterpret_cast<char*>(out.data()), (std::streamsize)(n * 2))) return fail(IAM_ERR_IO, "Failed to read " + file);
+    return IAM_OK;
+}
+
+int upload(iam_model_s* m, uint16_t** dst, const std::vector<uint16_t>& src) {
+    int rc = dalloc(m, dst, src.size());
+    if (rc) return rc;
+    IAM_CUDA_TRY(cudaMemcpy(*dst, src.data(), src.size() * 2, cudaMemcpyHostToDevice));
+    return IAM_OK;
+}
+
+int load_matrix(iam_model_s* m, const std::string& dir, int layer, int which, int out_dim, int in_dim, Matrix& mat) {
+    const std::string prefix = dir + "/layer" + std::to_string(layer) + "_" + kMatNames[which] + "_proj_bucketmul_fp16";
+    Meta mt;
+    int rc = read_meta(prefix + "_meta.txt", mt);
+    if (rc) return rc;
+    if (mt.in_dim != in_dim || mt.out_dim != out_dim || mt.b1 != 16L * in_dim || mt.b2 != out_dim / 16 ||
+        mt.s1 != 16L * in_dim || mt.p1 != in_dim)
+        return fail(IAM_ERR_IO, "weight shape differs from the model config: " + prefix);
+    std::vector<uint16_t> b, s, p;
+    if ((rc = read_u16(prefix + "_buckets.bin", (size_t)(mt.b0 * mt.b1 * mt.b2), b)) ||
+        (rc = read_u16(prefix + "_stats.bin", (size_t)(mt.s0 * mt.s1 * mt.s2), s)) ||
+        (rc = read_u16(prefix + "_probes.bin", (size_t)(mt.p0 * mt.p1), p)))
+        return rc;
+    std::vector<uint16_t> s1((size_t)mt.s1);
+    for (size_t r = 0; r < s1.size(); ++r) s1[r] = s[r * (size_t)mt.s2 + (size_t)(mt.s2 - 1)];  // channel 3
+    mat.in_dim = in_dim;
+    mat.out_dim = out_dim;
+    mat.cols = out_dim / 16;
+    mat.in_begin = 0;
+    mat.in_end = in_dim;
+    if ((rc = upload(m, &mat.buckets, b)) || (rc = upload(m, &mat.stats, s1))) return rc;
+    p.resize((size_t)in_dim);
+    return upload(m, &mat.probes, p);
+}
+
+// ------------------------------------------------------------------ step
+
+void fill_problem(iam_model_s* m, BMProblem& p, const Matrix& mat, float effort, float* out, int slot) {
+    memset(&p, 0, sizeof(p));
+    p.buckets = mat.buckets;
+    p.stats = mat.stats;
+    p.stats_stride = 1;
+    p.probes = mat.probes;
+    p.row0 = 0;
+    p.bucket_row0 = 16LL * mat.in_begin;
+    p.in_begin = mat.in_begin;
+    p.n_rows_valid = 16 * mat.in_end;
+    p.n_inputs = mat.in_end;
+    p.cols = mat.cols;
+    p.P = std::min(mat.in_dim, IAM_PROBES_COUNT);
+    p.target = bm_target(effort, p.P);
+    p.out = out;
+    p.partials = m->partials[slot];
+    p.slice_ctr = m->ctr[slot];
+    p.split_sel = m->split_sel[slot];
+}
+
+int build_plans(iam_model_s* m, float effort) {
+    if (m->plan_effort == effort && !m->plans.empty()) return IAM_OK;
+    const iam_model_config& c = m->cfg;
+    m->plans.assign((size_t)c.n_layers * 4, BMBatch{});
+    const int mac = bm_max_active_clusters(m->vec, m->G);
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer& L = m->layers[l];
+        int* sel = m->sel + l * NMAT;
+        BMBatch& qkv = m->plans[l * 4 + 0];
+        memset(&qkv, 0, sizeof(qkv));
+        qkv.nprob = 3;
+        qkv.mode = kModeFused;
+        qkv.xmode = kXRms;
+        float* outs[3] = {m->q, m->k, m->v};
+        for (int i = 0; i < 3; ++i) {
+            fill_problem(m, qkv.p[i], L.m[MQ + i], effort, outs[i], i);
+            qkv.p[i].x = m->x;
+            qkv.p[i].gain = L.attn_norm;
+            qkv.p[i].norm_eps = c.norm_eps;
+            qkv.p[i].norm_n = c.dim;
+            qkv.p[i].count_out = sel + MQ + i;
+        }
+        bm_plan(qkv, m->vec, m->G, mac);
+
+        BMBatch& o = m->plans[l * 4 + 1];
+        memset(&o, 0, sizeof(o));
+        o.nprob = 1;
+        o.mode = kModeFused;
+        o.xmode = kXPlain;
+        fill_problem(m, o.p[0], L.m[MO], effort, m->x1, 0);
+        o.p[0].x = m->att;
+        o.p[0].residual = m->tp_world == 1 ? m->x : nullptr;
+        o.p[0].count_out = sel + MO;
+        bm_plan(o, m->vec, m->G, mac);
+
+        BMBatch& gu = m->plans[l * 4 + 2];
+        memset(&gu, 0, sizeof(gu));
+        gu.nprob = 2;
+        gu.mode = kModeFused;
+        gu.xmode = kXRms;
+        float* gouts[2] = {m->g, m->u};
+        for (int i = 0; i < 2; ++i) {
+            fill_problem(m, gu.p[i], L.m[MG + i], effort, gouts[i], i);
+            gu.p[i].x = m->x1;
+            gu.p[i].gain = L.ffn_norm;
+            gu.p[i].norm_eps = c.norm_eps;
+            gu.p[i].norm_n = c.dim;
+            gu.p[i].count_out = sel + MG + i;
+        }
+        bm_plan(gu, m->vec, m->G, mac);
+
+        BMBatch& d = m->plans[l * 4 + 3];
+        memset(&d, 0, sizeof(d));
+        d.nprob = 1;
+        d.mode = kModeFused;
+        d.xmode = kXSilu;
+        fill_problem(m, d.p[0], L.m[MD], effort, m->x, 0);
+        d.p[0].x = m->g;
+        d.p[0].x2 = m->u;
+        d.p[0].residual = m->tp_world == 1 ? m->x1 : nullptr;
+        d.p[0].count_out = sel + MD;
+        bm_plan(d, m->vec, m->G, mac);
+    }
+    m->plan_effort = effort;
+    return IAM_OK;
+}
+
+// token: token_arg (>= 0), or the previous argmax when token_arg < 0.  pos: pos_arg (>= 0)
+// is written to the device first, else the device value is used.
+int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float* logits, cudaStream_t s) {
+    const iam_model_config& c = m->cfg;
+    int rc = build_plans(m, effort);
+    if (rc) return rc;
+    if (pos_arg >= 0) {
+        set_int_kernel<<<1, 1, 0, s>>>(m->pos, pos_arg);
+        IAM_CUDA_TRY(cudaGetLastError());
+    }
+    if ((rc = launch_embed(m->embed, c.dim, token_arg, token_arg < 0 ? m->key : nullptr, nullptr, m->x, m->key,
+                           m->token_used, s)))
+        return rc;
+    const int gq = c.n_heads / c.n_kv_heads;
+    for (int l = 0; l < c.n_layers; ++l) {
+        if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->G, s))) return rc;
+        AttnParams ap{};
+        ap.q = m->q;
+        ap.k = m->k;
+        ap.v = m->v;
+        const size_t layer_kv = (size_t)m->n_kv_local * c.max_ctx * c.head_dim;
+        ap.k_cache = m->k_cache + (size_t)l * layer_kv;
+        ap.v_cache = m->v_cache + (size_t)l * layer_kv;
+        ap.rope = m->rope;
+        ap.pos_dev = m->pos;
+        ap.out = m->att;
+        ap.part = m->att_part;
+        ap.ctr = m->att_ctr;
+        ap.n_kv_heads = m->n_kv_local;
+        ap.head_dim = c.head_dim;
+        ap.max_ctx = c.max_ctx;
+        ap.n_split = m->att_split;
+        ap.chunk_cap = m->chunk_cap;
+        if ((rc = launch_attention(ap, gq, s))) return rc;
+        if ((rc = bm_launch(m->plans[l * 4 + 1], m->vec, m->G, s))) return rc;
+        if ((rc = bm_launch(m->plans[l * 4 + 2], m->vec, m->G, s))) return rc;
+        if ((rc = bm_launch(m->plans[l * 4 + 3], m->vec, m->G, s))) return rc;
+    }
+    LMHeadParams hp{};
+    hp.W = m->lm_head;
+    hp.x = m->x;
+    hp.gain = m->final_norm;
+    hp.eps = c.norm_eps;
+    hp.dim = c.dim;
+    hp.rows = c.vocab;
+    hp.logits = logits;
+    hp.argmax_key = m->key;
+    return launch_lm_head(hp, 2 * m->sm_count, s);
+}
+
+bool effort_ok(float e) { return std::isfinite(e) && e > 0.0f && e <= 1.0f; }
+
+int finish_create(iam_model_s* m, iam_model_t* out) {
+    int rc = alloc_runtime(m);
+    if (rc) {
+        free_model(m);
+        return rc;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        free_model(m);
+        return cuda_fail(e, "model creation");
+    }
+    *out = m;
+    return IAM_OK;
+}
+
+int init_common(iam_model_s* m, const iam_model_config* cfg, int device) {
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    rc = iam_device_info(device, &m->sm_count, nullptr, nullptr);
+    if (rc) return rc;
+    IAM_CUDA_TRY(cudaSetDevice(device));
+    m->cfg = *cfg;
+    m->device = device;
+    m->n_heads_local = cfg->n_heads;
+    m->n_kv_local = cfg->n_kv_heads;
+    m->ffn_local = cfg->ffn_dim;
+    m->layers.assign(cfg->n_layers, Layer{});
+    const char* g = getenv("IAM_BM_CLUSTER");
+    m->G = g && *g ? atoi(g) : bm_default_cluster();
+    const char* v = getenv("IAM_BM_VEC");
+    m->vec = v && (atoi(v) == 8 || atoi(v) == 1) ? atoi(v) : 4;
+    return IAM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed, int device) {
+    if (!out) return fail(IAM_ERR_ARG, "iam_model_create_random: null out");
+    *out = nullptr;
+    iam_model_s* m = new iam_model_s();
+    int rc = init_common(m, cfg, device);
+    if (rc) {
+        delete m;
+        return rc;
+    }
+    const iam_model_config& c = m->cfg;
+    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim;
+    const size_t wmax = (size_t)std::max(std::max(qn, c.dim), c.ffn_dim) * std::max(c.dim, c.ffn_dim);
+    uint16_t* wtmp = nullptr;
+    if ((rc = dalloc(m, &wtmp, wmax))) {
+        free_model(m);
+        return rc;
+    }
+    const uint16_t one = 0x3c00;  // fp16 1.0: RMSNorm gains
+    unsigned long long tensor = 1;
+    for (int l = 0; l < c.n_layers && !rc; ++l) {
+        Layer& L = m->layers[l];
+        const int outs[NMAT] = {qn, kvn, kvn, c.dim, c.ffn_dim, c.ffn_dim, c.dim};
+        const int ins[NMAT] = {c.dim, c.dim, c.dim, qn, c.dim, c.dim, c.ffn_dim};
+        for (int i = 0; i < NMAT && !rc; ++i)
+            rc = make_matrix_random(m, L.m[i], outs[i], ins[i], seed, tensor++, wtmp);
+        if (!rc && !(rc = dalloc(m, &L.attn_norm, c.dim)) && !(rc = dalloc(m, &L.ffn_norm, c.dim))) {
+            fill_u16<<<8, 256>>>(L.attn_norm, c.dim, one);
+            fill_u16<<<8, 256>>>(L.ffn_norm, c.dim, one);
+        }
+    }
+    if (!rc && !(rc = dalloc(m, &m->embed, (size_t)c.vocab * c.dim)) && !(rc = dalloc(m, &m->final_norm, c.dim))) {
+        init_normal_fp16<<<4 * m->sm_count, 256>>>(m->embed, (size_t)c.vocab * c.dim, seed, 0, 0.02f);
+        fill_u16<<<8, 256>>>(m->final_norm, c.dim, one);
+        m->lm_head = m->embed;  // tied embeddings
+        if (!c.tied_embeddings && !(rc = dalloc(m, &m->lm_head, (size_t)c.vocab * c.dim)))
+            init_normal_fp16<<<4 * m->sm_count, 256>>>(m->lm_head, (size_t)c.vocab * c.dim, seed, tensor++, 0.02f);
+    }
+    if (rc) {
+        free_model(m);
+        return rc;
+    }
+    return finish_create(m, out);
+}
+
+int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device) {
+    if (!out || !weights_dir) return fail(IAM_ERR_ARG, "iam_model_load: null argument");
+    *out = nullptr;
+    iam_model_s* m = new iam_model_s();
+    int rc = init_common(m, cfg, device);
+    if (rc) {
+        delete m;
+        return rc;
+    }
+    const iam_model_config& c = m->cfg;
+    const std::string dir(weights_dir);
+    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim;
+    std::vector<uint16_t> buf;
+    for (int l = 0; l < c.n_layers && !rc; ++l) {
+        Layer& L = m->layers[l];
+        const int outs[NMAT] = {qn, kvn, kvn, c.dim, c.ffn_dim, c.ffn_dim, c.dim};
+        const int ins[NMAT] = {c.dim, c.dim, c.dim, qn, c.dim, c.dim, c.ffn_dim};
+        for (int i = 0; i < NMAT && !rc; ++i) rc = load_matrix(m, dir, l, i, outs[i], ins[i], L.m[i]);
+        const std::string lp = dir + "/layer" + std::to_string(l);
+        if (!rc && !(rc = read_npy_u16(lp + "_input_layernorm.npy", c.dim, buf))) rc = upload(m, &L.attn_norm, buf);
+        if (!rc && !(rc = read_npy_u16(lp + "_post_attention_layernorm.npy", c.dim, buf))) rc = upload(m, &L.ffn_norm, buf);
+    }
+    if (!rc && !(rc = read_npy_u16(dir + "/embed_tokens.npy", (size_t)c.vocab * c.dim, buf))) rc = upload(m, &m->embed, buf);
+    if (!rc && !(rc = read_npy_u16(dir + "/norm_weight.npy", c.dim, buf))) rc = upload(m, &m->final_norm, buf);
+    if (!rc) {
+        if (c.tied_embeddings) {
+            m->lm_head = m->embed;
+        } else if (!(rc = read_npy_u16(dir + "/lm_head.npy", (size_t)c.vocab * c.dim, buf))) {
+            rc = upload(m, &m->lm_head, buf);
+        }
+    }
+    if (rc) {
+        free_model(m);
+        return rc;
+    }
+    return finish_create(m, out);
+}
+
+int iam_model_destroy(iam_model_t m) {
+    if (m) free_model(m);
+    return IAM_OK;
+}
+
+int iam_model_reset(iam_model_t m, void* stream) {
+    if (!m) return fail(IAM_ERR_ARG, "iam_model_reset: null model");
+    const size_t kv = (size_t)m->cfg.n_layers * m->n_kv_local * m->cfg.max_ctx * m->cfg.head_dim * 2;
+    IAM_CUDA_TRY(cudaMemsetAsync(m->k_cache, 0, kv, (cudaStream_t)stream));
+    IAM_CUDA_TRY(cudaMemsetAsync(m->v_cache, 0, kv, (cudaStream_t)stream));
+    IAM_CUDA_TRY(cudaMemsetAsync(m->pos, 0, sizeof(int), (cudaStream_t)stream));
+    return IAM_OK;
+}
+
+int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* logits_dev, void* stream) {
+    if (!m) return fail(IAM_ERR_ARG, "iam_model_forward: null model");
+    if (token < 0 || token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_forward: token out of range");
+    if (pos < 0 || pos >= m->cfg.max_ctx) return fail(IAM_ERR_ARG, "iam_model_forward: pos out of range");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_forward: effort must be in (0, 1]");
+    return enqueue_step(m, token, pos, effort, logits_dev ? logits_dev : m->logits, (cudaStream_t)stream);
+}
+
+int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort, int* tokens_dev,
+                       void* stream) {
+    if (!m || !tokens_dev) return fail(IAM_ERR_ARG, "iam_model_generate: null argument");
+    if (first_token < 0 || first_token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_generate: bad token");
+    if (start_pos < 0 || n_tokens < 0 || start_pos + n_tokens > m->cfg.max_ctx)
+        return fail(IAM_ERR_ARG, "iam_model_generate: positions exceed max_ctx");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_generate: effort must be in (0, 1]");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n_tokens == 0) return IAM_OK;
+    // step 0 from the given token (eager), then one captured step replayed per token; each
+    // step appends its greedy token to tokens_dev[gen_count++] and advances pos on device
+    IAM_CUDA_TRY(cudaMemsetAsync(m->gen_count, 0, sizeof(int), s));
+    int rc = enqueue_step(m, first_token, start_pos, effort, m->logits, s);
+    if (rc) return rc;
+    if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s))) return rc;
+    if (n_tokens == 1) return IAM_OK;
+    if (!m->gen_graph || m->gen_effort != effort || m->gen_tokens != tokens_dev) {
+        if (m->gen_graph) {
+            cudaGraphExecDestroy(m->gen_graph);
+            m->gen_graph = nullptr;
+        }
+        cudaStream_t cap;
+        IAM_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess) {
+            rc = enqueue_step(m, -1, -1, effort, m->logits, cap);
+            if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, cap);
+            e = cudaStreamEndCapture(cap, &graph);
+        }
+        if (e == cudaSuccess && !rc) e = cudaGraphInstantiate(&m->gen_graph, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        cudaStreamDestroy(cap);
+        if (rc) return rc;
+        if (e != cudaSuccess) return cuda_fail(e, "iam_model_generate: graph capture");
+        m->gen_effort = effort;
+        m->gen_tokens = tokens_dev;
+    }
+    for (int i = 1; i < n_tokens; ++i) IAM_CUDA_TRY(cudaGraphLaunch(m->gen_graph, s));
+    return IAM_OK;
+}
+
+int iam_model_set_kv(iam_model_t m, int layer, const uint16_t* k_dev, const uint16_t* v_dev, int n_tokens,
+                     void* stream) {
+    if (!m || !k_dev || !v_dev) return fail(IAM_ERR_ARG, "iam_model_set_kv: null argument");
+    if (layer < 0 || layer >= m->cfg.n_layers || n_tokens < 0 || n_tokens > m->cfg.max_ctx)
+        return fail(IAM_ERR_ARG, "iam_model_set_kv: bad layer or n_tokens");
+    const size_t hd = m->cfg.head_dim, ctx = m->cfg.max_ctx;
+    const size_t layer_kv = (size_t)m->n_kv_local * ctx * hd;
+    for (int h = 0; h < m->n_kv_local; ++h) {
+        uint16_t* kd = m->k_cache + layer * layer_kv + h * ctx * hd;
+        uint16_t* vd = m->v_cache + layer * layer_kv + h * ctx * hd;
+        IAM_CUDA_TRY(cudaMemcpyAsync(kd, k_dev + (size_t)h * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
+                                     (cudaStream_t)stream));
+        IAM_CUDA_TRY(cudaMemcpyAsync(vd, v_dev + (size_t)h * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
+                                     (cudaStream_t)stream));
+    }
+    return IAM_OK;
+}
+
+int iam_model_fill_kv_random(iam_model_t m, int n_tokens, unsigned long long seed, void* stream) {
+    if (!m || n_tokens < 0 || n_tokens > m->cfg.max_ctx) return fail(IAM_ERR_ARG, "iam_model_fill_kv_random: bad arguments");
+    const size_t hd = m->cfg.head_dim, ctx = m->cfg.max_ctx;
+    for (int l = 0; l < m->cfg.n_layers; ++l)
+        for (int h = 0; h < m->n_kv_local; ++h) {
+            const size_t off = ((size_t)l * m->n_kv_local + h) * ctx * hd;
+            const unsigned long long t = 0x4b560000ull + ((unsigned long long)l << 8) + h;
+            init_normal_fp16<<<m->sm_count, 256, 0, (cudaStream_t)stream>>>(m->k_cache + off, n_tokens * hd, seed, 2 * t, 1.0f);
+            init_normal_fp16<<<m->sm_count, 256, 0, (cudaStream_t)stream>>>(m->v_cache + off, n_tokens * hd, seed, 2 * t + 1, 1.0f);
+        }
+    IAM_CUDA_TRY(cudaGetLastError());
+    return IAM_OK;
+}
+
+int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, size_t capacity_bytes,
+                          size_t* bytes_out) {
+    if (!m) return fail(IAM_ERR_ARG, "iam_model_read_weight: null model");
+    const iam_model_config& c = m->cfg;
+    const void* src = nullptr;
+    size_t bytes = 0;
+    if (which == IAM_W_EMBED) {
+        src = m->embed;
+        bytes = (size_t)c.vocab * c.dim * 2;
+    } else if (which == IAM_W_FINAL_NORM) {
+        src = m->final_norm;
+        bytes = (size_t)c.dim * 2;
+    } else if (which == IAM_W_LM_HEAD) {
+        src = m->lm_head;
+        bytes = (size_t)c.vocab * c.dim * 2;
+    } else {
+        if (layer < 0 || layer >= c.n_layers) return fail(IAM_ERR_ARG, "iam_model_read_weight: bad layer");
+        const Layer& L = m->layers[layer];
+        if (which == IAM_W_ATTN_NORM) {
+            src = L.attn_norm;
+            bytes = (size_t)c.dim * 2;
+        } else if (which == IAM_W_FFN_NORM) {
+            src = L.ffn_norm;
+            bytes = (size_t)c.dim * 2;
+        } else if (which == IAM_W_K_CACHE || which == IAM_W_V_CACHE) {
+            const size_t layer_kv = (size_t)m->n_kv_local * c.max_ctx * c.head_dim;
+            src = (which == IAM_W_K_CACHE ? m->k_cache : m->v_cache) + layer * layer_kv;
+            bytes = layer_kv * 2;
+        } else if (which >= IAM_W_MATRIX && which < IAM_W_MATRIX + 3 * NMAT) {
+            const Matrix& mt = L.m[(which - IAM_W_MATRIX) / 3];
+            const int part = (which - IAM_W_MATRIX) % 3;
+            const size_t rows = 16 * (size_t)(mt.in_end - mt.in_begin);
+            src = part == 0 ? (const void*)mt.buckets : part == 1 ? (const void*)mt.stats : (const void*)mt.probes;
+            bytes = part == 0 ? rows * mt.cols * 2 : part == 1 ? 16 * (size_t)mt.in_dim * 2 : (size_t)mt.in_dim * 2;
+        } else {
+            return fail(IAM_ERR_ARG, "iam_model_read_weight: unknown weight id");
+        }
+    }
+    if (bytes_out) *bytes_out = bytes;
+    if (!host_dst) return IAM_OK;
+    if (capacity_bytes < bytes) return fail(IAM_ERR_ARG, "iam_model_read_weight: buffer too small");
+    IAM_CUDA_TRY(cudaMemcpy(host_dst, src, bytes, cudaMemcpyDeviceToHost));
+    return IAM_OK;
+}
+
+int iam_model_selected_rows(iam_model_t m, long long* total) {
+    if (!m || !total) return fail(IAM_ERR_ARG, "iam_model_selected_rows: null argument");
+    std::vector<int> h((size_t)m->cfg.n_layers * NMAT);
+    IAM_CUDA_TRY(cudaMemcpy(h.data(), m->sel, h.size() * sizeof(int), cudaMemcpyDeviceToHost));
+    long long t = 0;
+    for (int v : h) t += v;
+    *total = t;
+    return IAM_OK;
+}
+
+// Algorithmic bytes of the last step (bucketMul selected weights, stats, x, probes, outputs,
+// attention K/V reads, LM head) for the roofline accounting of a decode step.
+int iam_model_step_bytes(iam_model_t m, int context, long long* bytes) {
+    if (!m || !bytes) return fail(IAM_ERR_ARG, "iam_model_step_bytes: null argument");
+    const iam_model_config& c = m->cfg;
+    std::vector<int> h((size_t)c.n_layers * NMAT);
+    IAM_CUDA_TRY(cudaMemcpy(h.data(), m->sel, h.size() * sizeof(int), cudaMemcpyDeviceToHost));
+    long long t = 0;
+    for (int l = 0; l < c.n_layers; ++l)
+        for (int i = 0; i < NMAT; ++i) {
+            const Matrix& mt = m->layers[l].m[i];
+            const long long R = 16LL * mt.in_dim;
+            t += 2LL * h[(size_t)l * NMAT + i] * mt.cols + 2 * R + 4LL * mt.in_dim +
+                 2LL * std::min(mt.in_dim, IAM_PROBES_COUNT) + 4LL * 16 * mt.cols;
+        }
+    t += 2LL * c.n_layers * m->n_kv_local * (long long)context * c.head_dim * 2;  // K and V fp16
+    t += 2LL * c.vocab * c.dim;                                                 // LM head
+    *bytes = t;
+    return IAM_OK;
+}
+
+}  // extern "C"

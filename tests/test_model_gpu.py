@@ -1,0 +1,156 @@
+"""Decode-model parity on the GPU against the CPU oracle's decode step (ora_model_forward,
+which follows model.hpp:152-231 / transformer_layer.hpp:75-122 / attention.hpp:135-404).
+
+Bar: greedy token ids equal for at least the first 32 tokens at each
+effort; logits within LOGIT_TOL x RMS (fp32 summation order, GPU expf and the occasional
+bucket row whose importance sits within an ulp of the cutoff differ from the oracle).
+"""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 5e-3
+SMALL = dict(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, ffn_dim=512, vocab=512, max_ctx=96)
+
+
+def rel_err(a, ref):
+    a, ref = np.asarray(a, np.float64), np.asarray(ref, np.float64)
+    rms = np.sqrt(np.mean(ref * ref))
+    return float(np.max(np.abs(a - ref)) / (rms if rms > 0 else 1.0))
+
+
+@pytest.fixture(scope="module")
+def torch_mod(cuda):
+    import torch
+    return torch
+
+
+@pytest.fixture(scope="module")
+def small(iam, cuda):
+    cfg = iam.ModelConfig.make(**SMALL)
+    m = iam.Model.random(cfg, seed=7)
+    w = m.export_weights()
+    yield cfg, m, w
+    m.close()
+
+
+def oracle_for(ora, cfg, w):
+    d = cfg.as_dict()
+    return ora.OracleModel(d, w)
+
+
+@pytest.mark.parametrize("effort", [0.25, 0.5, 1.0])
+def test_decode_matches_oracle(small, ora, torch_mod, effort):
+    torch = torch_mod
+    cfg, m, w = small
+    om = oracle_for(ora, cfg, w)
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(3, cfg.vocab, 8).tolist()
+    m.reset()
+    torch.cuda.synchronize()
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+    for pos, tok in enumerate(prompt):
+        m.forward(tok, pos, effort, logits)
+        torch.cuda.synchronize()
+        best, ref, _ = om.forward(tok, pos, effort)
+        got = logits.cpu().numpy()
+        assert rel_err(got, ref) < LOGIT_TOL, (pos, rel_err(got, ref))
+        assert int(np.argmax(got)) == best
+    # greedy continuation: the reference driver's loop (test_generation.cpp:239-291)
+    n_gen = 40
+    toks = torch.empty(n_gen, dtype=torch.int32, device="cuda")
+    first = best
+    m.generate(first, len(prompt), n_gen, effort, toks)
+    torch.cuda.synchronize()
+    gpu_toks = toks.cpu().numpy().tolist()
+    ref_toks, tok = [], first
+    for i in range(n_gen):
+        tok, _, _ = om.forward(tok, len(prompt) + i, effort)
+        ref_toks.append(tok)
+    assert gpu_toks[:32] == ref_toks[:32], (gpu_toks, ref_toks)
+
+
+def test_decode_is_deterministic(small, torch_mod):
+    torch = torch_mod
+    cfg, m, _ = small
+    outs = []
+    for _ in range(2):
+        m.reset()
+        logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+        for pos, tok in enumerate([5, 17, 99, 3]):
+            m.forward(tok, pos, 0.25, logits)
+        torch.cuda.synchronize()
+        outs.append(logits.cpu().numpy().view(np.uint32).copy())
+    assert (outs[0] == outs[1]).all()
+
+
+def test_reference_file_layout_loads(small, iam, weights_mod, torch_mod, tmp_path):
+    """Weights written in the reference's on-disk layout load through iam_model_load and
+    give bit-identical logits (same weights, deterministic kernels)."""
+    torch = torch_mod
+    cfg, m, w = small
+    d = str(tmp_path)
+    for l, lw in enumerate(w["layers"]):
+        for name in iam.MATRIX_NAMES:
+            bw = lw[name]
+            stats4 = np.repeat(np.asarray(bw.stats).reshape(-1, 1), 4, axis=1)
+            weights_mod.save_bucketmul_binary(
+                weights_mod.BucketWeight(bw.buckets, stats4, bw.probes, bw.in_dim, bw.out_dim),
+                os.path.join(d, weights_mod.layer_weight_name(l, name)))
+        np.save(os.path.join(d, f"layer{l}_input_layernorm.npy"), lw["attn_norm"].view(np.float16))
+        np.save(os.path.join(d, f"layer{l}_post_attention_layernorm.npy"), lw["ffn_norm"].view(np.float16))
+    np.save(os.path.join(d, "embed_tokens.npy"), w["embed"].view(np.float16))
+    np.save(os.path.join(d, "norm_weight.npy"), w["final_norm"].view(np.float16))
+    m2 = iam.Model.load(d, cfg)
+    outs = []
+    for mm in (m, m2):
+        mm.reset()
+        logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+        for pos, tok in enumerate([11, 22, 33]):
+            mm.forward(tok, pos, 0.5, logits)
+        torch.cuda.synchronize()
+        outs.append(logits.cpu().numpy().view(np.uint32).copy())
+    m2.close()
+    assert (outs[0] == outs[1]).all()
+    # truncated file -> IAM_ERR_IO
+    with open(os.path.join(d, weights_mod.layer_weight_name(1, "down") + "_stats.bin"), "r+b") as f:
+        f.truncate(10)
+    with pytest.raises(iam.IamError) as e:
+        iam.Model.load(d, cfg)
+    assert e.value.code == iam.IAM_ERR_IO
+
+
+def test_model_rejects_bad_arguments(small, iam):
+    cfg, m, _ = small
+    for token, pos, effort in [(-1, 0, 0.5), (cfg.vocab, 0, 0.5), (1, cfg.max_ctx, 0.5), (1, 0, 0.0), (1, 0, 2.0)]:
+        with pytest.raises(iam.IamError) as e:
+            m.forward(token, pos, effort)
+        assert e.value.code == iam.IAM_ERR_ARG
+    bad = iam.ModelConfig.make(**dict(SMALL, n_kv_heads=3))
+    with pytest.raises(iam.IamError):
+        iam.Model.random(bad)
+
+
+def test_config3_mistral_layer(iam, ora, torch_mod):
+    """one Mistral-7B decoder layer (d 4096, 32/8 heads, ffn 14336), KV cache
+    of 1024 random N(0,1) fp16 tokens, gains 1.0, effort 0.25; plus the tied 32000-row head."""
+    torch = torch_mod
+    cfg = iam.ModelConfig.make(**dict(iam.MISTRAL_7B, n_layers=1, max_ctx=1040))
+    m = iam.Model.random(cfg, seed=3)
+    m.fill_kv_random(1024, seed=5)
+    torch.cuda.synchronize()
+    w = m.export_weights()
+    om = oracle_for(ora, cfg, w)
+    om.set_kv(m.read_weight(iam.W_K_CACHE, 0), m.read_weight(iam.W_V_CACHE, 0))
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+    m.forward(1234, 1024, 0.25, logits)
+    torch.cuda.synchronize()
+    best, ref, sel = om.forward(1234, 1024, 0.25, nthreads=os.cpu_count() or 1)
+    got = logits.cpu().numpy()
+    assert rel_err(got, ref) < LOGIT_TOL
+    assert int(np.argmax(got)) == best
+    assert m.selected_rows() > 0
+    m.close()
