@@ -2,16 +2,27 @@
 """bench.py -- B200 benchmark of the Effort-style dynamic-sparse decode path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload bucketmul] [--effort 0.25]
+                  [--workload decode|bucketmul] [--effort 0.25]
 
-Prints ONE JSON line (rank 0).  Workload `bucketmul`: one step = the 7
-bucketMuls of a Mistral-7B layer (q,k,v 4096->4096/1024/1024, o 4096->4096, gate/up
-4096->14336, down 14336->4096) at the given effort over fp16 weights N(0,0.02) bucketized on
-the GPU, inputs N(0,1) with 1% of channels x20; consecutive steps alternate between two
-independent weight sets (~0.9 GB > the 126 MB L2).  `value` is effective HBM GB/s over the
-algorithmic bytes 2|S|C + 2R + 4N + 2*4096 + 4M per bucketMul (|S| = selected rows reported
-by the kernel).  `--impl reference` times the CPU restatement of the reference's kernels
-(oracle/, all host threads) on the same workload.
+Prints ONE JSON line (rank 0).
+
+`decode` (default): the 32-layer Mistral-7B shape (d 4096, 32/8 heads,
+head_dim 128, ffn 14336, vocab 32000, tied embeddings) with random-init N(0, 0.02) fp16
+weights bucketized on the GPU, RMSNorm gains 1.0, a 128-token prompt drawn uniformly from
+[3, 32000) with seed 1, then greedy decoding at `--effort`.  One step = one generated token
+(32 layers + LM head + argmax); W untimed tokens, then K timed tokens, all replays of one
+captured CUDA graph.  `value` = generated tokens/s on the device clock; `e2e` = the same
+through iam_model_forward from the host with the logits read back and argmaxed on the host
+every token (the reference driver's loop, test_generation.cpp:239-291).  The roofline is the
+fused bucketMul kernel's effective HBM bandwidth: its algorithmic bytes (2|S|C + 2R + 4N +
+2*4096 + 4M per bucketMul, |S| reported by the kernel) over its CUDA-event time inside the
+captured step.  Weights (13.9 GB) exceed the 126 MB L2 by two orders of magnitude.
+
+`bucketmul`: one step = the 7 bucketMuls of one Mistral layer on
+alternating weight sets; value = effective GB/s.
+
+`--impl reference` times the CPU restatement of the reference's kernels (oracle/, every
+host thread) on the same workload.
 """
 import argparse
 import json
@@ -262,10 +273,185 @@ def cpu_baseline_bucketmul(sets, effort, budget_s=10.0, steps=None):
             "seconds": round(el, 2), "ms_per_step": round(1e3 * el / done, 2)}
 
 
+# ---------------------------------------------------------------- decode workload
+
+PROMPT_LEN = 128
+
+
+def mistral_cfg(iam, max_ctx):
+    return iam.ModelConfig.make(**dict(iam.MISTRAL_7B, max_ctx=max_ctx))
+
+
+def prompt_tokens(vocab):
+    return np.random.default_rng(1).integers(3, vocab, PROMPT_LEN).tolist()
+
+
+def run_decode(args, rank, world):
+    import torch
+    iam = load_pkg()
+    dev = torch.device(f"cuda:{int(os.environ.get('LOCAL_RANK', 0))}")
+    torch.cuda.set_device(dev)
+    sweep = [e for e in (0.5, 1.0) if e != args.effort] if not args.no_sweep else []
+    n_sweep = max(8, args.steps // 4)
+    n_prof = 4
+    n_e2e = max(3, min(args.steps, 32))
+    max_ctx = PROMPT_LEN + args.warmup + args.steps + n_sweep * len(sweep) + n_prof + n_e2e + 8
+    cfg = mistral_cfg(iam, max_ctx)
+    t_build = time.perf_counter()
+    model = iam.Model.random(cfg, seed=0)
+    build_s = time.perf_counter() - t_build
+    stream = torch.cuda.current_stream()
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+    prompt = prompt_tokens(cfg.vocab)
+    for pos, tok in enumerate(prompt):  # token-by-token prompt ingestion (test_generation.cpp:202-210)
+        model.forward(tok, pos, args.effort, logits)
+    first = int(torch.argmax(logits).item())
+    toks = torch.empty(max_ctx, dtype=torch.int32, device=dev)
+    model.generate(first, PROMPT_LEN, args.warmup, args.effort, toks)  # includes the graph capture
+    torch.cuda.synchronize()
+
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        t0.record(stream)
+        model.generate(-1, 0, args.steps, args.effort, toks)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        torch.distributed.barrier()
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t[0])
+    ctx_end = PROMPT_LEN + args.warmup + args.steps
+    sel_rows = model.selected_rows()
+    step_bytes = model.step_bytes(ctx_end)
+    tok_s = world * args.steps / (ms * 1e-3)
+
+    # roofline of the fused bucketMul kernel: CUDA events between the kernels of a captured step
+    print(f"[bench] timed {args.steps} tokens in {ms:.2f} ms", file=sys.stderr, flush=True)
+    prof = model.profile_steps(args.effort, n_prof)
+    bm_ms = sum(t for k, t in prof if k == "bucketmul")
+    all_ms = sum(t for _, t in prof)
+    by_kind = {}
+    for k, t in prof:
+        by_kind[k] = by_kind.get(k, 0.0) + t
+    total_bytes = model.step_bytes(ctx_end + n_prof)
+    lm_bytes = 2 * cfg.vocab * cfg.dim
+    kv_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * (ctx_end + n_prof) * cfg.head_dim * 2
+    bm_bytes = total_bytes - lm_bytes - kv_bytes
+    peak, peak_kind = measured_peaks()
+    achieved = bm_bytes / (bm_ms * 1e-3) / 1e9
+
+    # effort sweep (same graph machinery, fewer tokens)
+    sweep_res = {}
+    for e in sweep:
+        model.generate(-1, 0, 2, e, toks)  # capture for this effort
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        model.generate(-1, 0, n_sweep, e, toks)
+        b.record(stream)
+        torch.cuda.synchronize()
+        sweep_res[str(e)] = round(n_sweep / (a.elapsed_time(b) * 1e-3), 1)
+    sweep_res[str(args.effort)] = round(args.steps / (ms * 1e-3), 1)
+
+    # e2e: the host API loop -- token in as a launch argument, logits back to pinned memory,
+    # argmax on the host, one synchronisation per token
+    host_logits = torch.empty(cfg.vocab, dtype=torch.float32).pin_memory()
+    tok = int(toks[0].item())
+    pos = int(ctx_end + n_prof + 2 * len(sweep) + n_sweep * len(sweep))
+    pos = min(pos, max_ctx - n_e2e - 1)
+    torch.cuda.synchronize()
+    e0 = time.perf_counter()
+    for i in range(n_e2e):
+        model.forward(tok, pos + i, args.effort, logits)
+        host_logits.copy_(logits, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        tok = int(np.argmax(host_logits.numpy()))
+    e2e_tok_s = world * n_e2e / (time.perf_counter() - e0)
+
+    res = {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
+                               "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)",
+                   "model": "Mistral-7B (random init)", "effort": args.effort, "global_batch": 1,
+                   "seq_len": ctx_end, "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token",
+                   "tokens_per_s_by_effort": sweep_res, "selected_rows_per_step": sel_rows,
+                   "algorithmic_bytes_per_step": step_bytes,
+                   "step_effective_GBps": round(step_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
+                   "model_build_s": round(build_s, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "kernel": "bm_fused_kernel", "bytes_per_launch": int(bm_bytes / (4 * cfg.n_layers)),
+                     "kernel_ms_per_step": round(bm_ms, 4), "step_ms_events": round(all_ms, 4),
+                     "ms_per_step_by_kernel": {k: round(v, 4) for k, v in by_kind.items()}},
+        "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * cfg.vocab},
+        "gpu_launches": args.steps * (2 + 5 * cfg.n_layers + 2),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_decode(model, cfg, args.effort, budget_s=args.cpu_seconds)
+    model.close()
+    return res
+
+
+def cpu_baseline_decode(model, cfg, effort, budget_s=10.0, steps=None):
+    """The oracle decode step (CPU restatement of the reference's kernels) on the same
+    weights, every host thread, continuing the same prompt."""
+    sys.path.insert(0, ROOT)
+    from oracle import ora
+    threads = os.cpu_count() or 1
+    om = ora.OracleModel(cfg.as_dict(), model.export_weights())
+    prompt = prompt_tokens(cfg.vocab)
+    t_pre = time.perf_counter()
+    tok = prompt[0]
+    ingest = 4  # a short prefix of the prompt keeps the sample bounded
+    for pos in range(ingest):
+        tok, _, _ = om.forward(prompt[pos], pos, effort, nthreads=threads)
+    t0 = time.perf_counter()
+    done = 0
+    pos = ingest
+    while True:
+        tok, _, _ = om.forward(tok, pos, effort, nthreads=threads)
+        pos += 1
+        done += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and done >= steps) or (steps is None and el >= budget_s):
+            break
+    return {"value": round(done / el, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{done} greedy decode steps of the same 32-layer model after a {ingest}-token prefix, "
+                      f"{el:.1f} s", "seconds": round(el, 2), "setup_s": round(t0 - t_pre, 1)}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the oracle port of the reference's kernels on the host cores."""
     if rank != 0:
         return None
+    if args.workload == "decode":
+        import torch
+        iam = load_pkg()
+        cfg = mistral_cfg(iam, PROMPT_LEN + 64)
+        model = iam.Model.random(cfg, seed=0)
+        steps = max(1, min(args.steps, 12))
+        cb = cpu_baseline_decode(model, cfg, args.effort, steps=steps)
+        model.close()
+        return {
+            "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * cb["seconds"] / steps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "decode: config 4 on the CPU restatement (oracle) of the reference kernels",
+                       "model": "Mistral-7B (random init)", "effort": args.effort, "global_batch": 1},
+            "cpu_baseline": {"value": cb["value"], "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
+                             "sample": cb["sample"]},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
     import torch
     iam = load_pkg()
     dev = torch.device("cuda:0") if torch.cuda.is_available() else None
@@ -292,10 +478,11 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="bucketmul", choices=["bucketmul"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "bucketmul"])
+    ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--effort", type=float, default=0.25)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -312,6 +499,8 @@ def main():
     try:
         if args.impl == "reference":
             res = run_reference(args, rank, world)
+        elif args.workload == "decode":
+            res = run_decode(args, rank, world)
         else:
             res = run_bucketmul(args, rank, world)
         if rank == 0 and res is not None:

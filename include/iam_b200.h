@@ -156,9 +156,18 @@ int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* lo
 /* Greedy generation on the device (the decode loop of test_generation.cpp:239-291 without
  * host round trips): step 0 decodes first_token at start_pos, every later step decodes the
  * previous step's argmax; the n_tokens generated ids land in tokens_dev.  Steps after the
- * first replay one captured CUDA graph. */
+ * first replay one captured CUDA graph.  first_token < 0 continues from the device position
+ * and the last argmax (start_pos is then ignored), replaying the graph for every step. */
 int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort,
                        int* tokens_dev, void* stream);
+/* Diagnostics: decodes `steps` greedy tokens (continuing from the device position and the
+ * last argmax) through one captured graph with a CUDA event between consecutive kernels.
+ * kernel_ms[k] (capacity entries) receives the average device time of launch k of a step and
+ * kinds[k] its IAM_KERNEL_* kind; *n_kernels the launches per step.  Advances the position. */
+enum { IAM_KERNEL_EMBED = 0, IAM_KERNEL_BUCKETMUL = 1, IAM_KERNEL_ATTENTION = 2, IAM_KERNEL_LM_HEAD = 3,
+       IAM_KERNEL_OTHER = 4 };
+int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kernel_ms, int* kinds,
+                            int capacity, int* n_kernels, void* stream);
 /* KV cache contents of one layer: k/v [n_kv_heads][n_tokens][head_dim] fp16 (post-RoPE k). */
 int iam_model_set_kv(iam_model_t m, int layer, const uint16_t* k_dev, const uint16_t* v_dev,
                      int n_tokens, void* stream);

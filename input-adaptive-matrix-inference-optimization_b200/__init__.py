@@ -197,7 +197,9 @@ _SIGNATURES.update({
     "iam_model_read_weight": [_vp, _i32, _i32, _vp, ctypes.c_size_t, _vp],
     "iam_model_selected_rows": [_vp, _vp],
     "iam_model_step_bytes": [_vp, _i32, _vp],
+    "iam_model_profile_steps": [_vp, _f32, _i32, _vp, _vp, _i32, _vp, _vp],
 })
+KERNEL_KINDS = ("embed", "bucketmul", "attention", "lm_head", "other")
 
 
 class Model:
@@ -266,6 +268,16 @@ class Model:
         t = ctypes.c_longlong()
         check(self.lib.iam_model_step_bytes(self.h, context, ctypes.byref(t)))
         return t.value
+
+    def profile_steps(self, effort, steps, stream=None):
+        """-> list of (kind, avg_ms) per launch of one decode step (diagnostics; advances pos)."""
+        cap = 4096
+        ms = (ctypes.c_float * cap)()
+        kinds = (ctypes.c_int * cap)()
+        n = ctypes.c_int()
+        check(self.lib.iam_model_profile_steps(self.h, effort, steps, ms, kinds, cap, ctypes.byref(n),
+                                               _stream(stream)))
+        return [(KERNEL_KINDS[kinds[k]], ms[k]) for k in range(n.value)]
 
     def export_weights(self):
         """Host copy of every weight in the oracle's layout (tests use it as the checker's input)."""

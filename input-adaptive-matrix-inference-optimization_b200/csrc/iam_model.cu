@@ -409,9 +409,29 @@ int build_plans(iam_model_s* m, float effort) {
     return IAM_OK;
 }
 
+// Optional per-launch CUDA events (diagnostics): an event is recorded before every launch
+// together with the kind of the launch that follows, and once after the last launch.
+struct StepHooks {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kinds;
+};
+
+int hook(StepHooks* h, int kind, cudaStream_t s) {
+    if (!h) return IAM_OK;
+    cudaEvent_t e;
+    IAM_CUDA_TRY(cudaEventCreate(&e));
+    h->ev.push_back(e);
+    h->kinds.push_back(kind);
+    // external record: inside a stream capture this becomes an event-record node that the
+    // host can time after the graph ran (a plain record would only order the capture)
+    IAM_CUDA_TRY(cudaEventRecordWithFlags(e, s, cudaEventRecordExternal));
+    return IAM_OK;
+}
+
 // token: token_arg (>= 0), or the previous argmax when token_arg < 0.  pos: pos_arg (>= 0)
 // is written to the device first, else the device value is used.
-int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float* logits, cudaStream_t s) {
+int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float* logits, cudaStream_t s,
+                 StepHooks* hk = nullptr) {
     const iam_model_config& c = m->cfg;
     int rc = build_plans(m, effort);
     if (rc) return rc;
@@ -419,11 +439,13 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         set_int_kernel<<<1, 1, 0, s>>>(m->pos, pos_arg);
         IAM_CUDA_TRY(cudaGetLastError());
     }
+    if ((rc = hook(hk, IAM_KERNEL_EMBED, s))) return rc;
     if ((rc = launch_embed(m->embed, c.dim, token_arg, token_arg < 0 ? m->key : nullptr, nullptr, m->x, m->key,
                            m->token_used, s)))
         return rc;
     const int gq = c.n_heads / c.n_kv_heads;
     for (int l = 0; l < c.n_layers; ++l) {
+        if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
         if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->G, s))) return rc;
         AttnParams ap{};
         ap.q = m->q;
@@ -442,10 +464,12 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         ap.max_ctx = c.max_ctx;
         ap.n_split = m->att_split;
         ap.chunk_cap = m->chunk_cap;
+        if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
         if ((rc = launch_attention(ap, gq, s))) return rc;
-        if ((rc = bm_launch(m->plans[l * 4 + 1], m->vec, m->G, s))) return rc;
-        if ((rc = bm_launch(m->plans[l * 4 + 2], m->vec, m->G, s))) return rc;
-        if ((rc = bm_launch(m->plans[l * 4 + 3], m->vec, m->G, s))) return rc;
+        for (int b = 1; b < 4; ++b) {
+            if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
+            if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->G, s))) return rc;
+        }
     }
     LMHeadParams hp{};
     hp.W = m->lm_head;
@@ -456,6 +480,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     hp.rows = c.vocab;
     hp.logits = logits;
     hp.argmax_key = m->key;
+    if ((rc = hook(hk, IAM_KERNEL_LM_HEAD, s))) return rc;
     return launch_lm_head(hp, 2 * m->sm_count, s);
 }
 
@@ -606,19 +631,26 @@ int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* lo
 int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort, int* tokens_dev,
                        void* stream) {
     if (!m || !tokens_dev) return fail(IAM_ERR_ARG, "iam_model_generate: null argument");
-    if (first_token < 0 || first_token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_generate: bad token");
-    if (start_pos < 0 || n_tokens < 0 || start_pos + n_tokens > m->cfg.max_ctx)
+    const bool cont = first_token < 0;  // continue from the device position and last argmax
+    if (first_token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_generate: bad token");
+    if (!cont && (start_pos < 0 || start_pos + n_tokens > m->cfg.max_ctx))
         return fail(IAM_ERR_ARG, "iam_model_generate: positions exceed max_ctx");
+    if (n_tokens < 0) return fail(IAM_ERR_ARG, "iam_model_generate: negative n_tokens");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_generate: effort must be in (0, 1]");
     cudaStream_t s = (cudaStream_t)stream;
     if (n_tokens == 0) return IAM_OK;
-    // step 0 from the given token (eager), then one captured step replayed per token; each
-    // step appends its greedy token to tokens_dev[gen_count++] and advances pos on device
+    // step 0 from the given token (eager) unless continuing, then one captured step replayed
+    // per token; each step appends its greedy token to tokens_dev[gen_count++] and advances
+    // pos on the device
     IAM_CUDA_TRY(cudaMemsetAsync(m->gen_count, 0, sizeof(int), s));
-    int rc = enqueue_step(m, first_token, start_pos, effort, m->logits, s);
-    if (rc) return rc;
-    if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s))) return rc;
-    if (n_tokens == 1) return IAM_OK;
+    int rc = IAM_OK;
+    int done = 0;
+    if (!cont) {
+        if ((rc = enqueue_step(m, first_token, start_pos, effort, m->logits, s))) return rc;
+        if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s))) return rc;
+        done = 1;
+        if (n_tokens == 1) return IAM_OK;
+    }
     if (!m->gen_graph || m->gen_effort != effort || m->gen_tokens != tokens_dev) {
         if (m->gen_graph) {
             cudaGraphExecDestroy(m->gen_graph);
@@ -641,7 +673,53 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
         m->gen_effort = effort;
         m->gen_tokens = tokens_dev;
     }
-    for (int i = 1; i < n_tokens; ++i) IAM_CUDA_TRY(cudaGraphLaunch(m->gen_graph, s));
+    for (int i = done; i < n_tokens; ++i) IAM_CUDA_TRY(cudaGraphLaunch(m->gen_graph, s));
+    return IAM_OK;
+}
+
+int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kernel_ms, int* kinds, int capacity,
+                            int* n_kernels, void* stream) {
+    if (!m || steps <= 0 || !n_kernels) return fail(IAM_ERR_ARG, "iam_model_profile_steps: bad arguments");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_profile_steps: effort must be in (0, 1]");
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc = build_plans(m, effort);
+    if (rc) return rc;
+    StepHooks hk;
+    cudaStream_t cap;
+    IAM_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        rc = enqueue_step(m, -1, -1, effort, m->logits, cap, &hk);
+        if (!rc) rc = hook(&hk, IAM_KERNEL_OTHER, cap);
+        if (!rc) rc = launch_advance(m->pos, m->key, nullptr, nullptr, cap);
+        if (!rc) rc = hook(&hk, IAM_KERNEL_OTHER, cap);
+        e = cudaStreamEndCapture(cap, &graph);
+    }
+    if (e == cudaSuccess && !rc) e = cudaGraphInstantiate(&exec, graph, 0);
+    const int nk = (int)hk.ev.size() - 1;
+    std::vector<double> acc(nk > 0 ? nk : 0, 0.0);
+    for (int it = 0; it < steps && e == cudaSuccess && !rc; ++it) {
+        e = cudaGraphLaunch(exec, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        for (int k = 0; k < nk && e == cudaSuccess; ++k) {
+            float ms = 0.0f;
+            e = cudaEventElapsedTime(&ms, hk.ev[k], hk.ev[k + 1]);
+            acc[k] += ms;
+        }
+    }
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    cudaStreamDestroy(cap);
+    for (cudaEvent_t ev : hk.ev) cudaEventDestroy(ev);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "iam_model_profile_steps");
+    *n_kernels = nk;
+    for (int k = 0; k < nk && k < capacity; ++k) {
+        if (kernel_ms) kernel_ms[k] = (float)(acc[k] / steps);
+        if (kinds) kinds[k] = hk.kinds[k];
+    }
     return IAM_OK;
 }
 
