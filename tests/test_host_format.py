@@ -74,3 +74,22 @@ def test_library_exports_every_declared_symbol(iam):
 
 def test_python_binding_covers_header(iam):
     assert set(_declared_symbols()) <= set(iam.exported_symbols()) | {"iam_model_forward_tokens"}
+
+
+def test_cpp_shim_compiles(tmp_path):
+    """include/iam_b200.hpp (the reference's class names over the C ABI) compiles as C++17."""
+    import shutil
+    import subprocess
+    cuda_inc = "/usr/local/cuda/include"
+    cxx = shutil.which("g++")
+    if not cxx or not os.path.isdir(cuda_inc):
+        pytest.skip("no host C++ compiler or CUDA headers")
+    src = tmp_path / "shim.cpp"
+    src.write_text('#include "iam_b200.hpp"\n'
+                   'int main() {\n'
+                   '  iam_model_config c = iam_shim::MistralModel::mistral7b(32000, 4096);\n'
+                   '  return c.dim == 4096 ? 0 : 1;\n'
+                   '}\n')
+    r = subprocess.run([cxx, "-std=c++17", "-fsyntax-only", "-Wall", "-I", os.path.join(ROOT, "include"),
+                        "-I", cuda_inc, str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
