@@ -111,6 +111,22 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
  * and min/max done, [9] bisection done.  NULL turns it off. */
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev);
 
+/* iam_bucketmul_full without any device allocation, for callers that cannot allocate device
+ * memory (inside an allocator or memory-pool callback, or a plug-in whose host framework owns
+ * every device allocation).  It has no counterpart in the reference, whose BucketMul
+ * allocates its scratch in the singleton's constructor.  Same arguments and results as
+ * iam_bucketmul_full minus the handle; its scratch is a ~1 MiB __device__ array built into
+ * the library, held by every GPU that loads it until exit.
+ * Limits: bucket_cols <= 1024 (out_dim <= 16384), else IAM_ERR_ARG.
+ * The first call on a device looks up that array's device address (cudaGetSymbolAddress),
+ * so make the first call on each device before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (different streams, or
+ * threads without ordering) race and corrupt each other's results; serialise them. */
+int iam_bucketmul_full_noalloc(const float* x_dev, const uint16_t* stats_dev, int stats_stride,
+                               const uint16_t* probes_dev, const uint16_t* buckets_dev, int expert_no,
+                               int in_dim, int bucket_cols, int expert_size, float effort, float* out_dev,
+                               int* count_dev, float* cutoff_dev, void* stream);
+
 /* Packs channel 3 of a [rows][4] stats array into [rows] (stats_stride = 1 layout). */
 int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_dev, void* stream);
 

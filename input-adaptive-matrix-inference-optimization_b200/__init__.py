@@ -40,6 +40,7 @@ _SIGNATURES = {
     "iam_bucketmul_mul": [_vp, _vp, _i32, _i32, _vp, _vp],
     "iam_bucketmul_full": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_bucketmul_phase_times": [_vp, _vp],
+    "iam_bucketmul_full_noalloc": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_stats_pack": [_vp, _i64, _vp, _vp],
     "iam_bucketize": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
 }
@@ -141,6 +142,15 @@ class BucketMul:
         check(self.lib.iam_bucketmul_full(self.h, _ptr(x), _ptr(stats), stats_stride, _ptr(probes),
                                           _ptr(buckets), expert_no, in_size, bucket_cols, expert_size, effort,
                                           _ptr(out), _ptr(count), _ptr(cutoff), _stream(stream)))
+
+
+def bucketmul_full_noalloc(x, stats, probes, buckets, expert_no, in_size, bucket_cols, expert_size, effort, out,
+                           stats_stride=4, count=None, cutoff=None, stream=None):
+    """iam_bucketmul_full_noalloc: fullMul with the library's built-in scratch (no device
+    allocation; calls must not overlap on the GPU; bucket_cols <= 1024)."""
+    check(load_library().iam_bucketmul_full_noalloc(_ptr(x), _ptr(stats), stats_stride, _ptr(probes), _ptr(buckets),
+                                                    expert_no, in_size, bucket_cols, expert_size, effort, _ptr(out),
+                                                    _ptr(count), _ptr(cutoff), _stream(stream)))
 
 
 def plan_info(vec, cluster, bucket_cols, in_dim):

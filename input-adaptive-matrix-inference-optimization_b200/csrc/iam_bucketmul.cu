@@ -477,7 +477,7 @@ int bm_default_cluster() {
 // VEC columns, i.e. 256 or 512 B of each row per tile), then as many input splits as its
 // share of the resident clusters (by selected-row work) allows, so the batch is one full
 // wave; splits are raised further if a CTA's input segment would not fit shared memory.
-void bm_plan(BMBatch& b, int vec, int G, int max_clusters) {
+void bm_plan(BMBatch& b, int vec, int G, int max_clusters, int max_splits) {
     const int forced_l2 = env_int("IAM_BM_LOG2L", -1);
     const int forced_k = env_int("IAM_BM_SPLIT", -1);
     double work_total = 0.0;
@@ -498,13 +498,14 @@ void bm_plan(BMBatch& b, int vec, int G, int max_clusters) {
             K = std::max(1, (int)(share / p.n_tiles));
             if (forced_k > 0) K = forced_k;
             K = std::min(K, std::max(1, inputs / G));  // at least one input per CTA
-            K = std::min(K, kMaxSplits);
+            K = std::min(K, std::min(max_splits, kMaxSplits));
         }
         int seg;
         for (;;) {
             const int span = (inputs + K - 1) / K;
             seg = (span + G - 1) / G;
-            if ((seg <= kMaxSegInputs && bm_smem_bytes(vec, seg) <= 227 * 1024) || K >= kMaxSplits) break;
+            if ((seg <= kMaxSegInputs && bm_smem_bytes(vec, seg) <= 227 * 1024) || K >= std::min(max_splits, kMaxSplits))
+                break;
             ++K;
         }
         p.n_split = K;

@@ -82,7 +82,7 @@ struct BMScratch {
 int bm_default_cluster();
 int bm_max_active_clusters(int vec, int G);
 size_t bm_smem_bytes(int vec, int seg_inputs);
-void bm_plan(BMBatch& b, int vec, int G, int max_clusters);
+void bm_plan(BMBatch& b, int vec, int G, int max_clusters, int max_splits = kMaxSplits);
 int bm_total_clusters(const BMBatch& b);
 int bm_launch(const BMBatch& b, int vec, int G, cudaStream_t s);
 int bm_launch_cutoff(const float* x, const uint16_t* probes, int P, int target, float* out, int* iters,

@@ -2,6 +2,7 @@
 // Declarations and the reference interface each one replaces: include/iam_b200.h.
 #include <cmath>
 #include <cstdlib>
+#include <mutex>
 #include <cstring>
 #include <string>
 
@@ -314,3 +315,98 @@ int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buck
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation variant
+//
+// Some callers of a bucketMul cannot allocate device memory at all: code that runs inside a
+// host-side allocator or memory-pool callback, a plug-in whose host framework owns every
+// device allocation and forbids its plug-ins from calling cudaMalloc, or a context where an
+// allocation would synchronise the device at the wrong moment.  For them the fused
+// bucketMul's scratch (the partial tiles of the input splits, the arrival counters and the
+// per-split selected counts) lives in one file-scope __device__ array instead of a handle.
+// The array is part of the module: every GPU that loads the library holds its ~1 MiB until
+// the process exits.
+
+namespace {
+
+constexpr int kNoAllocMaxCols = 1024;  // bucket columns, i.e. out_dim <= 16384
+constexpr int kNoAllocMaxSplits = 16;  // input splits the plan may use
+constexpr int kNoAllocCtrSlots = 1024; // column tiles x cluster size
+constexpr size_t kNoAllocPartials = (size_t)kNoAllocMaxSplits * 16 * kNoAllocMaxCols;  // floats
+constexpr size_t kNoAllocFloats = kNoAllocPartials + kNoAllocCtrSlots + kNoAllocMaxSplits;
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
+
+// Device address of g_noalloc_scratch on the current device (set up once per device; the
+// host-side name is only a stand-in for the symbol and must never reach a kernel).
+int noalloc_scratch(float** out) {
+    static std::mutex mu;
+    static float* addr[256] = {};
+    int dev = 0;
+    IAM_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 256) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full_noalloc: device index >= 256");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "iam_bucketmul_full_noalloc: cudaGetSymbolAddress");
+        addr[dev] = static_cast<float*>(p);
+    }
+    *out = addr[dev];
+    return IAM_OK;
+}
+
+}  // namespace
+
+extern "C" int iam_bucketmul_full_noalloc(const float* x_dev, const uint16_t* stats_dev, int stats_stride,
+                                          const uint16_t* probes_dev, const uint16_t* buckets_dev, int expert_no,
+                                          int in_dim, int bucket_cols, int expert_size, float effort, float* out_dev,
+                                          int* count_dev, float* cutoff_dev, void* stream) {
+    if (!x_dev || !stats_dev || !probes_dev || !buckets_dev || !out_dev)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: null input, stats, probes, buckets or output");
+    if (in_dim <= 0 || bucket_cols <= 0 || expert_size <= 0 || expert_no < 0)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: in_dim, bucket_cols, expert_size must be > 0");
+    if (bucket_cols > kNoAllocMaxCols)
+        return fail(IAM_ERR_ARG,
+                    "iam_bucketmul_full_noalloc: bucket_cols exceeds the built-in scratch (at most 1024 bucket "
+                    "columns, i.e. out_dim <= 16384); use iam_bucketmul_full");
+    if (stats_stride != 1 && stats_stride != 4)
+        return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: stats_stride must be 1 or 4");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: effort must be in (0, 1]");
+    float* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    const int G = bm_default_cluster();
+    BMBatch b;
+    memset(&b, 0, sizeof(b));
+    BMProblem& p = b.p[0];
+    p.x = x_dev;
+    p.stats = stats_dev;
+    p.stats_stride = stats_stride;
+    p.probes = probes_dev + (size_t)expert_no * IAM_PROBES_COUNT;
+    p.buckets = buckets_dev;
+    p.row0 = (long long)expert_size * expert_no;
+    p.n_rows_valid = expert_size < 16 * in_dim ? expert_size : 16 * in_dim;
+    p.n_inputs = (p.n_rows_valid + 15) / 16;
+    p.cols = bucket_cols;
+    p.P = in_dim < IAM_PROBES_COUNT ? in_dim : IAM_PROBES_COUNT;
+    p.target = bm_target(effort, p.P);
+    p.out = out_dev;
+    p.count_out = count_dev;
+    p.cutoff_out = cutoff_dev;
+    p.partials = scratch;
+    p.slice_ctr = reinterpret_cast<int*>(scratch + kNoAllocPartials);
+    p.split_sel = reinterpret_cast<int*>(scratch + kNoAllocPartials + kNoAllocCtrSlots);
+    if ((p.row0 + p.n_rows_valid) * (long long)bucket_cols >= (1LL << 31))
+        return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full_noalloc: rows * bucket_cols must stay below 2^31");
+    b.nprob = 1;
+    b.mode = kModeFused;
+    const int vec = pick_vec(b);
+    bm_plan(b, vec, G, bm_max_active_clusters(vec, G), kNoAllocMaxSplits);
+    if (p.n_tiles * G > kNoAllocCtrSlots)
+        return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full_noalloc: too many column tiles for the scratch");
+    // the arrival counters must start at zero (a launch leaves them at zero, but a call that
+    // failed before its kernel ran, or a kernel error, would not)
+    IAM_CUDA_TRY(cudaMemsetAsync(p.slice_ctr, 0, sizeof(int) * kNoAllocCtrSlots, (cudaStream_t)stream));
+    return bm_launch(b, vec, G, (cudaStream_t)stream);
+}
