@@ -8,6 +8,7 @@
 //     aux.cl:454-490) and the greedy argmax of the driver (test_generation.cpp:276).
 // RMSNorm, SiLU and the residual adds live inside the bucketMul kernel (input providers and
 // epilogue); see iam_bucketmul.cu.
+#include <algorithm>
 #include <cfloat>
 
 #include "iam_bucketmul.cuh"
@@ -47,69 +48,114 @@ IAM_DEV float rope_at(const float* m, const float* cs, int d, int half) {
     return __fadd_rn(__fmul_rn(m[d], c), __fmul_rn(m[d - half], s));
 }
 
-// grid = n_kv_heads * n_split, block = kAttnThreads.  CTA (kvh, s) handles context tokens
-// [s*chunk, (s+1)*chunk) for the GQ query heads that share KV head kvh.
-template <int GQ>
+// Loads VD consecutive fp16 values (VD = head_dim / 32 per lane) as floats.
+template <int VD>
+IAM_DEV void load_half_vec(const uint16_t* p, float* o) {
+    if constexpr (VD == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        o[0] = h2f(v.x & 0xffffu);
+        o[1] = h2f(v.x >> 16);
+        o[2] = h2f(v.y & 0xffffu);
+        o[3] = h2f(v.y >> 16);
+    } else if constexpr (VD == 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+        o[0] = h2f(v & 0xffffu);
+        o[1] = h2f(v >> 16);
+    } else {
+#pragma unroll
+        for (int e = 0; e < VD; ++e) o[e] = h2f(p[e]);
+    }
+}
+
+// grid = n_kv_heads * n_split, block = kAttnThreads.  The context [0, pos] is cut into
+// `active` chunks of at least kAttnMinChunk tokens (active <= n_split); CTA (kvh, s < active)
+// handles chunk s for the GQ query heads that share KV head kvh: warps take tokens round
+// robin, each lane holds head_dim/32 dimensions, kAttnTU tokens in flight per warp.  The
+// last of the active CTAs of a KV head combines the chunks in chunk order.
+template <int GQ, int VD>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
-    const int hd = p.head_dim, half = hd / 2;
+    constexpr int HD = 32 * VD;
+    constexpr int NWA = kAttnThreads / 32;
+    constexpr int TU = kAttnTU;
+    const int half = HD / 2;
     const int kvh = blockIdx.x / p.n_split, s = blockIdx.x % p.n_split;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int NWA = kAttnThreads / 32;
     const int pos = *p.pos_dev;
     const int n_tok = pos + 1;
-    const int chunk = (n_tok + p.n_split - 1) / p.n_split;
-    const int t0 = min(s * chunk, n_tok), t1 = min(t0 + chunk, n_tok);
+    int chunk = (n_tok + p.n_split - 1) / p.n_split;
+    if (chunk < kAttnMinChunk) chunk = kAttnMinChunk;
+    const int active = (n_tok + chunk - 1) / chunk;
+    if (s >= active) return;  // takes no part in the combine
+    const int t0 = s * chunk, t1 = min(t0 + chunk, n_tok);
     const int nt = t1 - t0;
 
-    float* qr = sm;                  // [GQ][hd] roped queries
-    float* knew = qr + GQ * hd;      // [hd] roped k at pos, rounded through fp16
-    float* vnew = knew + hd;         // [hd] v at pos, rounded through fp16
-    float* sc = vnew + hd;           // [GQ][chunk_cap] scores, then probabilities
-    const float* cs = p.rope + (size_t)pos * hd;  // [hd/2][2]
+    float* qr = sm;                   // [GQ][HD] roped queries
+    float* knew = qr + GQ * HD;       // [HD] roped k at pos, rounded through fp16
+    float* vnew = knew + HD;          // [HD] v at pos, rounded through fp16
+    float* sc = vnew + HD;            // [GQ][chunk_cap] scores, then exp(score - max)
+    float* red = sc + GQ * p.chunk_cap;  // [NWA][GQ][HD] per-warp partial p.V
+    const float* cs = p.rope + (size_t)pos * HD;
 
-    for (int e = tid; e < GQ * hd; e += kAttnThreads) {
-        const int j = e / hd, d = e % hd;
-        qr[e] = rope_at(p.q + (size_t)(kvh * GQ + j) * hd, cs, d, half);
+    for (int e = tid; e < GQ * HD; e += kAttnThreads) {
+        const int j = e / HD, d = e % HD;
+        qr[e] = rope_at(p.q + (size_t)(kvh * GQ + j) * HD, cs, d, half);
     }
-    for (int d = tid; d < hd; d += kAttnThreads) {
-        knew[d] = __half2float(__float2half_rn(rope_at(p.k + (size_t)kvh * hd, cs, d, half)));
-        vnew[d] = __half2float(__float2half_rn(p.v[(size_t)kvh * hd + d]));
+    for (int d = tid; d < HD; d += kAttnThreads) {
+        knew[d] = __half2float(__float2half_rn(rope_at(p.k + (size_t)kvh * HD, cs, d, half)));
+        vnew[d] = __half2float(__float2half_rn(p.v[(size_t)kvh * HD + d]));
     }
-    uint16_t* kc = p.k_cache + (size_t)kvh * p.max_ctx * hd;
-    uint16_t* vc = p.v_cache + (size_t)kvh * p.max_ctx * hd;
+    uint16_t* kc = p.k_cache + (size_t)kvh * p.max_ctx * HD;
+    uint16_t* vc = p.v_cache + (size_t)kvh * p.max_ctx * HD;
     __syncthreads();
     if (pos >= t0 && pos < t1) {  // the CTA whose chunk holds pos appends the new k/v
-        for (int d = tid; d < hd; d += kAttnThreads) {
-            kc[(size_t)pos * hd + d] = __half_as_ushort(__float2half_rn(knew[d]));
-            vc[(size_t)pos * hd + d] = __half_as_ushort(__float2half_rn(vnew[d]));
+        for (int d = tid; d < HD; d += kAttnThreads) {
+            kc[(size_t)pos * HD + d] = __half_as_ushort(__float2half_rn(knew[d]));
+            vc[(size_t)pos * HD + d] = __half_as_ushort(__float2half_rn(vnew[d]));
         }
     }
+    float qv[GQ][VD];
+#pragma unroll
+    for (int j = 0; j < GQ; ++j)
+#pragma unroll
+        for (int e = 0; e < VD; ++e) qv[j][e] = qr[j * HD + lane * VD + e];
+    const float scale_div = sqrtf((float)HD);
 
-    // scores: one warp per token, lanes split the head dimension
-    const float inv = sqrtf((float)hd);
-    for (int t = warp; t < nt; t += NWA) {
-        const int tok = t0 + t;
-        float dot[GQ];
+    // scores: q.k / sqrt(head_dim), TU tokens per warp in flight
+    for (int tb = warp * TU; tb < nt; tb += NWA * TU) {
+        float kv[TU][VD];
 #pragma unroll
-        for (int j = 0; j < GQ; ++j) dot[j] = 0.0f;
-        for (int d = lane; d < hd; d += 32) {
-            const float kv = (tok == pos) ? knew[d] : h2f(kc[(size_t)tok * hd + d]);
+        for (int u = 0; u < TU; ++u) {
+            const int t = tb + u;
+            if (t < nt) {
+                if (t0 + t == pos) {
 #pragma unroll
-            for (int j = 0; j < GQ; ++j) dot[j] = fmaf(qr[j * hd + d], kv, dot[j]);
+                    for (int e = 0; e < VD; ++e) kv[u][e] = knew[lane * VD + e];
+                } else {
+                    load_half_vec<VD>(kc + (size_t)(t0 + t) * HD + lane * VD, kv[u]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < VD; ++e) kv[u][e] = 0.0f;
+            }
         }
 #pragma unroll
-        for (int j = 0; j < GQ; ++j) {
-            float v = dot[j];
+        for (int u = 0; u < TU; ++u) {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) sc[j * p.chunk_cap + t] = __fdiv_rn(v, inv);  // q.k / sqrt(hd)
+            for (int j = 0; j < GQ; ++j) {
+                float dsum = 0.0f;
+#pragma unroll
+                for (int e = 0; e < VD; ++e) dsum = fmaf(qv[j][e], kv[u][e], dsum);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+                if (lane == 0 && tb + u < nt) sc[j * p.chunk_cap + tb + u] = __fdiv_rn(dsum, scale_div);
+            }
         }
     }
     __syncthreads();
 
-    // per head: max, exp, sum (one warp per head)
-    float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (hd + 2);
+    // per head: max and sum of exp over the chunk (one warp per head)
+    float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (HD + 2);
     for (int j = warp; j < GQ; j += NWA) {
         float m = -INFINITY;
         for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[j * p.chunk_cap + t]);
@@ -117,54 +163,95 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.0f;
         for (int t = lane; t < nt; t += 32) {
-            const float e = nt ? expf(sc[j * p.chunk_cap + t] - m) : 0.0f;
+            const float e = expf(sc[j * p.chunk_cap + t] - m);
             sc[j * p.chunk_cap + t] = e;
             l += e;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         if (lane == 0) {
-            stat[j * (hd + 2)] = m;
-            stat[j * (hd + 2) + 1] = l;
+            stat[j * (HD + 2)] = m;
+            stat[j * (HD + 2) + 1] = l;
         }
     }
     __syncthreads();
 
-    // unnormalised p.V for the chunk
-    for (int e = tid; e < GQ * hd; e += kAttnThreads) {
-        const int j = e / hd, d = e % hd;
-        float o = 0.0f;
-        for (int t = 0; t < nt; ++t) {
-            const int tok = t0 + t;
-            const float vv = (tok == pos) ? vnew[d] : h2f(vc[(size_t)tok * hd + d]);
-            o = fmaf(sc[j * p.chunk_cap + t], vv, o);
+    // unnormalised p.V: warps take tokens round robin, lanes hold VD dims of GQ heads
+    float o[GQ][VD];
+#pragma unroll
+    for (int j = 0; j < GQ; ++j)
+#pragma unroll
+        for (int e = 0; e < VD; ++e) o[j][e] = 0.0f;
+    for (int tb = warp * TU; tb < nt; tb += NWA * TU) {
+        float vv[TU][VD];
+#pragma unroll
+        for (int u = 0; u < TU; ++u) {
+            const int t = tb + u;
+            if (t < nt && t0 + t != pos) {
+                load_half_vec<VD>(vc + (size_t)(t0 + t) * HD + lane * VD, vv[u]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < VD; ++e) vv[u][e] = (t < nt) ? vnew[lane * VD + e] : 0.0f;
+            }
         }
-        stat[j * (hd + 2) + 2 + d] = o;
+#pragma unroll
+        for (int u = 0; u < TU; ++u) {
+            if (tb + u < nt) {
+#pragma unroll
+                for (int j = 0; j < GQ; ++j) {
+                    const float pw = sc[j * p.chunk_cap + tb + u];
+#pragma unroll
+                    for (int e = 0; e < VD; ++e) o[j][e] = fmaf(pw, vv[u][e], o[j][e]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < GQ; ++j)
+#pragma unroll
+        for (int e = 0; e < VD; ++e) red[(warp * GQ + j) * HD + lane * VD + e] = o[j][e];
+    __syncthreads();
+    for (int e = tid; e < GQ * HD; e += kAttnThreads) {
+        const int j = e / HD, d = e % HD;
+        float acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NWA; ++w) acc += red[(w * GQ + j) * HD + d];
+        stat[j * (HD + 2) + 2 + d] = acc;
     }
 
-    // last CTA of this KV head combines the splits in split order
+    // last active CTA of this KV head combines the chunks in chunk order
     __threadfence();
     __syncthreads();
     __shared__ int last;
-    if (tid == 0) last = (atomicAdd(p.ctr + kvh, 1) == p.n_split - 1);
+    if (tid == 0) last = (atomicAdd(p.ctr + kvh, 1) == active - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const float* base = p.part + (size_t)kvh * p.n_split * GQ * (hd + 2);
-    for (int e = tid; e < GQ * hd; e += kAttnThreads) {
-        const int j = e / hd, d = e % hd;
+    const float* base = p.part + (size_t)kvh * p.n_split * GQ * (HD + 2);
+    float* wgt = red;  // [GQ][active] chunk weights exp(m_r - M) / L
+    for (int j = warp; j < GQ; j += NWA) {
         float M = -INFINITY;
-        for (int r = 0; r < p.n_split; ++r) M = fmaxf(M, __ldcg(base + ((size_t)r * GQ + j) * (hd + 2)));
-        float L = 0.0f, O = 0.0f;
-        for (int r = 0; r < p.n_split; ++r) {
-            const float* st = base + ((size_t)r * GQ + j) * (hd + 2);
-            const float mr = __ldcg(st);
-            if (mr == -INFINITY) continue;
-            const float w = expf(mr - M);
+        for (int r = lane; r < active; r += 32) M = fmaxf(M, __ldcg(base + ((size_t)r * GQ + j) * (HD + 2)));
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+        float L = 0.0f;
+        for (int r = lane; r < active; r += 32) {
+            const float* st = base + ((size_t)r * GQ + j) * (HD + 2);
+            const float w = expf(__ldcg(st) - M);
+            wgt[j * p.n_split + r] = w;
             L = fmaf(w, __ldcg(st + 1), L);
-            O = fmaf(w, __ldcg(st + 2 + d), O);
         }
-        p.out[(size_t)(kvh * GQ + j) * hd + d] = __fdiv_rn(O, L);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        for (int r = lane; r < active; r += 32) wgt[j * p.n_split + r] = __fdiv_rn(wgt[j * p.n_split + r], L);
+    }
+    __syncthreads();
+    for (int e = tid; e < GQ * HD; e += kAttnThreads) {
+        const int j = e / HD, d = e % HD;
+        float O = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < active; ++r) O = fmaf(wgt[j * p.n_split + r], __ldcg(base + ((size_t)r * GQ + j) * (HD + 2) + 2 + d), O);
+        p.out[(size_t)(kvh * GQ + j) * HD + d] = O;
     }
     if (tid == 0) p.ctr[kvh] = 0;  // ready for the next launch
 }
@@ -247,30 +334,39 @@ int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long 
 }
 
 size_t attention_smem(const AttnParams& p, int gq) {
-    return sizeof(float) * ((size_t)gq * p.head_dim + 2 * p.head_dim + (size_t)gq * p.chunk_cap);
+    const int hd = p.head_dim;
+    const size_t red = std::max((size_t)(kAttnThreads / 32) * gq * hd, (size_t)gq * p.n_split);
+    return sizeof(float) * ((size_t)gq * hd + 2 * hd + (size_t)gq * p.chunk_cap + red);
+}
+
+template <int GQ, int VD>
+int launch_attention_t(const AttnParams& p, size_t smem, cudaStream_t s) {
+    auto kern = attention_kernel<GQ, VD>;
+    if (smem > 48 * 1024) IAM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<(unsigned)(p.n_kv_heads * p.n_split), kAttnThreads, smem, s>>>(p);
+    IAM_CUDA_TRY(cudaGetLastError());
+    return IAM_OK;
+}
+
+template <int GQ>
+int launch_attention_g(const AttnParams& p, size_t smem, cudaStream_t s) {
+    switch (p.head_dim) {
+        case 64: return launch_attention_t<GQ, 2>(p, smem, s);
+        case 128: return launch_attention_t<GQ, 4>(p, smem, s);
+        case 256: return launch_attention_t<GQ, 8>(p, smem, s);
+        default: return fail(IAM_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
+    }
 }
 
 int launch_attention(const AttnParams& p, int gq, cudaStream_t s) {
     const size_t smem = attention_smem(p, gq);
-    const dim3 grid((unsigned)(p.n_kv_heads * p.n_split));
     switch (gq) {
-#define IAM_ATTN_CASE(N)                                                                                   \
-    case N:                                                                                                \
-        if (smem > 48 * 1024)                                                                              \
-            IAM_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                              (int)smem));                                                 \
-        attention_kernel<N><<<grid, kAttnThreads, smem, s>>>(p);                                           \
-        break;
-        IAM_ATTN_CASE(1)
-        IAM_ATTN_CASE(2)
-        IAM_ATTN_CASE(4)
-        IAM_ATTN_CASE(8)
-#undef IAM_ATTN_CASE
-        default:
-            return fail(IAM_ERR_UNSUPPORTED, "attention: n_heads / n_kv_heads must be 1, 2, 4 or 8");
+        case 1: return launch_attention_g<1>(p, smem, s);
+        case 2: return launch_attention_g<2>(p, smem, s);
+        case 4: return launch_attention_g<4>(p, smem, s);
+        case 8: return launch_attention_g<8>(p, smem, s);
+        default: return fail(IAM_ERR_UNSUPPORTED, "attention: n_heads / n_kv_heads must be 1, 2, 4 or 8");
     }
-    IAM_CUDA_TRY(cudaGetLastError());
-    return IAM_OK;
 }
 
 int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s) {

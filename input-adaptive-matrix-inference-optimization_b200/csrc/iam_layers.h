@@ -7,6 +7,8 @@
 namespace iam {
 
 constexpr int kAttnThreads = 128;
+constexpr int kAttnTU = 4;          // tokens in flight per warp
+constexpr int kAttnMinChunk = 32;   // context tokens per CTA at least
 constexpr int kHeadThreads = 256;
 
 struct AttnParams {

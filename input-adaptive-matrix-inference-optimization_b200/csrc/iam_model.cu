@@ -139,7 +139,8 @@ int check_cfg(const iam_model_config* c) {
     if (c->n_heads % c->n_kv_heads) return fail(IAM_ERR_ARG, "model: n_heads must be a multiple of n_kv_heads");
     const int gq = c->n_heads / c->n_kv_heads;
     if (gq != 1 && gq != 2 && gq != 4 && gq != 8) return fail(IAM_ERR_UNSUPPORTED, "model: GQA group must be 1/2/4/8");
-    if (c->head_dim % 2 || c->head_dim > 1024) return fail(IAM_ERR_ARG, "model: head_dim must be even and <= 1024");
+    if (c->head_dim != 64 && c->head_dim != 128 && c->head_dim != 256)
+        return fail(IAM_ERR_UNSUPPORTED, "model: head_dim must be 64, 128 or 256");
     if (c->n_heads * c->head_dim % 16 || c->n_kv_heads * c->head_dim % 16 || c->dim % 16 || c->ffn_dim % 16)
         return fail(IAM_ERR_ARG, "model: every projection width must be a multiple of 16");
     if (c->dim % 8 || c->ffn_dim % 8) return fail(IAM_ERR_ARG, "model: dim and ffn_dim must be multiples of 8");
@@ -194,7 +195,15 @@ int alloc_runtime(iam_model_s* m) {
     }
     const int gq = c.n_heads / c.n_kv_heads;
     m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, m->n_kv_local)));
-    m->chunk_cap = (c.max_ctx + m->att_split - 1) / m->att_split;
+    // a CTA scores at most max(ceil(max_ctx / att_split), kAttnMinChunk) tokens
+    m->chunk_cap = std::max((c.max_ctx + m->att_split - 1) / m->att_split, kAttnMinChunk);
+    {
+        AttnParams probe{};
+        probe.head_dim = hd;
+        probe.n_split = m->att_split;
+        probe.chunk_cap = m->chunk_cap;
+        if (attention_smem(probe, gq) > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "model: max_ctx too large for attention");
+    }
     if ((rc = dalloc(m, &m->att_part, (size_t)m->n_kv_local * m->att_split * gq * (hd + 2))) ||
         (rc = dalloc(m, &m->att_ctr, m->n_kv_local)))
         return rc;
