@@ -111,6 +111,13 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
  * and min/max done, [9] bisection done.  NULL turns it off. */
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev);
 
+/* Diagnostics: every CTA c < capacity of later fused launches of `h` writes 8 int64 to
+ * trace_dev[8c .. 8c+7]: globaltimer stamps (ns) [0] start, [1] cutoff done, [2] row lists
+ * done, [3] cluster numbering done, [4] accumulation done, [5] partial tile done, [6] end,
+ * and [7] the number of bucket rows the CTA accumulated.  NULL turns it off.  (No
+ * counterpart in the reference: load-balance evidence for the fused kernel.) */
+int iam_bucketmul_trace(iam_bucketmul_t h, long long* trace_dev, int capacity);
+
 /* iam_bucketmul_full without any device allocation, for callers that cannot allocate device
  * memory (inside an allocator or memory-pool callback, or a plug-in whose host framework owns
  * every device allocation).  It has no counterpart in the reference, whose BucketMul

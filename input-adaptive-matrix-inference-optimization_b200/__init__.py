@@ -40,6 +40,7 @@ _SIGNATURES = {
     "iam_bucketmul_mul": [_vp, _vp, _i32, _i32, _vp, _vp],
     "iam_bucketmul_full": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_bucketmul_phase_times": [_vp, _vp],
+    "iam_bucketmul_trace": [_vp, _vp, ctypes.c_int],
     "iam_bucketmul_full_noalloc": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_stats_pack": [_vp, _i64, _vp, _vp],
     "iam_bucketize": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
@@ -117,6 +118,11 @@ class BucketMul:
     def phase_times(self, times):
         """Diagnostics: later launches write 7 int64 globaltimer stamps into `times`."""
         check(self.lib.iam_bucketmul_phase_times(self.h, _ptr(times)))
+
+    def trace(self, stamps):
+        """Diagnostics: later fused launches write 8 int64 per CTA into `stamps` (None: off)."""
+        cap = 0 if stamps is None else int(stamps.numel()) // 8
+        check(self.lib.iam_bucketmul_trace(self.h, _ptr(stamps), cap))
 
     def cutoff(self, x, probes, in_dim, effort, out, iters=None, expert_no=0, stream=None):
         check(self.lib.iam_bucketmul_cutoff(self.h, _ptr(x), _ptr(probes), expert_no, in_dim, effort,

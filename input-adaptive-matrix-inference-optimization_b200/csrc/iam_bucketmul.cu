@@ -29,7 +29,11 @@
 namespace iam {
 
 constexpr int kCH = 2048;  // rows per staged chunk
-constexpr int kU = 8;      // rows per lane per load group (two groups in flight)
+#ifndef IAM_BM_RING
+#define IAM_BM_RING 8
+#endif
+constexpr int kD = IAM_BM_RING;  // rows per lane in flight (register ring; 8 fits 128 registers)
+constexpr int kSumBatch = 16;  // split partials loaded at once by the last cluster
 
 // Threads per CTA for a vector width: the lane accumulators (16 slots x VEC floats per
 // lane) fill 128 KB of shared memory either way; narrower loads buy more warps.
@@ -57,6 +61,7 @@ constexpr size_t fixed_smem_bytes() {
     constexpr int NT = Threads<VEC>::value;
     return align16(sizeof(FusedHeader<NT>)) + 2 * kCH * sizeof(uint2)  // header, staging
            + sizeof(float) * 16 * VEC * 32                             // partial tile
+           + (16u << SlotShift<VEC>::value)                            // alignment of the accumulators
            + sizeof(float) * NT * VEC * 16;                            // lane accumulators
 }
 
@@ -92,7 +97,7 @@ struct Provider<kXSilu, NT> {
 
 template <int VEC, int XM>
 __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const __grid_constant__ BMBatch batch) {
-    constexpr int NT = Threads<VEC>::value, NW = NT / 32, U = kU;
+    constexpr int NT = Threads<VEC>::value, NW = NT / 32;
     using VL = VecLoad<VEC>;
     using VT = typename VL::T;
     cg::cluster_group cluster = cg::this_cluster();
@@ -107,32 +112,55 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     const int K = pr.n_split;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     long long* dbg = (ci == 0 && g == 0 && tid == 0) ? pr.dbg : nullptr;
+    long long* tr = (pr.trace && tid == 0 && (int)blockIdx.x < pr.trace_cap) ? pr.trace + 8 * blockIdx.x : nullptr;
     stamp(dbg, 0);
+    stamp(tr, 0);
 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FusedHeader<NT>& hdr = *reinterpret_cast<FusedHeader<NT>*>(smem_raw);
     uint2* stage = reinterpret_cast<uint2*>(smem_raw + align16(sizeof(FusedHeader<NT>)));
     float* part = reinterpret_cast<float*>(stage + 2 * kCH);
-    float* acc = part + 16 * VEC * 32;
+    // lane accumulators: one region of 16 << SS bytes per warp, aligned to its size in the
+    // shared window so that slot bits can be OR-ed into the lane's address
+    constexpr uint32_t kRegion = 16u << SlotShift<VEC>::value;
+    const uint32_t acc_sh0 = (uint32_t)__cvta_generic_to_shared(part + 16 * VEC * 32);
+    const uint32_t acc_sh = (acc_sh0 + kRegion - 1) & ~(kRegion - 1);
+    float* acc = part + 16 * VEC * 32 + (acc_sh - acc_sh0) / sizeof(float);
     uint16_t* masks = reinterpret_cast<uint16_t*>(acc + NT * VEC * 16);
     uint16_t* rows16 = masks + align16((size_t)pr.seg_inputs * sizeof(uint16_t)) / sizeof(uint16_t);
 
-    const auto xp = Provider<XM, NT>::make(pr, hdr.red);
     const long long row0 = pr.row0;
+    const bool from_list = batch.mode == kModeMulOnly;
+    const int span = (pr.n_inputs - pr.in_begin + K - 1) / K;
+    const int klo = min(pr.in_begin + split * span, pr.n_inputs);
+    const int khi = min(klo + span, pr.n_inputs);
+    const int i0 = min(klo + g * pr.seg_inputs, khi);
+    const int i1 = min(i0 + pr.seg_inputs, khi);
+
+    // ---- prologue on weights only (nothing an earlier kernel of the stream writes): the
+    // cutoff's probes and this CTA's stats segment start on their way to L2
+    if (!from_list) {
+        if (tid == 0 && ((reinterpret_cast<uintptr_t>(pr.probes) & 15u) == 0) && (pr.P % 8) == 0)
+            prefetch_l2(pr.probes, (uint32_t)pr.P * 2u);
+        const uint16_t* s0 = pr.stats + (row0 + 16LL * i0) * pr.stats_stride;
+        const long long sbytes = 32LL * (i1 - i0) * pr.stats_stride;
+        if (((reinterpret_cast<uintptr_t>(s0) & 15u) == 0)) {
+            for (long long off = (long long)tid * 16384; off < sbytes; off += (long long)NT * 16384)
+                prefetch_l2(reinterpret_cast<const unsigned char*>(s0) + off, (uint32_t)min(16384LL, sbytes - off));
+        }
+    }
+    pdl_wait();  // from here on: x, residuals and scratch written by earlier kernels
+
+    const auto xp = Provider<XM, NT>::make(pr, hdr.red);
 
     // ---- phases 1-2: cutoff, selection masks, cluster-local row numbering
     int S, list_lo = 0;
-    const bool from_list = batch.mode == kModeMulOnly;
     if (!from_list) {
         int iters = 0;
         const float cutoff =
             block_find_cutoff<NT>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters, dbg ? dbg + 8 : nullptr);
         stamp(dbg, 1);
-        const int span = (pr.n_inputs - pr.in_begin + K - 1) / K;
-        const int klo = min(pr.in_begin + split * span, pr.n_inputs);
-        const int khi = min(klo + span, pr.n_inputs);
-        const int i0 = min(klo + g * pr.seg_inputs, khi);
-        const int i1 = min(i0 + pr.seg_inputs, khi);
+        stamp(tr, 1);
         const int n = block_masks<NT>(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i0, i1, cutoff,
                                       masks, hdr.scan);
         block_write_rows_local<NT>(masks, i0, i1, rows16, hdr.scan);
@@ -141,6 +169,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
             hdr.my_row_base = (int)(row0 + 16LL * i0);
         }
         stamp(dbg, 2);
+        stamp(tr, 2);
         cluster.sync();  // counts and local row lists visible cluster-wide
         if (warp == 0) {  // all G peer counts read in parallel, then a warp scan
             const int c = lane < G ? *cluster.map_shared_rank(&hdr.my_count, lane) : 0;
@@ -174,6 +203,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
             if (K > 1) pr.split_sel[split] = S;
         }
         stamp(dbg, 3);
+        stamp(tr, 3);
     } else {
         const int total = __ldcg(pr.sel_total);
         list_lo = (int)(((long long)total * split) / K);
@@ -183,6 +213,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     // ---- phase 3: accumulate rows [a, b) of the cluster's numbering
     const int a = (int)(((long long)S * g) / G);
     const int b = (int)(((long long)S * (g + 1)) / G);
+    if (tr) tr[7] = b - a;
     const int log2L = pr.log2L;
     const int L = 1 << log2L, P = 32 >> log2L;
     const int rg = lane >> log2L, q = lane & (L - 1);
@@ -194,6 +225,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     const int32_t bucket_row0 = (int32_t)pr.bucket_row0;
 
     float* my_acc = acc + (size_t)warp * 16 * VEC * 32 + lane;
+    const uint32_t acc_lane = acc_sh + (uint32_t)warp * kRegion + (uint32_t)lane * 4u;
 #pragma unroll 4
     for (int j = 0; j < 16 * VEC; ++j) my_acc[j * 32] = 0.0f;
 
@@ -241,43 +273,39 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
         stage_fetch(cstart + kCH, nn, rr, xx);  // next chunk, overlapped with this one
 
         const uint2* st = stage + buf * kCH;
+        // rows j = rg + P*(warp + NW*m), m = 0..mw-1; a ring of kD rows per lane: row m is
+        // accumulated, then row m + kD is loaded into its registers (kD - 1 rows in flight)
         const int first = P * warp;
         const int mw = n > first ? (n - first + P * NW - 1) / (P * NW) : 0;
-        const int ng = (mw + U - 1) / U;
-        VT wA[U], wB[U];
-        float xA[U], xB[U];
-        auto load_group = [&](int grp, VT* w, float* xs) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int j = rg + P * (warp + NW * (grp * U + u));
-                if (j < n && col_ok) {
-                    const uint2 e = st[j];
-                    w[u] = VL::load(wbase + e.x);
-                    xs[u] = __uint_as_float(e.y);
-                } else {
-                    w[u] = VL::zero();
-                    xs[u] = 0.0f;
-                }
+        VT w[kD];
+        float xs[kD];
+        auto load_row = [&](int m, VT& wr, float& xr) {
+            const int j = rg + P * (warp + NW * m);
+            if (m < mw && j < n && col_ok) {
+                const uint2 e = st[j];
+                wr = VL::load(wbase + e.x);
+                xr = __uint_as_float(e.y);
+            } else {
+                wr = VL::zero();
+                xr = 0.0f;
             }
         };
-        auto acc_group = [&](const VT* w, const float* xs) {
 #pragma unroll
-            for (int u = 0; u < U; ++u) accumulate<VEC>(my_acc, w[u], xs[u]);
-        };
-        if (ng > 0) load_group(0, wA, xA);
-        int gi = 0;
-        for (; gi + 1 < ng; gi += 2) {
-            load_group(gi + 1, wB, xB);
-            acc_group(wA, xA);
-            if (gi + 2 < ng) load_group(gi + 2, wA, xA);
-            acc_group(wB, xB);
+        for (int d = 0; d < kD; ++d) load_row(d, w[d], xs[d]);
+        for (int base = 0; base < mw; base += kD) {
+#pragma unroll
+            for (int d = 0; d < kD; ++d) {
+                if (base + d < mw) accumulate_sh<VEC>(acc_lane, w[d], xs[d]);
+                load_row(base + d + kD, w[d], xs[d]);
+            }
         }
-        if (gi < ng) acc_group(wA, xA);
 
         stage_store(stage + (buf ^ 1) * kCH, nn, rr, xx);
         __syncthreads();
     }
     stamp(dbg, 4);
+    stamp(tr, 4);
+    pdl_trigger();  // the successor may start its weights-only prologue on SMs this launch frees
 
     // ---- phase 4: lane accumulators -> CTA partial tile -> cluster sum -> splits
     for (int sk = warp; sk < 16 * VEC; sk += NW) {
@@ -292,6 +320,7 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     }
     cluster.sync();
     stamp(dbg, 5);
+    stamp(tr, 5);
     const int nout = 16 * TW;
     const int per = (nout + G - 1) / G;
     const int o0 = min(nout, g * per), o1 = min(nout, o0 + per);
@@ -329,24 +358,33 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
                 const int o = o0 + oo;
                 if (tile * TW + o / 16 < cols) {
                     const size_t j = tile_out + o;
+                    const float res = pr.residual ? pr.residual[j] : 0.0f;  // in flight with the partials
                     float s = 0.0f;
-                    for (int k = 0; k < K; ++k) s += __ldcg(pr.partials + (size_t)k * split_stride + j);
-                    if (pr.residual) s = pr.residual[j] + s;
+                    for (int kb = 0; kb < K; kb += kSumBatch) {  // kSumBatch loads in flight, added in split order
+                        float v[kSumBatch];
+#pragma unroll
+                        for (int u = 0; u < kSumBatch; ++u)
+                            v[u] = kb + u < K ? __ldcg(pr.partials + (size_t)(kb + u) * split_stride + j) : 0.0f;
+#pragma unroll
+                        for (int u = 0; u < kSumBatch; ++u)
+                            if (kb + u < K) s += v[u];
+                    }
+                    if (pr.residual) s = res + s;
                     pr.out[j] = s;
                 }
             }
-            if (tid == 0) {
-                pr.slice_ctr[tile * G + g] = 0;  // ready for the next launch
-                if (tile == 0 && g == 0 && pr.count_out) {
-                    int t = 0;
-                    for (int k = 0; k < K; ++k) t += __ldcg(pr.split_sel + k);
-                    *pr.count_out = t;
-                }
+            if (tid == 0) pr.slice_ctr[tile * G + g] = 0;  // ready for the next launch
+            if (warp == NW - 1 && tile == 0 && g == 0 && pr.count_out) {  // one warp, all loads at once
+                int t = 0;
+                for (int k = lane; k < K; k += 32) t += __ldcg(pr.split_sel + k);
+                t = __reduce_add_sync(0xffffffffu, t);
+                if (lane == 0) *pr.count_out = t;
             }
         }
     }
     cluster.sync();  // peers are done reading `part` and my row list
     stamp(dbg, 6);
+    stamp(tr, 6);
 }
 
 // ------------------------------------------------------------------ standalone kernels
@@ -400,13 +438,15 @@ int launch_one(const BMBatch& b, int G, int n_clusters, size_t smem, cudaStream_
     cfg.blockDim = dim3(Threads<VEC>::value);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)G;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = b.pdl ? 2 : 1;
     IAM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, b));
     return IAM_OK;
 }

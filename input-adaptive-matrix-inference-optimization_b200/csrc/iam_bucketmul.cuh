@@ -398,6 +398,7 @@ struct VecLoad<8> {
     using T = uint4;
     static IAM_DEV T load(const uint16_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
     static IAM_DEV T zero() { return make_uint4(0u, 0u, 0u, 0u); }
+    static IAM_DEV uint32_t word(const T& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
     static IAM_DEV uint32_t bits(const T& v, int k) {
         const uint32_t w = (k >> 1) == 0 ? v.x : (k >> 1) == 1 ? v.y : (k >> 1) == 2 ? v.z : v.w;
         return (k & 1) ? (w >> 16) : (w & 0xffffu);
@@ -408,6 +409,7 @@ struct VecLoad<4> {
     using T = uint2;
     static IAM_DEV T load(const uint16_t* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
     static IAM_DEV T zero() { return make_uint2(0u, 0u); }
+    static IAM_DEV uint32_t word(const T& v, int i) { return i == 0 ? v.x : v.y; }
     static IAM_DEV uint32_t bits(const T& v, int k) {
         const uint32_t w = (k >> 1) == 0 ? v.x : v.y;
         return (k & 1) ? (w >> 16) : (w & 0xffffu);
@@ -418,8 +420,48 @@ struct VecLoad<1> {
     using T = uint32_t;
     static IAM_DEV T load(const uint16_t* p) { return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p)); }
     static IAM_DEV T zero() { return 0u; }
+    static IAM_DEV uint32_t word(const T& v, int) { return v; }
     static IAM_DEV uint32_t bits(const T& v, int) { return v; }
 };
+
+// Adds x * w_k into this lane's private slot accumulators, addressed in the shared window:
+// acc_lane = the lane's float in a per-warp region aligned to its size (16 slots x VEC x 32
+// lanes x 4 B = 16 << SS bytes), slot s / column k at acc_lane + s * (1 << SS) + k * 128.  The
+// slot (low 4 bits of the fp16 word) becomes an address with one shift and one LOP3:
+// ((word << SS) & (15 << SS)) | acc_lane (low half) or ((word >> (16 - SS)) & ...) (high half).
+template <int VEC>
+struct SlotShift {
+    static constexpr int value = VEC == 8 ? 10 : VEC == 4 ? 9 : 7;  // log2(VEC * 128)
+};
+
+// Volatile asm keeps these in program order among themselves (a later row may hit the same
+// slot); the accumulators are only touched elsewhere across __syncthreads().
+IAM_DEV float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+IAM_DEV void sts_f32(uint32_t a, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v)); }
+
+template <int VEC>
+IAM_DEV void accumulate_sh(uint32_t acc_lane, const typename VecLoad<VEC>::T& w, float x) {
+    constexpr int SS = SlotShift<VEC>::value;
+    constexpr uint32_t M = 15u << SS;
+    uint32_t a[VEC];
+    float old[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        const uint32_t word = VecLoad<VEC>::word(w, k >> 1);
+        const uint32_t sh = (k & 1) ? ((word >> (16 - SS)) & M) : ((word << SS) & M);
+        a[k] = (sh | acc_lane) + (uint32_t)(k * 128);
+    }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) old[k] = lds_f32(a[k]);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) old[k] = fmaf(x, h2f(VecLoad<VEC>::bits(w, k)), old[k]);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) sts_f32(a[k], old[k]);
+}
 
 // Adds x * w_k into this lane's private slot accumulators acc[(slot*VEC + k) * 32].  The
 // VEC addresses of one call are distinct (k differs), so all loads are issued before any

@@ -47,6 +47,8 @@ struct BMProblem {
     int* count_out;           // optional
     int* iters_out;           // optional
     long long* dbg;           // optional per-phase globaltimer stamps (cluster 0, CTA 0)
+    long long* trace;         // optional: 8 stamps per CTA (blockIdx.x < trace_cap), see iam_bucketmul_trace
+    int trace_cap;
     long long row0;           // expert row offset (expertSize * expertNo)
     long long bucket_row0;    // absolute row held by buckets[0] (0, or the first row of a shard)
     int in_begin;             // first input of this shard (row-parallel tensor parallelism)
@@ -68,6 +70,7 @@ struct BMBatch {
     int nprob;
     int mode;
     int xmode;
+    int pdl;  // launched with programmatic stream serialization (waits on its predecessor in-kernel)
 };
 
 // Scratch a problem needs beyond its inputs and outputs (device memory the caller owns).

@@ -44,6 +44,8 @@ struct iam_bucketmul_s {
     int disp_G = 8;
     int disp_bucket_cols = 0;
     long long* dbg = nullptr;  // optional phase stamps
+    long long* trace = nullptr;  // optional per-CTA stamps
+    int trace_cap = 0;
 };
 
 namespace {
@@ -93,6 +95,8 @@ int fill_problem(iam_bucketmul_s* h, BMProblem& p, int G, const float* x, const 
     p.split_sel = h->ints + 8;
     p.slice_ctr = h->ctr;
     p.dbg = h->dbg;
+    p.trace = h->trace;
+    p.trace_cap = h->trace_cap;
     const size_t need = (size_t)kMaxSplits * 16 * (size_t)bucket_cols;
     if (need > h->partials_cap) {
         if (h->partials) IAM_CUDA_TRY(cudaFree(h->partials));
@@ -114,11 +118,12 @@ bool plan_fits(const BMBatch& b, int G) {
     return true;
 }
 
-// Widest vector load every problem of the batch supports (IAM_BM_VEC may lower it).
+// Vector width: 4 columns per lane (IAM_BM_VEC may pick 8 or 1), lowered to what every
+// problem's column count and alignment allow.
 int pick_vec(const BMBatch& b) {
-    int vec = 8;
+    int vec = 4;
     const char* env = getenv("IAM_BM_VEC");
-    if (env && (atoi(env) == 4 || atoi(env) == 1)) vec = atoi(env);
+    if (env && (atoi(env) == 8 || atoi(env) == 4 || atoi(env) == 1)) vec = atoi(env);
     for (int i = 0; i < b.nprob; ++i) {
         const BMProblem& p = b.p[i];
         const uintptr_t a = reinterpret_cast<uintptr_t>(p.buckets);
@@ -296,6 +301,13 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev) {
     if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_phase_times: null handle");
     h->dbg = times_dev;
+    return IAM_OK;
+}
+
+int iam_bucketmul_trace(iam_bucketmul_t h, long long* trace_dev, int capacity) {
+    if (!h || capacity < 0) return fail(IAM_ERR_ARG, "iam_bucketmul_trace: bad arguments");
+    h->trace = trace_dev;
+    h->trace_cap = trace_dev ? capacity : 0;
     return IAM_OK;
 }
 

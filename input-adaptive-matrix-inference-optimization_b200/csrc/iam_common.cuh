@@ -19,6 +19,20 @@ constexpr int kMaxIters = 20;              // bucketMul.cl:148
 
 // Exact fp16 -> fp32 of raw bits (the 4 slot bits stay part of the value, as in
 // bucketMul.cl:430-431 where the unmasked packed weight is the multiplicand).
+// Asks the L2 to fetch [p, p + bytes) (cp.async.bulk.prefetch.L2; p 16-byte aligned, bytes a
+// multiple of 16).  No registers, no shared memory, no completion to wait for.
+IAM_DEV void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(__cvta_generic_to_global(p)), "r"(bytes)
+                 : "memory");
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while its predecessor still runs; pdl_wait() returns once the predecessor grid
+// has completed and its writes are visible (immediately when launched without the
+// attribute).  pdl_trigger() lets the successor launch early.
+IAM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+IAM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 IAM_DEV float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
 // 1e5 * |x * s| with both multiplies rounded separately (bucketMul.cl:110, :378).
@@ -32,6 +46,24 @@ int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
 }  // namespace iam
+
+// cudaLaunchKernelEx with programmatic stream serialization when `pdl` is set (the kernel
+// must call pdl_wait() before it touches what earlier kernels of the stream write).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                             Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 #define IAM_CUDA_TRY(expr)                                          \
     do {                                                            \

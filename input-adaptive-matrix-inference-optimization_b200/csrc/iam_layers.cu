@@ -23,6 +23,8 @@ namespace iam {
 __global__ void embed_kernel(const uint16_t* __restrict__ embed, int dim, int token_arg,
                              const unsigned long long* token_key, const int* token_dev, float* __restrict__ x,
                              unsigned long long* argmax_key, int* token_used) {
+    pdl_trigger();
+    pdl_wait();
     int token = token_arg;
     if (token_key) token = (int)(0xffffffffu - (unsigned)(*token_key & 0xffffffffull));
     else if (token_dev) token = *token_dev;
@@ -36,7 +38,11 @@ __global__ void embed_kernel(const uint16_t* __restrict__ embed, int dim, int to
 }
 
 // Clears the argmax slot (used when the embedding read its token from the same slot).
-__global__ void clear_key_kernel(unsigned long long* key) { *key = 0ull; }
+__global__ void clear_key_kernel(unsigned long long* key) {
+    pdl_trigger();
+    pdl_wait();
+    *key = 0ull;
+}
 
 // ------------------------------------------------------------------ attention
 
@@ -79,6 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     constexpr int NWA = kAttnThreads / 32;
     constexpr int TU = kAttnTU;
     const int half = HD / 2;
+    pdl_wait();
     const int kvh = blockIdx.x / p.n_split, s = blockIdx.x % p.n_split;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int pos = *p.pos_dev;
@@ -220,6 +227,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     }
 
     // last active CTA of this KV head combines the chunks in chunk order
+    pdl_trigger();
     __threadfence();
     __syncthreads();
     __shared__ int last;
@@ -266,29 +274,48 @@ IAM_DEV unsigned long long argmax_key(float v, int idx) {
 }
 
 // logits[r] = sum_c W[r][c] * xf[c], xf = rmsnorm(x) * gain; one warp per row, rows strided
-// over the grid; also folds the greedy argmax into *argmax_key with atomicMax.
+// over the grid, 8 x 16 B of the row per lane in flight; also folds the greedy argmax into
+// *argmax_key with atomicMax.
 __global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(LMHeadParams p) {
     extern __shared__ __align__(16) float xf[];
     __shared__ float red[256];
     __shared__ unsigned long long wbest[kHeadThreads / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NWH = kHeadThreads / 32;
+    constexpr int KB = 8;  // 16-byte loads per lane in flight
+    const int first = blockIdx.x * NWH + warp;
+    // the first row of this warp starts on its way to L2 before the dependency wait
+    if (first < p.rows && (p.dim % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.W) & 15u) == 0) && lane == 0)
+        prefetch_l2(p.W + (size_t)first * p.dim, (uint32_t)p.dim * 2u);
+    pdl_trigger();
+    pdl_wait();
     const float scale = block_rms_scale<kHeadThreads>(p.x, p.dim, p.eps, red);
     for (int i = tid; i < p.dim; i += kHeadThreads) xf[i] = __fmul_rn(__fmul_rn(p.x[i], scale), h2f(p.gain[i]));
     __syncthreads();
     unsigned long long best = 0ull;
-    const int vec_ok = (p.dim % 256 == 0);
-    for (int r = blockIdx.x * NWH + warp; r < p.rows; r += gridDim.x * NWH) {
+    const int vec_ok = (p.dim % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.W) & 15u) == 0);
+    for (int r = first; r < p.rows; r += gridDim.x * NWH) {
         const uint16_t* w = p.W + (size_t)r * p.dim;
         float acc0 = 0.0f, acc1 = 0.0f;
         if (vec_ok) {
-            for (int c = lane * 8; c < p.dim; c += 256) {
-                const uint4 v = __ldcs(reinterpret_cast<const uint4*>(w + c));
-                const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+            for (int cb = 0; cb < p.dim; cb += 256 * KB) {
+                uint4 v[KB];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    acc0 = fmaf(h2f(wd[e] & 0xffffu), xf[c + 2 * e], acc0);
-                    acc1 = fmaf(h2f(wd[e] >> 16), xf[c + 2 * e + 1], acc1);
+                for (int k = 0; k < KB; ++k) {
+                    const int c = cb + k * 256 + lane * 8;
+                    v[k] = c < p.dim ? __ldcs(reinterpret_cast<const uint4*>(w + c)) : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+                for (int k = 0; k < KB; ++k) {
+                    const int c = cb + k * 256 + lane * 8;
+                    if (c < p.dim) {
+                        const uint32_t wd[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            acc0 = fmaf(h2f(wd[e] & 0xffffu), xf[c + 2 * e], acc0);
+                            acc1 = fmaf(h2f(wd[e] >> 16), xf[c + 2 * e + 1], acc1);
+                        }
+                    }
                 }
             }
         } else {
@@ -314,6 +341,8 @@ __global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(LMHeadParams p) {
 
 // pos += 1 after a generated step, and the chosen token appended to tokens_out[*count].
 __global__ void advance_kernel(int* pos, const unsigned long long* key, int* tokens_out, int* count) {
+    pdl_trigger();
+    pdl_wait();
     if (tokens_out) tokens_out[*count] = (int)(0xffffffffu - (unsigned)(*key & 0xffffffffull));
     if (count) *count += 1;
     *pos += 1;
@@ -322,14 +351,12 @@ __global__ void advance_kernel(int* pos, const unsigned long long* key, int* tok
 // ------------------------------------------------------------------ host launchers
 
 int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long long* token_key,
-                 const int* token_dev, float* x, unsigned long long* argmax_key, int* token_used, cudaStream_t s) {
-    embed_kernel<<<(dim + 1023) / 1024, 1024, 0, s>>>(embed, dim, token, token_key, token_dev, x, argmax_key,
-                                                       token_used);
-    IAM_CUDA_TRY(cudaGetLastError());
-    if (argmax_key && token_key == argmax_key) {
-        clear_key_kernel<<<1, 1, 0, s>>>(argmax_key);
-        IAM_CUDA_TRY(cudaGetLastError());
-    }
+                 const int* token_dev, float* x, unsigned long long* argmax_key, int* token_used, cudaStream_t s,
+                 bool pdl) {
+    IAM_CUDA_TRY(launch_ex(embed_kernel, dim3((dim + 1023) / 1024), dim3(1024), 0, s, pdl, embed, dim, token,
+                           token_key, token_dev, x, argmax_key, token_used));
+    if (argmax_key && token_key == argmax_key)
+        IAM_CUDA_TRY(launch_ex(clear_key_kernel, dim3(1), dim3(1), 0, s, pdl, argmax_key));
     return IAM_OK;
 }
 
@@ -340,47 +367,44 @@ size_t attention_smem(const AttnParams& p, int gq) {
 }
 
 template <int GQ, int VD>
-int launch_attention_t(const AttnParams& p, size_t smem, cudaStream_t s) {
+int launch_attention_t(const AttnParams& p, size_t smem, cudaStream_t s, bool pdl) {
     auto kern = attention_kernel<GQ, VD>;
     if (smem > 48 * 1024) IAM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)(p.n_kv_heads * p.n_split), kAttnThreads, smem, s>>>(p);
-    IAM_CUDA_TRY(cudaGetLastError());
+    IAM_CUDA_TRY(launch_ex(kern, dim3((unsigned)(p.n_kv_heads * p.n_split)), dim3(kAttnThreads), smem, s, pdl, p));
     return IAM_OK;
 }
 
 template <int GQ>
-int launch_attention_g(const AttnParams& p, size_t smem, cudaStream_t s) {
+int launch_attention_g(const AttnParams& p, size_t smem, cudaStream_t s, bool pdl) {
     switch (p.head_dim) {
-        case 64: return launch_attention_t<GQ, 2>(p, smem, s);
-        case 128: return launch_attention_t<GQ, 4>(p, smem, s);
-        case 256: return launch_attention_t<GQ, 8>(p, smem, s);
+        case 64: return launch_attention_t<GQ, 2>(p, smem, s, pdl);
+        case 128: return launch_attention_t<GQ, 4>(p, smem, s, pdl);
+        case 256: return launch_attention_t<GQ, 8>(p, smem, s, pdl);
         default: return fail(IAM_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
     }
 }
 
-int launch_attention(const AttnParams& p, int gq, cudaStream_t s) {
+int launch_attention(const AttnParams& p, int gq, cudaStream_t s, bool pdl) {
     const size_t smem = attention_smem(p, gq);
     switch (gq) {
-        case 1: return launch_attention_g<1>(p, smem, s);
-        case 2: return launch_attention_g<2>(p, smem, s);
-        case 4: return launch_attention_g<4>(p, smem, s);
-        case 8: return launch_attention_g<8>(p, smem, s);
+        case 1: return launch_attention_g<1>(p, smem, s, pdl);
+        case 2: return launch_attention_g<2>(p, smem, s, pdl);
+        case 4: return launch_attention_g<4>(p, smem, s, pdl);
+        case 8: return launch_attention_g<8>(p, smem, s, pdl);
         default: return fail(IAM_ERR_UNSUPPORTED, "attention: n_heads / n_kv_heads must be 1, 2, 4 or 8");
     }
 }
 
-int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s) {
+int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s, bool pdl) {
     const size_t smem = sizeof(float) * (size_t)p.dim;
     if (smem > 48 * 1024)
         IAM_CUDA_TRY(cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    lm_head_kernel<<<grid, kHeadThreads, smem, s>>>(p);
-    IAM_CUDA_TRY(cudaGetLastError());
+    IAM_CUDA_TRY(launch_ex(lm_head_kernel, dim3(grid), dim3(kHeadThreads), smem, s, pdl, p));
     return IAM_OK;
 }
 
-int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s) {
-    advance_kernel<<<1, 1, 0, s>>>(pos, key, tokens_out, count);
-    IAM_CUDA_TRY(cudaGetLastError());
+int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s, bool pdl) {
+    IAM_CUDA_TRY(launch_ex(advance_kernel, dim3(1), dim3(1), 0, s, pdl, pos, key, tokens_out, count));
     return IAM_OK;
 }
 

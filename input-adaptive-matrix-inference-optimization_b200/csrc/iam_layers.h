@@ -36,10 +36,13 @@ struct LMHeadParams {
 };
 
 int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long long* token_key,
-                 const int* token_dev, float* x, unsigned long long* argmax_key, int* token_used, cudaStream_t s);
+                 const int* token_dev, float* x, unsigned long long* argmax_key, int* token_used, cudaStream_t s,
+                 bool pdl = false);
 size_t attention_smem(const AttnParams& p, int gq);
-int launch_attention(const AttnParams& p, int gq, cudaStream_t s);
-int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s);
-int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s);
+// pdl: launch with programmatic stream serialization (see launch_ex)
+int launch_attention(const AttnParams& p, int gq, cudaStream_t s, bool pdl = false);
+int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s, bool pdl = false);
+int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s,
+                   bool pdl = false);
 
 }  // namespace iam

@@ -9,6 +9,7 @@
 // Position and token live in device memory, so a step can be captured once as a CUDA graph
 // and replayed for every generated token without host round trips.
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -64,7 +65,11 @@ __global__ void fill_u16(uint16_t* w, size_t n, uint16_t v) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) w[i] = v;
 }
 
-__global__ void set_int_kernel(int* p, int v) { *p = v; }
+__global__ void set_int_kernel(int* p, int v) {
+    pdl_trigger();
+    pdl_wait();
+    *p = v;
+}
 
 // Copies columns [c0, c0+cols_out) of every row of a [rows][cols_in] u16 array.
 __global__ void slice_cols_kernel(const uint16_t* src, int rows, int cols_in, int c0, int cols_out, uint16_t* dst) {
@@ -110,6 +115,7 @@ struct iam_model_s {
     std::vector<BMBatch> plans;  // 4 per layer
     float plan_effort = -1.0f;
     int vec = 4, G = 4;
+    bool pdl = true;  // step kernels launched with programmatic stream serialization (IAM_PDL=0: off)
     // generation graph
     cudaGraphExec_t gen_graph = nullptr;
     float gen_effort = -1.0f;
@@ -444,17 +450,18 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     const iam_model_config& c = m->cfg;
     int rc = build_plans(m, effort);
     if (rc) return rc;
-    if (pos_arg >= 0) {
-        set_int_kernel<<<1, 1, 0, s>>>(m->pos, pos_arg);
-        IAM_CUDA_TRY(cudaGetLastError());
-    }
+    // per-launch event hooks sit between the kernels, so they run without programmatic
+    // serialization
+    const bool pdl = m->pdl && !hk;
+    if (pos_arg >= 0) IAM_CUDA_TRY(launch_ex(set_int_kernel, dim3(1), dim3(1), 0, s, pdl, m->pos, pos_arg));
     if ((rc = hook(hk, IAM_KERNEL_EMBED, s))) return rc;
     if ((rc = launch_embed(m->embed, c.dim, token_arg, token_arg < 0 ? m->key : nullptr, nullptr, m->x, m->key,
-                           m->token_used, s)))
+                           m->token_used, s, pdl)))
         return rc;
     const int gq = c.n_heads / c.n_kv_heads;
     for (int l = 0; l < c.n_layers; ++l) {
         if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
+        m->plans[l * 4 + 0].pdl = pdl;
         if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->G, s))) return rc;
         AttnParams ap{};
         ap.q = m->q;
@@ -474,9 +481,10 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         ap.n_split = m->att_split;
         ap.chunk_cap = m->chunk_cap;
         if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
-        if ((rc = launch_attention(ap, gq, s))) return rc;
+        if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
         for (int b = 1; b < 4; ++b) {
             if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
+            m->plans[l * 4 + b].pdl = pdl;
             if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->G, s))) return rc;
         }
     }
@@ -490,7 +498,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     hp.logits = logits;
     hp.argmax_key = m->key;
     if ((rc = hook(hk, IAM_KERNEL_LM_HEAD, s))) return rc;
-    return launch_lm_head(hp, 2 * m->sm_count, s);
+    return launch_lm_head(hp, 2 * m->sm_count, s, pdl);
 }
 
 bool effort_ok(float e) { return std::isfinite(e) && e > 0.0f && e <= 1.0f; }
@@ -518,6 +526,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device) {
     IAM_CUDA_TRY(cudaSetDevice(device));
     m->cfg = *cfg;
     m->device = device;
+    if (const char* v = getenv("IAM_PDL")) m->pdl = atoi(v) != 0;
     m->n_heads_local = cfg->n_heads;
     m->n_kv_local = cfg->n_kv_heads;
     m->ffn_local = cfg->ffn_dim;
@@ -656,7 +665,7 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
     int done = 0;
     if (!cont) {
         if ((rc = enqueue_step(m, first_token, start_pos, effort, m->logits, s))) return rc;
-        if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s))) return rc;
+        if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s, m->pdl))) return rc;
         done = 1;
         if (n_tokens == 1) return IAM_OK;
     }
@@ -671,7 +680,7 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
         cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
         if (e == cudaSuccess) {
             rc = enqueue_step(m, -1, -1, effort, m->logits, cap);
-            if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, cap);
+            if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, cap, m->pdl);
             e = cudaStreamEndCapture(cap, &graph);
         }
         if (e == cudaSuccess && !rc) e = cudaGraphInstantiate(&m->gen_graph, graph, 0);
