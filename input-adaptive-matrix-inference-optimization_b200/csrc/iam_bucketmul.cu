@@ -274,29 +274,31 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
 
         const uint2* st = stage + buf * kCH;
         // rows j = rg + P*(warp + NW*m), m = 0..mw-1; a ring of kD rows per lane: row m is
-        // accumulated, then row m + kD is loaded into its registers (kD - 1 rows in flight)
+        // accumulated, then row m + kD is loaded into its registers (kD - 1 rows in flight).
+        // Past the end a lane re-reads the last row with x = 0 (adds exact zeros), so the
+        // loop carries no branches; lanes of a partial tile read column 0 into accumulators
+        // that are never written out.
         const int first = P * warp;
         const int mw = n > first ? (n - first + P * NW - 1) / (P * NW) : 0;
-        VT w[kD];
-        float xs[kD];
-        auto load_row = [&](int m, VT& wr, float& xr) {
-            const int j = rg + P * (warp + NW * m);
-            if (m < mw && j < n && col_ok) {
-                const uint2 e = st[j];
+        if (mw > 0) {
+            const int j0 = rg + first, jstep = P * NW, jlast = n - 1;
+            VT w[kD];
+            float xs[kD];
+            auto load_row = [&](int m, VT& wr, float& xr) {
+                const int j = j0 + m * jstep;
+                const bool ok = j < n;
+                const uint2 e = st[ok ? j : jlast];
                 wr = VL::load(wbase + e.x);
-                xr = __uint_as_float(e.y);
-            } else {
-                wr = VL::zero();
-                xr = 0.0f;
-            }
-        };
+                xr = ok ? __uint_as_float(e.y) : 0.0f;
+            };
 #pragma unroll
-        for (int d = 0; d < kD; ++d) load_row(d, w[d], xs[d]);
-        for (int base = 0; base < mw; base += kD) {
+            for (int d = 0; d < kD; ++d) load_row(d, w[d], xs[d]);
+            for (int base = 0; base < mw; base += kD) {
 #pragma unroll
-            for (int d = 0; d < kD; ++d) {
-                if (base + d < mw) accumulate_sh<VEC>(acc_lane, w[d], xs[d]);
-                load_row(base + d + kD, w[d], xs[d]);
+                for (int d = 0; d < kD; ++d) {
+                    accumulate_sh<VEC>(acc_lane, w[d], xs[d]);
+                    load_row(base + d + kD, w[d], xs[d]);
+                }
             }
         }
 

@@ -7,6 +7,8 @@
 
 #include <cooperative_groups.h>
 
+#include <utility>
+
 #include "iam_common.cuh"
 
 namespace iam {
@@ -435,32 +437,39 @@ struct SlotShift {
 };
 
 // Volatile asm keeps these in program order among themselves (a later row may hit the same
-// slot); the accumulators are only touched elsewhere across __syncthreads().
+// slot); the accumulators are only touched elsewhere across __syncthreads().  The column
+// offset OFF rides in the instruction's immediate.
+template <int OFF>
 IAM_DEV float lds_f32(uint32_t a) {
     float v;
-    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    asm volatile("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(a), "n"(OFF));
     return v;
 }
-IAM_DEV void sts_f32(uint32_t a, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v)); }
+template <int OFF>
+IAM_DEV void sts_f32(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0+%1], %2;" ::"r"(a), "n"(OFF), "f"(v));
+}
+
+template <int VEC, int K>
+IAM_DEV uint32_t slot_addr(const typename VecLoad<VEC>::T& w, uint32_t acc_lane) {
+    constexpr int SS = SlotShift<VEC>::value;
+    constexpr uint32_t M = 15u << SS;
+    const uint32_t word = VecLoad<VEC>::word(w, K >> 1);
+    return ((K & 1) ? ((word >> (16 - SS)) & M) : ((word << SS) & M)) | acc_lane;
+}
+
+template <int VEC, int... K>
+IAM_DEV void accumulate_sh_impl(uint32_t acc_lane, const typename VecLoad<VEC>::T& w, float x,
+                                std::integer_sequence<int, K...>) {
+    const uint32_t a[VEC] = {slot_addr<VEC, K>(w, acc_lane)...};
+    float old[VEC] = {lds_f32<K * 128>(a[K])...};  // braced lists evaluate left to right
+    ((old[K] = fmaf(x, h2f(VecLoad<VEC>::bits(w, K)), old[K])), ...);
+    (sts_f32<K * 128>(a[K], old[K]), ...);
+}
 
 template <int VEC>
 IAM_DEV void accumulate_sh(uint32_t acc_lane, const typename VecLoad<VEC>::T& w, float x) {
-    constexpr int SS = SlotShift<VEC>::value;
-    constexpr uint32_t M = 15u << SS;
-    uint32_t a[VEC];
-    float old[VEC];
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-        const uint32_t word = VecLoad<VEC>::word(w, k >> 1);
-        const uint32_t sh = (k & 1) ? ((word >> (16 - SS)) & M) : ((word << SS) & M);
-        a[k] = (sh | acc_lane) + (uint32_t)(k * 128);
-    }
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) old[k] = lds_f32(a[k]);
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) old[k] = fmaf(x, h2f(VecLoad<VEC>::bits(w, k)), old[k]);
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) sts_f32(a[k], old[k]);
+    accumulate_sh_impl<VEC>(acc_lane, w, x, std::make_integer_sequence<int, VEC>{});
 }
 
 // Adds x * w_k into this lane's private slot accumulators acc[(slot*VEC + k) * 32].  The
