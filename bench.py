@@ -55,6 +55,25 @@ def load_pkg():
     return mod
 
 
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "decode_step_launch_list.md")
+TRAFFIC_EFFORT = 0.25  # the effort the committed ncu traffic capture ran at
+
+
+def profiled_traffic(effort):
+    """DRAM bytes (read + write) per bm_fused_kernel launch from the committed ncu summary of
+    the decode step, when this run's effort is the one that was profiled; else None."""
+    if abs(effort - TRAFFIC_EFFORT) > 1e-9:
+        return None
+    try:
+        with open(TRAFFIC_PROFILE) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -387,7 +406,10 @@ def run_decode(args, rank, world):
                    "step_effective_GBps": round(step_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
                    "model_build_s": round(build_s, 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.effort),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one "
+                                       "decode step's 128 launches (profiles/decode_step_launch_list.md)",
+                     "peak_source": peak_kind,
                      "kernel": "bm_fused_kernel", "bytes_per_launch": int(bm_bytes / (4 * cfg.n_layers)),
                      "kernel_ms_per_step": round(bm_ms, 4), "step_ms_events": round(all_ms, 4),
                      "ms_per_step_by_kernel": {k: round(v, 4) for k, v in by_kind.items()}},
