@@ -170,6 +170,33 @@ int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsig
  * {meta.txt,buckets.bin,stats.bin,probes.bin} (preprocess_layer_fixed_gpu.py:245-333), with the
  * loader's validation (binary_loader.hpp:96-123): IAM_ERR_IO on missing or mis-sized files. */
 int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device);
+
+/* Tensor parallelism over NCCL (one process per GPU, `world` ranks).  The reference runs one
+ * GPU (model.hpp:84-231); this shards its decode step Megatron-style: q/k/v and gate/up are
+ * column-parallel (rank r holds bucket columns [r*C/world, (r+1)*C/world), i.e. its heads and
+ * its FFN slice), o and down are row-parallel (rank r holds the bucket rows of its inputs),
+ * stats and probes are replicated so every rank computes the identical cutoff and selection,
+ * and the LM head is vocab-sharded.  Per layer: an all-gather of the attention output, an
+ * all-reduce of the o output, an all-gather of gate and up, an all-reduce of the down
+ * output; per step a max all-reduce of the argmax key (and an all-gather of the logits when a
+ * caller asks for them).  n_heads, n_kv_heads, the bucket columns of every matrix and vocab
+ * must divide by `world`.
+ *
+ * iam_tp_unique_id fills the 128-byte NCCL id that rank 0 creates and the caller broadcasts
+ * (any side channel: torch.distributed, MPI, a file). */
+#define IAM_TP_ID_BYTES 128
+int iam_tp_unique_id(unsigned char* id_out);
+/* Shard layout of rank `rank` of `world` without a GPU: for each of the 7 matrices
+ * (q, k, v, o, gate, up, down) four ints {first bucket column, bucket columns held, first
+ * input, end input}, then {first vocab row, vocab rows held}: 30 ints in out. */
+int iam_tp_shard_info(const iam_model_config* cfg, int rank, int world, int* out);
+/* iam_model_create_random / iam_model_load for one rank of a tensor-parallel group: every rank
+ * calls it at the same time (the NCCL communicator is created inside).  Random weights are
+ * the same as iam_model_create_random's for the same seed, then sharded. */
+int iam_model_create_random_tp(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed,
+                               int device, int rank, int world, const unsigned char* nccl_id);
+int iam_model_load_tp(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device,
+                      int rank, int world, const unsigned char* nccl_id);
 int iam_model_destroy(iam_model_t m);
 /* MistralModel::reset_caches (model.hpp:233-237): zero the KV cache and the position. */
 int iam_model_reset(iam_model_t m, void* stream);
@@ -188,13 +215,15 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
  * kernel_ms[k] (capacity entries) receives the average device time of launch k of a step and
  * kinds[k] its IAM_KERNEL_* kind; *n_kernels the launches per step.  Advances the position. */
 enum { IAM_KERNEL_EMBED = 0, IAM_KERNEL_BUCKETMUL = 1, IAM_KERNEL_ATTENTION = 2, IAM_KERNEL_LM_HEAD = 3,
-       IAM_KERNEL_OTHER = 4 };
+       IAM_KERNEL_OTHER = 4, IAM_KERNEL_COLLECTIVE = 5 };
 int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kernel_ms, int* kinds,
                             int capacity, int* n_kernels, void* stream);
-/* KV cache contents of one layer: k/v [n_kv_heads][n_tokens][head_dim] fp16 (post-RoPE k). */
+/* KV cache contents of one layer: k/v [n_kv_heads][n_tokens][head_dim] fp16 (post-RoPE k).
+ * Under tensor parallelism every rank takes the full arrays and keeps its own kv heads. */
 int iam_model_set_kv(iam_model_t m, int layer, const uint16_t* k_dev, const uint16_t* v_dev,
                      int n_tokens, void* stream);
-/* Fills positions [0, n_tokens) of every layer's K and V cache with N(0,1) fp16. */
+/* Fills positions [0, n_tokens) of every layer's K and V cache with N(0,1) fp16 (the same
+ * values per kv head at every tensor-parallel width). */
 int iam_model_fill_kv_random(iam_model_t m, int n_tokens, unsigned long long seed, void* stream);
 
 enum {
@@ -205,13 +234,16 @@ enum {
     IAM_W_MATRIX = 16
 };
 /* Copies one weight tensor to host memory; *bytes_out receives its size (host_dst may be
- * NULL to query it). */
+ * NULL to query it).  Under tensor parallelism: this rank's shard (buckets, LM head rows, KV
+ * heads); stats and probes are whole. */
 int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, size_t capacity_bytes,
                           size_t* bytes_out);
-/* Selected bucket rows summed over the 7*n_layers bucketMuls of the last step. */
+/* Selected bucket rows summed over the 7*n_layers bucketMuls of the last step (under tensor
+ * parallelism a collective call: every rank calls it and all get the whole-model total). */
 int iam_model_selected_rows(iam_model_t m, long long* total);
 /* Algorithmic bytes of the last step at KV length `context`: per bucketMul
- * 2|S|C + 2R + 4N + 2*min(N,4096) + 4M, plus K/V reads and the dense LM head. */
+ * 2|S|C + 2R + 4N + 2*min(N,4096) + 4M, plus K/V reads and the dense LM head (this rank's
+ * share under tensor parallelism). */
 int iam_model_step_bytes(iam_model_t m, int context, long long* bytes);
 
 #ifdef __cplusplus

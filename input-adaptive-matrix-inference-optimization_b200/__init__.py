@@ -214,29 +214,69 @@ _SIGNATURES.update({
     "iam_model_selected_rows": [_vp, _vp],
     "iam_model_step_bytes": [_vp, _i32, _vp],
     "iam_model_profile_steps": [_vp, _f32, _i32, _vp, _vp, _i32, _vp, _vp],
+    "iam_tp_unique_id": [_vp],
+    "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
+    "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
+    "iam_model_load_tp": [_vp, ctypes.c_char_p, _vp, _i32, _i32, _i32, _vp],
 })
-KERNEL_KINDS = ("embed", "bucketmul", "attention", "lm_head", "other")
+KERNEL_KINDS = ("embed", "bucketmul", "attention", "lm_head", "other", "collective")
+TP_ID_BYTES = 128
+
+
+def tp_unique_id():
+    """NCCL id for a tensor-parallel group (rank 0 makes it, every rank passes it in)."""
+    buf = (ctypes.c_ubyte * TP_ID_BYTES)()
+    check(load_library().iam_tp_unique_id(buf))
+    return bytes(buf)
+
+
+def tp_shard_info(cfg, rank, world):
+    """Shards of rank `rank` of `world` (no GPU needed): {matrix: (col0, cols, in0, in1)}, plus
+    'vocab': (row0, rows)."""
+    out = (ctypes.c_int * (4 * len(MATRIX_NAMES) + 2))()
+    check(load_library().iam_tp_shard_info(ctypes.byref(cfg), rank, world, out))
+    res = {name: tuple(out[4 * i:4 * i + 4]) for i, name in enumerate(MATRIX_NAMES)}
+    res["vocab"] = (out[4 * len(MATRIX_NAMES)], out[4 * len(MATRIX_NAMES) + 1])
+    return res
+
+
+def _tp_args(tp):
+    rank, world, uid = tp
+    if len(uid) != TP_ID_BYTES:
+        raise IamError(IAM_ERR_ARG, "tensor parallel id must be 128 bytes")
+    return rank, world, (ctypes.c_ubyte * TP_ID_BYTES).from_buffer_copy(uid)
 
 
 class Model:
-    """Mirror of MistralModel (model.hpp:84-237) on one device."""
+    """Mirror of MistralModel (model.hpp:84-237) on one device, or one rank of a
+    tensor-parallel group (tp=(rank, world, tp_unique_id() of rank 0))."""
 
-    def __init__(self, cfg, h):
+    def __init__(self, cfg, h, tp=None):
         self.cfg, self.h, self.lib = cfg, h, load_library()
+        self.rank, self.world = (tp[0], tp[1]) if tp else (0, 1)
 
     @classmethod
-    def random(cls, cfg, seed=0, device=0):
+    def random(cls, cfg, seed=0, device=0, tp=None):
         lib = load_library()
         h = ctypes.c_void_p()
-        check(lib.iam_model_create_random(ctypes.byref(h), ctypes.byref(cfg), seed, device))
-        return cls(cfg, h)
+        if tp:
+            rank, world, uid = _tp_args(tp)
+            check(lib.iam_model_create_random_tp(ctypes.byref(h), ctypes.byref(cfg), seed, device, rank, world, uid))
+        else:
+            check(lib.iam_model_create_random(ctypes.byref(h), ctypes.byref(cfg), seed, device))
+        return cls(cfg, h, tp)
 
     @classmethod
-    def load(cls, weights_dir, cfg, device=0):
+    def load(cls, weights_dir, cfg, device=0, tp=None):
         lib = load_library()
         h = ctypes.c_void_p()
-        check(lib.iam_model_load(ctypes.byref(h), os.fsencode(weights_dir), ctypes.byref(cfg), device))
-        return cls(cfg, h)
+        if tp:
+            rank, world, uid = _tp_args(tp)
+            check(lib.iam_model_load_tp(ctypes.byref(h), os.fsencode(weights_dir), ctypes.byref(cfg), device, rank,
+                                        world, uid))
+        else:
+            check(lib.iam_model_load(ctypes.byref(h), os.fsencode(weights_dir), ctypes.byref(cfg), device))
+        return cls(cfg, h, tp)
 
     def close(self):
         if self.h:

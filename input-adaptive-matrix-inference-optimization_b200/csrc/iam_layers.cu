@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(LMHeadParams p) {
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         if (lane == 0) {
             if (p.logits) p.logits[r] = v;
-            const unsigned long long k = argmax_key(v, r);
+            const unsigned long long k = argmax_key(v, p.row0 + r);
             best = k > best ? k : best;
         }
     }

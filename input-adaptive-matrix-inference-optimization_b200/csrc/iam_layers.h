@@ -33,6 +33,7 @@ struct LMHeadParams {
     int dim, rows;
     float* logits;                   // [rows] (may be null)
     unsigned long long* argmax_key;  // greedy argmax (may be null)
+    int row0;                        // vocabulary index of row 0 (vocab-sharded LM head)
 };
 
 int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long long* token_key,

@@ -11,11 +11,15 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
+#include <chrono>
 #include <cstring>
+#include <thread>
 #include <fstream>
 #include <sstream>
 #include <string>
 #include <vector>
+
+#include <nccl.h>
 
 #include "iam_bucketmul_launch.h"
 #include "iam_common.cuh"
@@ -41,6 +45,49 @@ struct Layer {
     Matrix m[NMAT];
 };
 
+// ------------------------------------------------------------------ tensor-parallel shards
+
+// q, k, v, gate, up are column-parallel; o and down row-parallel (their inputs are the
+// column-parallel outputs of the same rank, so no exchange is needed between the two halves).
+inline bool column_parallel(int which) { return which != MO && which != MD; }
+
+struct Shard {
+    int col0, cols;  // bucket columns held
+    int in0, in1;    // inputs held
+};
+
+inline void matrix_dims(const iam_model_config& c, int which, int* out_dim, int* in_dim) {
+    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim;
+    const int outs[NMAT] = {qn, kvn, kvn, c.dim, c.ffn_dim, c.ffn_dim, c.dim};
+    const int ins[NMAT] = {c.dim, c.dim, c.dim, qn, c.dim, c.dim, c.ffn_dim};
+    *out_dim = outs[which];
+    *in_dim = ins[which];
+}
+
+inline Shard shard_of(const iam_model_config& c, int which, int rank, int world) {
+    int out_dim, in_dim;
+    matrix_dims(c, which, &out_dim, &in_dim);
+    const int C = out_dim / 16;
+    if (world <= 1) return {0, C, 0, in_dim};
+    if (column_parallel(which)) return {rank * (C / world), C / world, 0, in_dim};
+    return {0, C, rank * (in_dim / world), (rank + 1) * (in_dim / world)};
+}
+
+int check_tp(const iam_model_config& c, int rank, int world) {
+    if (world < 1 || rank < 0 || rank >= world) return fail(IAM_ERR_ARG, "tensor parallel: bad rank or world");
+    if (world == 1) return IAM_OK;
+    if (c.n_heads % world || c.n_kv_heads % world || c.vocab % world)
+        return fail(IAM_ERR_UNSUPPORTED, "tensor parallel: n_heads, n_kv_heads and vocab must divide by world");
+    for (int i = 0; i < NMAT; ++i) {
+        int out_dim, in_dim;
+        matrix_dims(c, i, &out_dim, &in_dim);
+        if (column_parallel(i) ? (out_dim / 16) % world : in_dim % world)
+            return fail(IAM_ERR_UNSUPPORTED, std::string("tensor parallel: ") + kMatNames[i] +
+                                                 " does not split evenly over world");
+    }
+    return IAM_OK;
+}
+
 // splitmix64 -> two uniforms -> Box-Muller: a reproducible N(0,1) per (seed, tensor, index).
 IAM_DEV unsigned long long mix64(unsigned long long z) {
     z += 0x9e3779b97f4a7c15ull;
@@ -49,15 +96,18 @@ IAM_DEV unsigned long long mix64(unsigned long long z) {
     return z ^ (z >> 31);
 }
 
+// Element i of the tensor is a function of (seed, tensor, i0 + i) only, so any slice of a
+// tensor can be generated on its own (i0 even keeps the Box-Muller pairs aligned).
 __global__ void init_normal_fp16(uint16_t* w, size_t n, unsigned long long seed, unsigned long long tensor,
-                                 float stddev) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+                                 float stddev, size_t i0 = 0) {
+    for (size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x; j < n; j += (size_t)gridDim.x * blockDim.x) {
+        const size_t i = i0 + j;
         const unsigned long long h = mix64(seed ^ mix64(tensor * 0x100000001b3ull + (i >> 1)));
         const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
         const float u2 = ((float)((h >> 16) & 0xffffffull) + 0.5f) * (1.0f / 16777216.0f);
         const float r = sqrtf(-2.0f * logf(u1));
         const float z = (i & 1) ? r * sinpif(2.0f * u2) : r * cospif(2.0f * u2);
-        w[i] = __half_as_ushort(__float2half_rn(z * stddev));
+        w[j] = __half_as_ushort(__float2half_rn(z * stddev));
     }
 }
 
@@ -89,6 +139,9 @@ struct iam_model_s {
     int device = 0;
     int sm_count = 148;
     int tp_rank = 0, tp_world = 1;
+    ncclComm_t comm = nullptr;  // tensor-parallel group (world > 1)
+    double tp_timeout_s = 300.0;
+    int vocab0 = 0, vocab_local = 0;  // LM head rows held
     uint16_t* embed = nullptr;
     uint16_t* final_norm = nullptr;
     uint16_t* lm_head = nullptr;
@@ -123,6 +176,7 @@ struct iam_model_s {
     int* gen_tokens = nullptr;
     std::vector<void*> allocs;
     int n_heads_local = 0, n_kv_local = 0, ffn_local = 0;
+    long long* tp_tmp = nullptr;  // 2 int64 of device scratch for host-side agreements
 };
 
 namespace {
@@ -218,26 +272,91 @@ int alloc_runtime(iam_model_s* m) {
 }
 
 void free_model(iam_model_s* m) {
-    if (m->gen_graph) cudaGraphExecDestroy(m->gen_graph);
+    if (m->gen_graph) cudaGraphExecDestroy(m->gen_graph);  // holds NCCL work: released first
+    if (m->comm) {
+        cudaDeviceSynchronize();
+        ncclResult_t st = ncclSuccess;
+        ncclCommGetAsyncError(m->comm, &st);
+        if (st == ncclSuccess) ncclCommDestroy(m->comm);
+        else ncclCommAbort(m->comm);
+    }
     for (void* p : m->allocs) cudaFree(p);
     delete m;
 }
 
-int make_matrix_random(iam_model_s* m, Matrix& mat, int out_dim, int in_dim, unsigned long long seed,
-                       unsigned long long tensor, uint16_t* wtmp) {
+// Waits (bounded) for a call on the non-blocking communicator to finish.
+int nccl_done(iam_model_s* m, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return IAM_OK;
+    if (r != ncclInProgress) return fail(IAM_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclCommGetAsyncError(m->comm, &st);
+        if (st == ncclSuccess) return IAM_OK;
+        if (st != ncclInProgress) return fail(IAM_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(st));
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > m->tp_timeout_s) {
+            ncclCommAbort(m->comm);
+            m->comm = nullptr;
+            return fail(IAM_ERR_TIMEOUT, std::string(what) + ": peers did not answer in time");
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+}
+
+int tp_allgather(iam_model_s* m, float* buf, size_t per_rank, cudaStream_t s) {
+    return nccl_done(m, ncclAllGather(buf + (size_t)m->tp_rank * per_rank, buf, per_rank, ncclFloat, m->comm, s),
+                     "ncclAllGather");
+}
+
+int tp_allreduce_sum(iam_model_s* m, float* buf, size_t n, cudaStream_t s) {
+    return nccl_done(m, ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, m->comm, s), "ncclAllReduce");
+}
+
+// Every rank of the group learns whether all ranks got here with rc == IAM_OK (a rank that
+// failed to build still takes part, so no rank waits on it in a later collective).
+int tp_agree(iam_model_s* m, int rc) {
+    if (m->tp_world == 1) return rc;
+    long long h[2] = {rc != IAM_OK ? 1 : 0, 0};
+    IAM_CUDA_TRY(cudaMemcpy(m->tp_tmp, h, sizeof(h), cudaMemcpyHostToDevice));
+    int r2 = nccl_done(m, ncclAllReduce(m->tp_tmp, m->tp_tmp, 1, ncclInt64, ncclMax, m->comm, 0), "status all-reduce");
+    if (r2) return r2;
+    IAM_CUDA_TRY(cudaMemcpy(h, m->tp_tmp, sizeof(h), cudaMemcpyDeviceToHost));
+    if (rc) return rc;
+    if (h[0]) return fail(IAM_ERR_UNSUPPORTED, "tensor parallel: another rank failed to build its shard");
+    return IAM_OK;
+}
+
+// Full matrix from (seed, tensor), bucketized whole (so stats, probes and the bucket layout
+// are those of the unsharded model), then this rank's shard kept.
+int make_matrix_random(iam_model_s* m, Matrix& mat, int which, unsigned long long seed, unsigned long long tensor,
+                       uint16_t* wtmp, uint16_t* btmp) {
+    int out_dim, in_dim;
+    matrix_dims(m->cfg, which, &out_dim, &in_dim);
+    const Shard sh = shard_of(m->cfg, which, m->tp_rank, m->tp_world);
     mat.in_dim = in_dim;
     mat.out_dim = out_dim;
-    mat.cols = out_dim / 16;
-    mat.in_begin = 0;
-    mat.in_end = in_dim;
+    mat.cols = sh.cols;
+    mat.in_begin = sh.in0;
+    mat.in_end = sh.in1;
     int rc;
-    if ((rc = dalloc(m, &mat.buckets, (size_t)16 * in_dim * mat.cols)) || (rc = dalloc(m, &mat.stats, (size_t)16 * in_dim)) ||
-        (rc = dalloc(m, &mat.probes, (size_t)in_dim)))
+    if ((rc = dalloc(m, &mat.buckets, (size_t)16 * (sh.in1 - sh.in0) * sh.cols)) ||
+        (rc = dalloc(m, &mat.stats, (size_t)16 * in_dim)) || (rc = dalloc(m, &mat.probes, (size_t)in_dim)))
         return rc;
     const size_t n = (size_t)out_dim * in_dim;
     init_normal_fp16<<<4 * m->sm_count, 256>>>(wtmp, n, seed, tensor, 0.02f);
     IAM_CUDA_TRY(cudaGetLastError());
-    return bucketize_launch(wtmp, out_dim, in_dim, mat.buckets, nullptr, mat.stats, mat.probes, 0);
+    if (m->tp_world == 1) return bucketize_launch(wtmp, out_dim, in_dim, mat.buckets, nullptr, mat.stats, mat.probes, 0);
+    if ((rc = bucketize_launch(wtmp, out_dim, in_dim, btmp, nullptr, mat.stats, mat.probes, 0))) return rc;
+    const int C = out_dim / 16;
+    if (column_parallel(which)) {
+        slice_cols_kernel<<<4 * m->sm_count, 256>>>(btmp, 16 * in_dim, C, sh.col0, sh.cols, mat.buckets);
+        IAM_CUDA_TRY(cudaGetLastError());
+    } else {
+        IAM_CUDA_TRY(cudaMemcpy(mat.buckets, btmp + (size_t)16 * sh.in0 * C, (size_t)16 * (sh.in1 - sh.in0) * C * 2,
+                                cudaMemcpyDeviceToDevice));
+    }
+    return IAM_OK;
 }
 
 // ------------------------------------------------------------------ reference file format
@@ -325,11 +444,19 @@ int load_matrix(iam_model_s* m, const std::string& dir, int layer, int which, in
         return rc;
     std::vector<uint16_t> s1((size_t)mt.s1);
     for (size_t r = 0; r < s1.size(); ++r) s1[r] = s[r * (size_t)mt.s2 + (size_t)(mt.s2 - 1)];  // channel 3
+    const Shard sh = shard_of(m->cfg, which, m->tp_rank, m->tp_world);
     mat.in_dim = in_dim;
     mat.out_dim = out_dim;
-    mat.cols = out_dim / 16;
-    mat.in_begin = 0;
-    mat.in_end = in_dim;
+    mat.cols = sh.cols;
+    mat.in_begin = sh.in0;
+    mat.in_end = sh.in1;
+    if (m->tp_world > 1) {  // keep this rank's shard of the bucket rows / columns
+        const size_t C = (size_t)out_dim / 16;
+        std::vector<uint16_t> part((size_t)16 * (sh.in1 - sh.in0) * sh.cols);
+        for (size_t r = 0; r < (size_t)16 * (sh.in1 - sh.in0); ++r)
+            std::memcpy(&part[r * sh.cols], &b[((size_t)16 * sh.in0 + r) * C + sh.col0], (size_t)sh.cols * 2);
+        b.swap(part);
+    }
     if ((rc = upload(m, &mat.buckets, b)) || (rc = upload(m, &mat.stats, s1))) return rc;
     p.resize((size_t)in_dim);
     return upload(m, &mat.probes, p);
@@ -370,7 +497,7 @@ int build_plans(iam_model_s* m, float effort) {
         qkv.nprob = 3;
         qkv.mode = kModeFused;
         qkv.xmode = kXRms;
-        float* outs[3] = {m->q, m->k, m->v};
+        float* outs[3] = {m->q, m->k, m->v};  // this rank's heads
         for (int i = 0; i < 3; ++i) {
             fill_problem(m, qkv.p[i], L.m[MQ + i], effort, outs[i], i);
             qkv.p[i].x = m->x;
@@ -387,8 +514,8 @@ int build_plans(iam_model_s* m, float effort) {
         o.mode = kModeFused;
         o.xmode = kXPlain;
         fill_problem(m, o.p[0], L.m[MO], effort, m->x1, 0);
-        o.p[0].x = m->att;
-        o.p[0].residual = m->tp_world == 1 ? m->x : nullptr;
+        o.p[0].x = m->att;  // every head (gathered under tensor parallelism)
+        o.p[0].residual = m->tp_rank == 0 ? m->x : nullptr;  // added once; the all-reduce sums the ranks
         o.p[0].count_out = sel + MO;
         bm_plan(o, m->vec, m->G, mac);
 
@@ -397,7 +524,8 @@ int build_plans(iam_model_s* m, float effort) {
         gu.nprob = 2;
         gu.mode = kModeFused;
         gu.xmode = kXRms;
-        float* gouts[2] = {m->g, m->u};
+        const size_t f0 = (size_t)m->tp_rank * m->ffn_local;  // this rank's FFN slice
+        float* gouts[2] = {m->g + f0, m->u + f0};
         for (int i = 0; i < 2; ++i) {
             fill_problem(m, gu.p[i], L.m[MG + i], effort, gouts[i], i);
             gu.p[i].x = m->x1;
@@ -416,7 +544,7 @@ int build_plans(iam_model_s* m, float effort) {
         fill_problem(m, d.p[0], L.m[MD], effort, m->x, 0);
         d.p[0].x = m->g;
         d.p[0].x2 = m->u;
-        d.p[0].residual = m->tp_world == 1 ? m->x1 : nullptr;
+        d.p[0].residual = m->tp_rank == 0 ? m->x1 : nullptr;
         d.p[0].count_out = sel + MD;
         bm_plan(d, m->vec, m->G, mac);
     }
@@ -472,7 +600,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         ap.v_cache = m->v_cache + (size_t)l * layer_kv;
         ap.rope = m->rope;
         ap.pos_dev = m->pos;
-        ap.out = m->att;
+        ap.out = m->att + (size_t)m->tp_rank * m->n_heads_local * c.head_dim;
         ap.part = m->att_part;
         ap.ctr = m->att_ctr;
         ap.n_kv_heads = m->n_kv_local;
@@ -483,32 +611,51 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
         if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
         for (int b = 1; b < 4; ++b) {
+            if (m->tp_world > 1) {  // the exchange in front of launch b
+                if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+                if (b == 1) rc = tp_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
+                else if (b == 2) rc = tp_allreduce_sum(m, m->x1, c.dim, s);
+                else {
+                    if ((rc = nccl_done(m, ncclGroupStart(), "ncclGroupStart"))) return rc;
+                    ncclAllGather(m->g + (size_t)m->tp_rank * m->ffn_local, m->g, m->ffn_local, ncclFloat, m->comm, s);
+                    ncclAllGather(m->u + (size_t)m->tp_rank * m->ffn_local, m->u, m->ffn_local, ncclFloat, m->comm, s);
+                    rc = nccl_done(m, ncclGroupEnd(), "ncclAllGather (gate, up)");
+                }
+                if (rc) return rc;
+            }
             if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
             m->plans[l * 4 + b].pdl = pdl;
             if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->G, s))) return rc;
         }
+        if (m->tp_world > 1) {
+            if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+            if ((rc = tp_allreduce_sum(m, m->x, c.dim, s))) return rc;
+        }
     }
     LMHeadParams hp{};
-    hp.W = m->lm_head;
+    hp.W = m->lm_head;  // this rank's vocabulary rows
     hp.x = m->x;
     hp.gain = m->final_norm;
     hp.eps = c.norm_eps;
     hp.dim = c.dim;
-    hp.rows = c.vocab;
-    hp.logits = logits;
+    hp.rows = m->vocab_local;
+    hp.row0 = m->vocab0;
+    hp.logits = logits ? logits + m->vocab0 : nullptr;
     hp.argmax_key = m->key;
     if ((rc = hook(hk, IAM_KERNEL_LM_HEAD, s))) return rc;
-    return launch_lm_head(hp, 2 * m->sm_count, s, pdl);
+    if ((rc = launch_lm_head(hp, 2 * m->sm_count, s, pdl))) return rc;
+    if (m->tp_world > 1) {  // the greedy token: max of the packed (logit, index) keys
+        if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+        if ((rc = nccl_done(m, ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s), "argmax all-reduce")))
+            return rc;
+        if (logits && (rc = tp_allgather(m, logits, m->vocab_local, s))) return rc;
+    }
+    return IAM_OK;
 }
 
 bool effort_ok(float e) { return std::isfinite(e) && e > 0.0f && e <= 1.0f; }
 
 int finish_create(iam_model_s* m, iam_model_t* out) {
-    int rc = alloc_runtime(m);
-    if (rc) {
-        free_model(m);
-        return rc;
-    }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         free_model(m);
@@ -518,18 +665,35 @@ int finish_create(iam_model_s* m, iam_model_t* out) {
     return IAM_OK;
 }
 
-int init_common(iam_model_s* m, const iam_model_config* cfg, int device) {
+int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int rank = 0, int world = 1,
+                const unsigned char* nccl_id = nullptr) {
     int rc = check_cfg(cfg);
     if (rc) return rc;
+    if ((rc = check_tp(*cfg, rank, world))) return rc;
     rc = iam_device_info(device, &m->sm_count, nullptr, nullptr);
     if (rc) return rc;
     IAM_CUDA_TRY(cudaSetDevice(device));
     m->cfg = *cfg;
     m->device = device;
+    m->tp_rank = rank;
+    m->tp_world = world;
     if (const char* v = getenv("IAM_PDL")) m->pdl = atoi(v) != 0;
-    m->n_heads_local = cfg->n_heads;
-    m->n_kv_local = cfg->n_kv_heads;
-    m->ffn_local = cfg->ffn_dim;
+    if (const char* v = getenv("IAM_TP_TIMEOUT_S")) m->tp_timeout_s = atof(v);
+    m->n_heads_local = cfg->n_heads / world;
+    m->n_kv_local = cfg->n_kv_heads / world;
+    m->ffn_local = cfg->ffn_dim / world;
+    m->vocab_local = cfg->vocab / world;
+    m->vocab0 = rank * m->vocab_local;
+    if (world > 1) {
+        if (!nccl_id) return fail(IAM_ERR_ARG, "tensor parallel: null NCCL id");
+        if ((rc = dalloc(m, &m->tp_tmp, 2))) return rc;
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+        conf.blocking = 0;  // bounded wait for the peers instead of blocking forever
+        if ((rc = nccl_done(m, ncclCommInitRankConfig(&m->comm, world, id, rank, &conf), "ncclCommInitRank")))
+            return rc;
+    }
     m->layers.assign(cfg->n_layers, Layer{});
     const char* g = getenv("IAM_BM_CLUSTER");
     m->G = g && *g ? atoi(g) : bm_default_cluster();
@@ -538,35 +702,28 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device) {
     return IAM_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed, int device) {
+int create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed, int device, int rank,
+                  int world, const unsigned char* nccl_id) {
     if (!out) return fail(IAM_ERR_ARG, "iam_model_create_random: null out");
     *out = nullptr;
     iam_model_s* m = new iam_model_s();
-    int rc = init_common(m, cfg, device);
+    int rc = init_common(m, cfg, device, rank, world, nccl_id);
     if (rc) {
-        delete m;
-        return rc;
-    }
-    const iam_model_config& c = m->cfg;
-    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim;
-    const size_t wmax = (size_t)std::max(std::max(qn, c.dim), c.ffn_dim) * std::max(c.dim, c.ffn_dim);
-    uint16_t* wtmp = nullptr;
-    if ((rc = dalloc(m, &wtmp, wmax))) {
         free_model(m);
         return rc;
     }
+    const iam_model_config& c = m->cfg;
+    const int qn = c.n_heads * c.head_dim;
+    const size_t wmax = (size_t)std::max(std::max(qn, c.dim), c.ffn_dim) * std::max(c.dim, c.ffn_dim);
+    uint16_t *wtmp = nullptr, *btmp = nullptr;  // full matrix and, when sharding, its full buckets
+    cudaError_t e = cudaMalloc(&wtmp, wmax * 2);
+    if (e == cudaSuccess && world > 1) e = cudaMalloc(&btmp, wmax * 2);
+    if (e != cudaSuccess) rc = cuda_fail(e, "model build scratch");
     const uint16_t one = 0x3c00;  // fp16 1.0: RMSNorm gains
     unsigned long long tensor = 1;
     for (int l = 0; l < c.n_layers && !rc; ++l) {
         Layer& L = m->layers[l];
-        const int outs[NMAT] = {qn, kvn, kvn, c.dim, c.ffn_dim, c.ffn_dim, c.dim};
-        const int ins[NMAT] = {c.dim, c.dim, c.dim, qn, c.dim, c.dim, c.ffn_dim};
-        for (int i = 0; i < NMAT && !rc; ++i)
-            rc = make_matrix_random(m, L.m[i], outs[i], ins[i], seed, tensor++, wtmp);
+        for (int i = 0; i < NMAT && !rc; ++i) rc = make_matrix_random(m, L.m[i], i, seed, tensor++, wtmp, btmp);
         if (!rc && !(rc = dalloc(m, &L.attn_norm, c.dim)) && !(rc = dalloc(m, &L.ffn_norm, c.dim))) {
             fill_u16<<<8, 256>>>(L.attn_norm, c.dim, one);
             fill_u16<<<8, 256>>>(L.ffn_norm, c.dim, one);
@@ -575,10 +732,19 @@ int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsig
     if (!rc && !(rc = dalloc(m, &m->embed, (size_t)c.vocab * c.dim)) && !(rc = dalloc(m, &m->final_norm, c.dim))) {
         init_normal_fp16<<<4 * m->sm_count, 256>>>(m->embed, (size_t)c.vocab * c.dim, seed, 0, 0.02f);
         fill_u16<<<8, 256>>>(m->final_norm, c.dim, one);
-        m->lm_head = m->embed;  // tied embeddings
-        if (!c.tied_embeddings && !(rc = dalloc(m, &m->lm_head, (size_t)c.vocab * c.dim)))
-            init_normal_fp16<<<4 * m->sm_count, 256>>>(m->lm_head, (size_t)c.vocab * c.dim, seed, tensor++, 0.02f);
+        m->lm_head = m->embed + (size_t)m->vocab0 * c.dim;  // tied embeddings
+        if (!c.tied_embeddings && !(rc = dalloc(m, &m->lm_head, (size_t)m->vocab_local * c.dim)))
+            init_normal_fp16<<<4 * m->sm_count, 256>>>(m->lm_head, (size_t)m->vocab_local * c.dim, seed, tensor++,
+                                                       0.02f, (size_t)m->vocab0 * c.dim);
     }
+    if (!rc) {
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) rc = cuda_fail(e, "model build");
+    }
+    cudaFree(wtmp);
+    cudaFree(btmp);
+    if (!rc) rc = alloc_runtime(m);
+    rc = tp_agree(m, rc);
     if (rc) {
         free_model(m);
         return rc;
@@ -586,24 +752,24 @@ int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsig
     return finish_create(m, out);
 }
 
-int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device) {
+int load_model(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device, int rank,
+               int world, const unsigned char* nccl_id) {
     if (!out || !weights_dir) return fail(IAM_ERR_ARG, "iam_model_load: null argument");
     *out = nullptr;
     iam_model_s* m = new iam_model_s();
-    int rc = init_common(m, cfg, device);
+    int rc = init_common(m, cfg, device, rank, world, nccl_id);
     if (rc) {
-        delete m;
+        free_model(m);
         return rc;
     }
     const iam_model_config& c = m->cfg;
     const std::string dir(weights_dir);
-    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim;
+    int dims_out[NMAT], dims_in[NMAT];
+    for (int i = 0; i < NMAT; ++i) matrix_dims(c, i, &dims_out[i], &dims_in[i]);
     std::vector<uint16_t> buf;
     for (int l = 0; l < c.n_layers && !rc; ++l) {
         Layer& L = m->layers[l];
-        const int outs[NMAT] = {qn, kvn, kvn, c.dim, c.ffn_dim, c.ffn_dim, c.dim};
-        const int ins[NMAT] = {c.dim, c.dim, c.dim, qn, c.dim, c.dim, c.ffn_dim};
-        for (int i = 0; i < NMAT && !rc; ++i) rc = load_matrix(m, dir, l, i, outs[i], ins[i], L.m[i]);
+        for (int i = 0; i < NMAT && !rc; ++i) rc = load_matrix(m, dir, l, i, dims_out[i], dims_in[i], L.m[i]);
         const std::string lp = dir + "/layer" + std::to_string(l);
         if (!rc && !(rc = read_npy_u16(lp + "_input_layernorm.npy", c.dim, buf))) rc = upload(m, &L.attn_norm, buf);
         if (!rc && !(rc = read_npy_u16(lp + "_post_attention_layernorm.npy", c.dim, buf))) rc = upload(m, &L.ffn_norm, buf);
@@ -612,16 +778,68 @@ int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_co
     if (!rc && !(rc = read_npy_u16(dir + "/norm_weight.npy", c.dim, buf))) rc = upload(m, &m->final_norm, buf);
     if (!rc) {
         if (c.tied_embeddings) {
-            m->lm_head = m->embed;
+            m->lm_head = m->embed + (size_t)m->vocab0 * c.dim;
         } else if (!(rc = read_npy_u16(dir + "/lm_head.npy", (size_t)c.vocab * c.dim, buf))) {
-            rc = upload(m, &m->lm_head, buf);
+            std::vector<uint16_t> part(buf.begin() + (size_t)m->vocab0 * c.dim,
+                                       buf.begin() + (size_t)(m->vocab0 + m->vocab_local) * c.dim);
+            rc = upload(m, &m->lm_head, part);
         }
     }
+    if (!rc) rc = alloc_runtime(m);
+    rc = tp_agree(m, rc);
     if (rc) {
         free_model(m);
         return rc;
     }
     return finish_create(m, out);
+}
+
+}  // namespace
+
+extern "C" {
+
+int iam_tp_unique_id(unsigned char* id_out) {
+    if (!id_out) return fail(IAM_ERR_ARG, "iam_tp_unique_id: null argument");
+    static_assert(sizeof(ncclUniqueId) == IAM_TP_ID_BYTES, "NCCL id size");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return fail(IAM_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(id_out, &id, sizeof(id));
+    return IAM_OK;
+}
+
+int iam_tp_shard_info(const iam_model_config* cfg, int rank, int world, int* out) {
+    if (!cfg || !out) return fail(IAM_ERR_ARG, "iam_tp_shard_info: null argument");
+    int rc = check_cfg(cfg);
+    if (rc || (rc = check_tp(*cfg, rank, world))) return rc;
+    for (int i = 0; i < NMAT; ++i) {
+        const Shard sh = shard_of(*cfg, i, rank, world);
+        out[4 * i + 0] = sh.col0;
+        out[4 * i + 1] = sh.cols;
+        out[4 * i + 2] = sh.in0;
+        out[4 * i + 3] = sh.in1;
+    }
+    out[4 * NMAT] = rank * (cfg->vocab / world);
+    out[4 * NMAT + 1] = cfg->vocab / world;
+    return IAM_OK;
+}
+
+int iam_model_create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed, int device) {
+    return create_random(out, cfg, seed, device, 0, 1, nullptr);
+}
+
+int iam_model_create_random_tp(iam_model_t* out, const iam_model_config* cfg, unsigned long long seed, int device,
+                               int rank, int world, const unsigned char* nccl_id) {
+    return create_random(out, cfg, seed, device, rank, world, nccl_id);
+}
+
+int iam_model_load(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device) {
+    return load_model(out, weights_dir, cfg, device, 0, 1, nullptr);
+}
+
+int iam_model_load_tp(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device, int rank,
+                      int world, const unsigned char* nccl_id) {
+    return load_model(out, weights_dir, cfg, device, rank, world, nccl_id);
 }
 
 int iam_model_destroy(iam_model_t m) {
@@ -664,7 +882,8 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
     int rc = IAM_OK;
     int done = 0;
     if (!cont) {
-        if ((rc = enqueue_step(m, first_token, start_pos, effort, m->logits, s))) return rc;
+        if ((rc = enqueue_step(m, first_token, start_pos, effort, m->tp_world > 1 ? nullptr : m->logits, s)))
+            return rc;
         if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s, m->pdl))) return rc;
         done = 1;
         if (n_tokens == 1) return IAM_OK;
@@ -679,7 +898,9 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
         if (e == cudaSuccess) {
-            rc = enqueue_step(m, -1, -1, effort, m->logits, cap);
+            // greedy generation needs only the argmax key: under tensor parallelism the
+            // logits all-gather is left out
+            rc = enqueue_step(m, -1, -1, effort, m->tp_world > 1 ? nullptr : m->logits, cap);
             if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, cap, m->pdl);
             e = cudaStreamEndCapture(cap, &graph);
         }
@@ -748,12 +969,13 @@ int iam_model_set_kv(iam_model_t m, int layer, const uint16_t* k_dev, const uint
         return fail(IAM_ERR_ARG, "iam_model_set_kv: bad layer or n_tokens");
     const size_t hd = m->cfg.head_dim, ctx = m->cfg.max_ctx;
     const size_t layer_kv = (size_t)m->n_kv_local * ctx * hd;
+    const size_t h0 = (size_t)m->tp_rank * m->n_kv_local;  // this rank's first kv head
     for (int h = 0; h < m->n_kv_local; ++h) {
         uint16_t* kd = m->k_cache + layer * layer_kv + h * ctx * hd;
         uint16_t* vd = m->v_cache + layer * layer_kv + h * ctx * hd;
-        IAM_CUDA_TRY(cudaMemcpyAsync(kd, k_dev + (size_t)h * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
+        IAM_CUDA_TRY(cudaMemcpyAsync(kd, k_dev + (h0 + h) * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
                                      (cudaStream_t)stream));
-        IAM_CUDA_TRY(cudaMemcpyAsync(vd, v_dev + (size_t)h * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
+        IAM_CUDA_TRY(cudaMemcpyAsync(vd, v_dev + (h0 + h) * n_tokens * hd, n_tokens * hd * 2, cudaMemcpyDefault,
                                      (cudaStream_t)stream));
     }
     return IAM_OK;
@@ -765,7 +987,8 @@ int iam_model_fill_kv_random(iam_model_t m, int n_tokens, unsigned long long see
     for (int l = 0; l < m->cfg.n_layers; ++l)
         for (int h = 0; h < m->n_kv_local; ++h) {
             const size_t off = ((size_t)l * m->n_kv_local + h) * ctx * hd;
-            const unsigned long long t = 0x4b560000ull + ((unsigned long long)l << 8) + h;
+            const unsigned long long hg = (unsigned long long)m->tp_rank * m->n_kv_local + h;  // global kv head
+            const unsigned long long t = 0x4b560000ull + ((unsigned long long)l << 8) + hg;
             init_normal_fp16<<<m->sm_count, 256, 0, (cudaStream_t)stream>>>(m->k_cache + off, n_tokens * hd, seed, 2 * t, 1.0f);
             init_normal_fp16<<<m->sm_count, 256, 0, (cudaStream_t)stream>>>(m->v_cache + off, n_tokens * hd, seed, 2 * t + 1, 1.0f);
         }
@@ -787,7 +1010,7 @@ int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, s
         bytes = (size_t)c.dim * 2;
     } else if (which == IAM_W_LM_HEAD) {
         src = m->lm_head;
-        bytes = (size_t)c.vocab * c.dim * 2;
+        bytes = (size_t)m->vocab_local * c.dim * 2;
     } else {
         if (layer < 0 || layer >= c.n_layers) return fail(IAM_ERR_ARG, "iam_model_read_weight: bad layer");
         const Layer& L = m->layers[layer];
@@ -823,7 +1046,17 @@ int iam_model_selected_rows(iam_model_t m, long long* total) {
     std::vector<int> h((size_t)m->cfg.n_layers * NMAT);
     IAM_CUDA_TRY(cudaMemcpy(h.data(), m->sel, h.size() * sizeof(int), cudaMemcpyDeviceToHost));
     long long t = 0;
-    for (int v : h) t += v;
+    for (size_t i = 0; i < h.size(); ++i) {
+        // column-parallel matrices select the same rows on every rank: count them once
+        if (m->tp_world > 1 && m->tp_rank != 0 && column_parallel((int)(i % NMAT))) continue;
+        t += h[i];
+    }
+    if (m->tp_world > 1) {  // row-parallel selections are per rank: sum over the group
+        IAM_CUDA_TRY(cudaMemcpy(m->tp_tmp, &t, sizeof(t), cudaMemcpyHostToDevice));
+        int rc = nccl_done(m, ncclAllReduce(m->tp_tmp, m->tp_tmp, 1, ncclInt64, ncclSum, m->comm, 0), "selected rows");
+        if (rc) return rc;
+        IAM_CUDA_TRY(cudaMemcpy(&t, m->tp_tmp, sizeof(t), cudaMemcpyDeviceToHost));
+    }
     *total = t;
     return IAM_OK;
 }
@@ -838,13 +1071,13 @@ int iam_model_step_bytes(iam_model_t m, int context, long long* bytes) {
     long long t = 0;
     for (int l = 0; l < c.n_layers; ++l)
         for (int i = 0; i < NMAT; ++i) {
-            const Matrix& mt = m->layers[l].m[i];
-            const long long R = 16LL * mt.in_dim;
-            t += 2LL * h[(size_t)l * NMAT + i] * mt.cols + 2 * R + 4LL * mt.in_dim +
+            const Matrix& mt = m->layers[l].m[i];  // this rank's shard
+            const long long n_in = mt.in_end - mt.in_begin;
+            t += 2LL * h[(size_t)l * NMAT + i] * mt.cols + 2 * 16 * n_in + 4LL * n_in +
                  2LL * std::min(mt.in_dim, IAM_PROBES_COUNT) + 4LL * 16 * mt.cols;
         }
     t += 2LL * c.n_layers * m->n_kv_local * (long long)context * c.head_dim * 2;  // K and V fp16
-    t += 2LL * c.vocab * c.dim;                                                 // LM head
+    t += 2LL * m->vocab_local * c.dim;                                          // LM head rows
     *bytes = t;
     return IAM_OK;
 }
