@@ -314,19 +314,30 @@ def run_decode(args, rank, world):
     n_sweep = max(8, args.steps // 4)
     n_prof = 4
     n_e2e = max(3, min(args.steps, 32))
-    max_ctx = PROMPT_LEN + args.warmup + args.steps + n_sweep * len(sweep) + n_prof + n_e2e + 8
+    # config 4: a 128-token prompt ingested token by token; config 5 (--kv-prefix 8192): a
+    # random fp16 KV prefix, decoding starts after it
+    start = args.kv_prefix if args.kv_prefix > 0 else PROMPT_LEN
+    max_ctx = start + args.warmup + args.steps + n_sweep * len(sweep) + n_prof + n_e2e + 8
     cfg = mistral_cfg(iam, max_ctx)
+    tp = None
+    if world > 1:  # one decode stream, tensor-parallel over the ranks (NCCL inside the library)
+        uid = [iam.tp_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        tp = (rank, world, uid[0])
     t_build = time.perf_counter()
-    model = iam.Model.random(cfg, seed=0)
+    model = iam.Model.random(cfg, seed=0, device=dev.index, tp=tp)
     build_s = time.perf_counter() - t_build
     stream = torch.cuda.current_stream()
     logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
-    prompt = prompt_tokens(cfg.vocab)
-    for pos, tok in enumerate(prompt):  # token-by-token prompt ingestion (test_generation.cpp:202-210)
-        model.forward(tok, pos, args.effort, logits)
+    if args.kv_prefix > 0:
+        model.fill_kv_random(args.kv_prefix, seed=1)
+        model.forward(int(prompt_tokens(cfg.vocab)[0]), start - 1, args.effort, logits)
+    else:
+        for pos, tok in enumerate(prompt_tokens(cfg.vocab)):  # token by token (test_generation.cpp:202-210)
+            model.forward(tok, pos, args.effort, logits)
     first = int(torch.argmax(logits).item())
     toks = torch.empty(max_ctx, dtype=torch.int32, device=dev)
-    model.generate(first, PROMPT_LEN, args.warmup, args.effort, toks)  # includes the graph capture
+    model.generate(first, start, args.warmup, args.effort, toks)  # includes the graph capture
     torch.cuda.synchronize()
 
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -344,10 +355,14 @@ def run_decode(args, rank, world):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t[0])
-    ctx_end = PROMPT_LEN + args.warmup + args.steps
+    ctx_end = start + args.warmup + args.steps
     sel_rows = model.selected_rows()
-    step_bytes = model.step_bytes(ctx_end)
-    tok_s = world * args.steps / (ms * 1e-3)
+    step_bytes = model.step_bytes(ctx_end)  # this rank's share
+    if world > 1:
+        t = torch.tensor([float(step_bytes)], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t)
+        step_bytes = int(t[0])
+    tok_s = args.steps / (ms * 1e-3)  # one token stream, whatever the number of GPUs
 
     # roofline of the fused bucketMul kernel: CUDA events between the kernels of a captured step
     print(f"[bench] timed {args.steps} tokens in {ms:.2f} ms", file=sys.stderr, flush=True)
@@ -357,9 +372,9 @@ def run_decode(args, rank, world):
     by_kind = {}
     for k, t in prof:
         by_kind[k] = by_kind.get(k, 0.0) + t
-    total_bytes = model.step_bytes(ctx_end + n_prof)
-    lm_bytes = 2 * cfg.vocab * cfg.dim
-    kv_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * (ctx_end + n_prof) * cfg.head_dim * 2
+    total_bytes = model.step_bytes(ctx_end + n_prof)  # this rank's share
+    lm_bytes = 2 * (cfg.vocab // world) * cfg.dim
+    kv_bytes = 2 * cfg.n_layers * (cfg.n_kv_heads // world) * (ctx_end + n_prof) * cfg.head_dim * 2
     bm_bytes = total_bytes - lm_bytes - kv_bytes
     peak, peak_kind = measured_peaks()
     achieved = bm_bytes / (bm_ms * 1e-3) / 1e9
@@ -384,22 +399,32 @@ def run_decode(args, rank, world):
     pos = int(ctx_end + n_prof + 2 * len(sweep) + n_sweep * len(sweep))
     pos = min(pos, max_ctx - n_e2e - 1)
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     e0 = time.perf_counter()
     for i in range(n_e2e):
-        model.forward(tok, pos + i, args.effort, logits)
+        model.forward(tok, pos + i, args.effort, logits)  # every rank: the same token, gathered logits
         host_logits.copy_(logits, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         tok = int(np.argmax(host_logits.numpy()))
-    e2e_tok_s = world * n_e2e / (time.perf_counter() - e0)
+    e2e_s = time.perf_counter() - e0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t[0])
+    e2e_tok_s = n_e2e / e2e_s
 
     res = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
-                               "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": ("decode: config 5 context, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
+                                f"tied embeddings, greedy batch-1 decode after a random fp16 KV prefix of "
+                                f"{args.kv_prefix} tokens") if args.kv_prefix > 0 else
+                               ("decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
+                                "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)"),
                    "model": "Mistral-7B (random init)", "effort": args.effort, "global_batch": 1,
-                   "seq_len": ctx_end, "parallelism": "replicas" if world > 1 else "single",
+                   "seq_len": ctx_end, "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token",
                    "tokens_per_s_by_effort": sweep_res, "selected_rows_per_step": sel_rows,
                    "algorithmic_bytes_per_step": step_bytes,
@@ -415,12 +440,12 @@ def run_decode(args, rank, world):
                      "ms_per_step_by_kernel": {k: round(v, 4) for k, v in by_kind.items()}},
         "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab},
-        "gpu_launches": args.steps * (2 + 5 * cfg.n_layers + 2),
+        "gpu_launches": world * args.steps * (2 + 5 * cfg.n_layers + 2),  # ours; NCCL's own kernels not counted
         "clocks": clk.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU port runs on rank 0 at N=1 only
         res["cpu_baseline"] = cpu_baseline_decode(model, cfg, args.effort, budget_s=args.cpu_seconds)
-    model.close()
+    model.close()  # its captured graph holds NCCL work: released before the process group
     return res
 
 
@@ -508,6 +533,8 @@ def main():
     ap.add_argument("--effort", type=float, default=0.25)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-prefix", type=int, default=0,
+                    help="decode after a random KV prefix of this many tokens (config 5: 8192) instead of the prompt")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

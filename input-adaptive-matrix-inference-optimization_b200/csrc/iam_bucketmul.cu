@@ -33,7 +33,11 @@ constexpr int kCH = 2048;  // rows per staged chunk
 #define IAM_BM_RING 8
 #endif
 constexpr int kD = IAM_BM_RING;  // rows per lane in flight (register ring; 8 fits 128 registers)
-constexpr int kSumBatch = 16;  // split partials loaded at once by the last cluster
+constexpr int kSumBatch = 16;
+#ifndef IAM_BM_EARLY_ROWS
+#define IAM_BM_EARLY_ROWS 256
+#endif
+constexpr int kEarlyRows = IAM_BM_EARLY_ROWS;  // selected rows per CTA prefetched to L2 before the numbering  // split partials loaded at once by the last cluster
 
 // Threads per CTA for a vector width: the lane accumulators (16 slots x VEC floats per
 // lane) fill 128 KB of shared memory either way; narrower loads buy more warps.
@@ -157,12 +161,24 @@ __global__ void __launch_bounds__(Threads<VEC>::value, 1) bm_fused_kernel(const 
     int S, list_lo = 0;
     if (!from_list) {
         int iters = 0;
-        const float cutoff =
-            block_find_cutoff<NT>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters, dbg ? dbg + 8 : nullptr);
+        // the warps outside the cutoff search compute the row importances of the first
+        // NT - 128 inputs of this CTA's segment meanwhile; only the comparisons wait
+        constexpr int kSearch = 128, kPre = NT - kSearch;
+        float pimp[16];
+        int pin = -1;
+        auto side = [&]() {
+            const int i = i0 + (tid - kSearch);
+            if (i < i1) {
+                input_importances(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i, pimp);
+                pin = i;
+            }
+        };
+        const float cutoff = block_find_cutoff<NT, 4>(xp, pr.probes, pr.P, pr.target, hdr.cut, &iters,
+                                                      dbg ? dbg + 8 : nullptr, side);
         stamp(dbg, 1);
         stamp(tr, 1);
-        const int n = block_masks<NT>(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i0, i1, cutoff,
-                                      masks, hdr.scan);
+        const int n = block_masks_pre<NT>(xp, pr.stats, pr.stats_stride, row0, pr.n_rows_valid, i0, i1, kPre, cutoff,
+                                          pin, pimp, masks, hdr.scan);
         block_write_rows_local<NT>(masks, i0, i1, rows16, hdr.scan);
         if (tid == 0) {
             hdr.my_count = n;

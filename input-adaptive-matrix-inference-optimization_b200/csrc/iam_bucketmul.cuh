@@ -45,10 +45,16 @@ IAM_DEV void debug_stamp(long long* dbg, int k) {
     }
 }
 
-template <int NT, int NWC = 4, class XP>
+struct NoSideTask {
+    IAM_DEV void operator()() const {}
+};
+
+// side(): work for the warps outside the search (anything that does not need the cutoff),
+// run while the NWC search warps bisect.
+template <int NT, int NWC = 4, class XP, class Side = NoSideTask>
 __device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ probes, int P,
                                    int target, CutoffShared<NT>& sm, int* iters_out,
-                                   long long* dbg = nullptr) {
+                                   long long* dbg = nullptr, const Side& side = Side()) {
     static_assert(NWC * 32 <= NT, "cutoff warps exceed the block");
     constexpr int NCT = NWC * 32;
     constexpr int VPT = (kProbes + NCT - 1) / NCT;
@@ -120,30 +126,26 @@ __device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ pr
             int cnt = 0;
 #pragma unroll
             for (int w = 0; w < NWC; ++w) cnt += sm.cnt[it & 1][w];
-            if (cnt < target) {
-                hi = mid;
-                max_count = cnt;
-            } else {
-                lo = mid;
-                min_count = cnt;
-            }
+            // the update of :150-213 with selects instead of branches
+            const bool below = cnt < target;
+            hi = below ? mid : hi;
+            max_count = below ? cnt : max_count;
+            lo = below ? lo : mid;
+            min_count = below ? min_count : cnt;
             const float next = bisect_mid(lo, hi);
             ++it;
-            if (cnt == target || __fsub_rn(hi, lo) < 1e-5f || abs(max_count - min_count) < 3) {
-                result = mid;  // the mid that was tested (:198)
-                break;
-            }
-            mid = next;
-            if (it == kMaxIters) {
-                result = mid;  // bounds[2] after the last update (:211-213)
-                break;
-            }
+            const bool stop = (cnt == target) | (__fsub_rn(hi, lo) < 1e-5f) | (abs(max_count - min_count) < 3);
+            result = stop ? mid : next;  // the mid that was tested (:198), else bounds[2] (:211-213)
+            mid = stop ? mid : next;
+            if (stop | (it == kMaxIters)) break;
         }
         if (tid == 0) {
             sm.result = result;
             sm.steps = it;
         }
         debug_stamp(dbg, 1);
+    } else {
+        side();
     }
     __syncthreads();
     const float result = sm.result;
@@ -226,7 +228,9 @@ struct XSilu {
 
 // rsqrt(sum(x^2)/n + eps) with the reduction order of rmsNorm32fast (aux.cl:165-190) when
 // n is a multiple of 256 (256 contiguous runs, then a halving tree), else sequential.
-// Every thread returns the same value.  red must hold 256 floats.
+// Every thread returns the same value.  red must hold 256 floats.  The run loads are issued
+// together (float4 when aligned); the tree levels 16..1 pair the same elements through warp
+// shuffles (lane t + s is thread t + s of warp 0), so the sums are bit-identical.
 template <int NT>
 __device__ float block_rms_scale(const float* __restrict__ x, int n, float eps, float* red) {
     static_assert(NT >= 256, "rms scale needs >= 256 threads");
@@ -234,18 +238,41 @@ __device__ float block_rms_scale(const float* __restrict__ x, int n, float eps, 
     if (n >= 256 && n % 256 == 0) {
         if (tid < 256) {
             const int e = n / 256;
+            const float* xr = x + (size_t)tid * e;
             float s = 0.0f;
-            for (int i = tid * e; i < tid * e + e; ++i) {
-                const float v = __ldg(x + i);
-                s = __fadd_rn(s, __fmul_rn(v, v));
+            if (e % 16 == 0 && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0)) {
+                for (int b = 0; b < e; b += 16) {
+                    float4 q[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) q[k] = __ldg(reinterpret_cast<const float4*>(xr + b) + k);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        s = __fadd_rn(s, __fmul_rn(q[k].x, q[k].x));
+                        s = __fadd_rn(s, __fmul_rn(q[k].y, q[k].y));
+                        s = __fadd_rn(s, __fmul_rn(q[k].z, q[k].z));
+                        s = __fadd_rn(s, __fmul_rn(q[k].w, q[k].w));
+                    }
+                }
+            } else {
+                for (int i = 0; i < e; ++i) {
+                    const float v = __ldg(xr + i);
+                    s = __fadd_rn(s, __fmul_rn(v, v));
+                }
             }
             red[tid] = s;
         }
         __syncthreads();
-        for (int s = 128; s > 0; s >>= 1) {
+        for (int s = 128; s >= 32; s >>= 1) {
             if (tid < s) red[tid] = __fadd_rn(red[tid], red[tid + s]);
             __syncthreads();
         }
+        if (tid < 32) {
+            float v = red[tid];
+#pragma unroll
+            for (int s = 16; s > 0; s >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, s));
+            if (tid == 0) red[0] = v;
+        }
+        __syncthreads();
     } else {
         if (tid == 0) {
             float s = 0.0f;
@@ -298,6 +325,62 @@ __device__ int block_masks(const XP& xp, const uint16_t* __restrict__ stats, int
             for (int r = 0; r < rmax; ++r)
                 if (importance(xi, h2f(__ldg(sp + r * stride))) >= cutoff) mask |= 1u << r;
         }
+        masks[i - i0] = (uint16_t)mask;
+        cnt += __popc(mask);
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (lane == 0) sm.tot[0][warp] = cnt;
+    __syncthreads();
+    int total = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) total += sm.tot[0][w];
+    __syncthreads();
+    return total;
+}
+
+// The 16 row importances 1e5*|x[i]*stats[row]| of one input (-1 for rows past
+// n_rows_valid: never selected, every cutoff is >= 0).
+template <class XP>
+IAM_DEV void input_importances(const XP& xp, const uint16_t* __restrict__ stats, int stride, long long row0,
+                               int n_rows_valid, int i, float* imp) {
+    const float xi = xp(i);
+    const int rmax = min(16, n_rows_valid - i * 16);
+    const uint16_t* sp = stats + (row0 + (long long)i * 16) * stride + (stride - 1);
+    if (stride == 1 && rmax == 16 && ((reinterpret_cast<uintptr_t>(sp) & 15u) == 0)) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(sp));
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(sp + 8));
+        const uint32_t wds[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int r = 0; r < 16; ++r) imp[r] = importance(xi, h2f((r & 1) ? (wds[r >> 1] >> 16) : (wds[r >> 1] & 0xffffu)));
+    } else {
+#pragma unroll
+        for (int r = 0; r < 16; ++r) imp[r] = r < rmax ? importance(xi, h2f(__ldg(sp + r * stride))) : -1.0f;
+    }
+}
+
+// block_masks with the importances of inputs [i0, i0 + npre) computed beforehand (by the
+// warps outside the cutoff search, during the search): thread NWC*32 + t holds input i0 + t
+// in pimp when pin >= 0.  Inputs past i0 + npre are done here by every thread.
+template <int NT, class XP>
+__device__ int block_masks_pre(const XP& xp, const uint16_t* __restrict__ stats, int stride, long long row0,
+                               int n_rows_valid, int i0, int i1, int npre, float cutoff, int pin,
+                               const float* pimp, uint16_t* __restrict__ masks, ScanShared<NT>& sm) {
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int cnt = 0;
+    if (pin >= 0) {
+        unsigned mask = 0u;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) mask |= (pimp[r] >= cutoff) ? (1u << r) : 0u;  // ">=" (:380)
+        masks[pin - i0] = (uint16_t)mask;
+        cnt += __popc(mask);
+    }
+    for (int i = i0 + npre + tid; i < i1; i += NT) {
+        float imp[16];
+        input_importances(xp, stats, stride, row0, n_rows_valid, i, imp);
+        unsigned mask = 0u;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) mask |= (imp[r] >= cutoff) ? (1u << r) : 0u;
         masks[i - i0] = (uint16_t)mask;
         cnt += __popc(mask);
     }

@@ -17,8 +17,6 @@ constexpr int kProbes = IAM_PROBES_COUNT;  // bucketMul.cl:18
 constexpr float kCutoffScale = 100000.0f;  // bucketMul.cl:17
 constexpr int kMaxIters = 20;              // bucketMul.cl:148
 
-// Exact fp16 -> fp32 of raw bits (the 4 slot bits stay part of the value, as in
-// bucketMul.cl:430-431 where the unmasked packed weight is the multiplicand).
 // Asks the L2 to fetch [p, p + bytes) (cp.async.bulk.prefetch.L2; p 16-byte aligned, bytes a
 // multiple of 16).  No registers, no shared memory, no completion to wait for.
 IAM_DEV void prefetch_l2(const void* p, uint32_t bytes) {
@@ -33,6 +31,8 @@ IAM_DEV void prefetch_l2(const void* p, uint32_t bytes) {
 IAM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 IAM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Exact fp16 -> fp32 of raw bits (the 4 slot bits stay part of the value, as in
+// bucketMul.cl:430-431 where the unmasked packed weight is the multiplicand).
 IAM_DEV float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
 // 1e5 * |x * s| with both multiplies rounded separately (bucketMul.cl:110, :378).

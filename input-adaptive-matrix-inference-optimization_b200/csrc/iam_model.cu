@@ -300,7 +300,9 @@ int nccl_done(iam_model_s* m, ncclResult_t r, const char* what) {
             m->comm = nullptr;
             return fail(IAM_ERR_TIMEOUT, std::string(what) + ": peers did not answer in time");
         }
-        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        // an enqueue finishes in microseconds: spin first, sleep only on long waits (peers joining)
+        if (el < 0.02) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::milliseconds(1));
     }
 }
 
