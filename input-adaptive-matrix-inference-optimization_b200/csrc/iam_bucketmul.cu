@@ -33,11 +33,7 @@ constexpr int kCH = 2048;  // rows per staged chunk
 #define IAM_BM_RING 8
 #endif
 constexpr int kD = IAM_BM_RING;  // rows per lane in flight (register ring; 8 fits 128 registers)
-constexpr int kSumBatch = 16;
-#ifndef IAM_BM_EARLY_ROWS
-#define IAM_BM_EARLY_ROWS 256
-#endif
-constexpr int kEarlyRows = IAM_BM_EARLY_ROWS;  // selected rows per CTA prefetched to L2 before the numbering  // split partials loaded at once by the last cluster
+constexpr int kSumBatch = 16;  // split partials loaded at once by the last cluster
 
 // Threads per CTA for a vector width: the lane accumulators (16 slots x VEC floats per
 // lane) fill 128 KB of shared memory either way; narrower loads buy more warps.
