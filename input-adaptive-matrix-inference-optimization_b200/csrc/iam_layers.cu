@@ -73,35 +73,59 @@ IAM_DEV void load_half_vec(const uint16_t* p, float* o) {
     }
 }
 
-// grid = n_kv_heads * n_split, block = kAttnThreads.  The context [0, pos] is cut into
-// `active` chunks of at least kAttnMinChunk tokens (active <= n_split); CTA (kvh, s < active)
-// handles chunk s for the GQ query heads that share KV head kvh: warps take tokens round
-// robin, each lane holds head_dim/32 dimensions, kAttnTU tokens in flight per warp.  The
-// last of the active CTAs of a KV head combines the chunks in chunk order.
+// Loads 2*NV halves (16-byte aligned when NV >= 4) as floats.
+template <int VD>
+IAM_DEV void load_halves(const uint16_t* p, float* o) {
+    if constexpr (VD % 8 == 0) {
+#pragma unroll
+        for (int c = 0; c < VD; c += 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(p + c);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                o[c + 2 * e] = h2f(w[e] & 0xffffu);
+                o[c + 2 * e + 1] = h2f(w[e] >> 16);
+            }
+        }
+    } else {
+        load_half_vec<VD>(p, o);
+    }
+}
+
+// grid = n_kv_heads * n_split, block = kAttnThreads (16 half-warps).  Single pass over the
+// context (flash-decoding): the tokens [0, pos] are cut into `active` chunks of at least
+// p.min_chunk tokens; CTA (kvh, s < active) runs chunk s for the GQ query heads of KV head kvh.
+// Each half-warp takes kAttnTU tokens at a time (K and V loads issued together, 16 lanes x
+// VD dimensions), reduces the GQ dot products over its 16 lanes, and keeps an online softmax
+// (running max, sum and p.V per head) in registers.  The half-warps are combined in shared
+// memory; with more than one chunk the last CTA of the KV head combines the chunks in chunk
+// order.  The new token's K/V (RoPE'd, rounded through fp16) are appended by the CTA whose
+// chunk holds pos and used from shared memory for that token.
 template <int GQ, int VD>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
-    constexpr int HD = 32 * VD;
-    constexpr int NWA = kAttnThreads / 32;
+    constexpr int HD = 16 * VD;
+    constexpr int NH = kAttnThreads / 16;  // half-warps
     constexpr int TU = kAttnTU;
     const int half = HD / 2;
     pdl_wait();
     const int kvh = blockIdx.x / p.n_split, s = blockIdx.x % p.n_split;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, hw = tid >> 4, hl = tid & 15;
     const int pos = *p.pos_dev;
     const int n_tok = pos + 1;
     int chunk = (n_tok + p.n_split - 1) / p.n_split;
-    if (chunk < kAttnMinChunk) chunk = kAttnMinChunk;
+    if (chunk < p.min_chunk) chunk = p.min_chunk;
     const int active = (n_tok + chunk - 1) / chunk;
     if (s >= active) return;  // takes no part in the combine
     const int t0 = s * chunk, t1 = min(t0 + chunk, n_tok);
-    const int nt = t1 - t0;
 
-    float* qr = sm;                   // [GQ][HD] roped queries
-    float* knew = qr + GQ * HD;       // [HD] roped k at pos, rounded through fp16
-    float* vnew = knew + HD;          // [HD] v at pos, rounded through fp16
-    float* sc = vnew + HD;            // [GQ][chunk_cap] scores, then exp(score - max)
-    float* red = sc + GQ * p.chunk_cap;  // [NWA][GQ][HD] per-warp partial p.V
+    float* qr = sm;                 // [GQ][HD] roped queries
+    float* knew = qr + GQ * HD;     // [HD] roped k at pos, rounded through fp16
+    float* vnew = knew + HD;        // [HD] v at pos, rounded through fp16
+    float* cm = vnew + HD;          // [NH][GQ] half-warp running max
+    float* cl = cm + NH * GQ;       // [NH][GQ] half-warp running sum
+    float* co = cl + NH * GQ;       // [NH][GQ][HD] half-warp p.V
+    float* wgt = co + NH * GQ * HD; // [GQ][n_split] chunk weights (combine)
     const float* cs = p.rope + (size_t)pos * HD;
 
     for (int e = tid; e < GQ * HD; e += kAttnThreads) {
@@ -125,109 +149,109 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
 #pragma unroll
     for (int j = 0; j < GQ; ++j)
 #pragma unroll
-        for (int e = 0; e < VD; ++e) qv[j][e] = qr[j * HD + lane * VD + e];
+        for (int e = 0; e < VD; ++e) qv[j][e] = qr[j * HD + hl * VD + e];
     const float scale_div = sqrtf((float)HD);
 
-    // scores: q.k / sqrt(head_dim), TU tokens per warp in flight
-    for (int tb = warp * TU; tb < nt; tb += NWA * TU) {
-        float kv[TU][VD];
+    float m[GQ], l[GQ], o[GQ][VD];
 #pragma unroll
-        for (int u = 0; u < TU; ++u) {
-            const int t = tb + u;
-            if (t < nt) {
-                if (t0 + t == pos) {
-#pragma unroll
-                    for (int e = 0; e < VD; ++e) kv[u][e] = knew[lane * VD + e];
-                } else {
-                    load_half_vec<VD>(kc + (size_t)(t0 + t) * HD + lane * VD, kv[u]);
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < VD; ++e) kv[u][e] = 0.0f;
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < TU; ++u) {
-#pragma unroll
-            for (int j = 0; j < GQ; ++j) {
-                float dsum = 0.0f;
-#pragma unroll
-                for (int e = 0; e < VD; ++e) dsum = fmaf(qv[j][e], kv[u][e], dsum);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
-                if (lane == 0 && tb + u < nt) sc[j * p.chunk_cap + tb + u] = __fdiv_rn(dsum, scale_div);
-            }
-        }
-    }
-    __syncthreads();
-
-    // per head: max and sum of exp over the chunk (one warp per head)
-    float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (HD + 2);
-    for (int j = warp; j < GQ; j += NWA) {
-        float m = -INFINITY;
-        for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[j * p.chunk_cap + t]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int t = lane; t < nt; t += 32) {
-            const float e = expf(sc[j * p.chunk_cap + t] - m);
-            sc[j * p.chunk_cap + t] = e;
-            l += e;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            stat[j * (HD + 2)] = m;
-            stat[j * (HD + 2) + 1] = l;
-        }
-    }
-    __syncthreads();
-
-    // unnormalised p.V: warps take tokens round robin, lanes hold VD dims of GQ heads
-    float o[GQ][VD];
-#pragma unroll
-    for (int j = 0; j < GQ; ++j)
+    for (int j = 0; j < GQ; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.0f;
 #pragma unroll
         for (int e = 0; e < VD; ++e) o[j][e] = 0.0f;
-    for (int tb = warp * TU; tb < nt; tb += NWA * TU) {
-        float vv[TU][VD];
+    }
+    // warp-uniform trip count (the dot-product shuffles use the full warp); each half-warp
+    // takes TU tokens of its warp's group of 2*TU, masking those past the chunk
+    const int warp = tid >> 5, hwin = (tid >> 4) & 1;
+    constexpr int NWT = kAttnThreads / 32;
+    for (int wb = t0 + warp * 2 * TU; wb < t1; wb += NWT * 2 * TU) {
+        const int tb = wb + hwin * TU;
+        float kv[TU][VD], vv[TU][VD];
 #pragma unroll
         for (int u = 0; u < TU; ++u) {
             const int t = tb + u;
-            if (t < nt && t0 + t != pos) {
-                load_half_vec<VD>(vc + (size_t)(t0 + t) * HD + lane * VD, vv[u]);
+            if (t < t1 && t != pos) {
+                load_halves<VD>(kc + (size_t)t * HD + hl * VD, kv[u]);
+                load_halves<VD>(vc + (size_t)t * HD + hl * VD, vv[u]);
             } else {
 #pragma unroll
-                for (int e = 0; e < VD; ++e) vv[u][e] = (t < nt) ? vnew[lane * VD + e] : 0.0f;
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < TU; ++u) {
-            if (tb + u < nt) {
-#pragma unroll
-                for (int j = 0; j < GQ; ++j) {
-                    const float pw = sc[j * p.chunk_cap + tb + u];
-#pragma unroll
-                    for (int e = 0; e < VD; ++e) o[j][e] = fmaf(pw, vv[u][e], o[j][e]);
+                for (int e = 0; e < VD; ++e) {
+                    kv[u][e] = t < t1 ? knew[hl * VD + e] : 0.0f;
+                    vv[u][e] = t < t1 ? vnew[hl * VD + e] : 0.0f;
                 }
             }
         }
+        float sc[TU][GQ];
+#pragma unroll
+        for (int u = 0; u < TU; ++u)
+#pragma unroll
+            for (int j = 0; j < GQ; ++j) {
+                float d = 0.0f;
+#pragma unroll
+                for (int e = 0; e < VD; ++e) d = fmaf(qv[j][e], kv[u][e], d);
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);  // 16-lane groups
+                sc[u][j] = (tb + u < t1) ? __fdiv_rn(d, scale_div) : -INFINITY;
+            }
+#pragma unroll
+        for (int j = 0; j < GQ; ++j) {
+            float mx = m[j];
+#pragma unroll
+            for (int u = 0; u < TU; ++u) mx = fmaxf(mx, sc[u][j]);
+            if (mx == -INFINITY) continue;  // no token of this group in range yet
+            const float r = expf(m[j] - mx);
+            l[j] *= r;
+#pragma unroll
+            for (int e = 0; e < VD; ++e) o[j][e] *= r;
+#pragma unroll
+            for (int u = 0; u < TU; ++u) {
+                const float pu = expf(sc[u][j] - mx);
+                l[j] += pu;
+#pragma unroll
+                for (int e = 0; e < VD; ++e) o[j][e] = fmaf(pu, vv[u][e], o[j][e]);
+            }
+            m[j] = mx;
+        }
     }
 #pragma unroll
-    for (int j = 0; j < GQ; ++j)
+    for (int j = 0; j < GQ; ++j) {
+        if (hl == 0) {
+            cm[hw * GQ + j] = m[j];
+            cl[hw * GQ + j] = l[j];
+        }
 #pragma unroll
-        for (int e = 0; e < VD; ++e) red[(warp * GQ + j) * HD + lane * VD + e] = o[j][e];
+        for (int e = 0; e < VD; ++e) co[(hw * GQ + j) * HD + hl * VD + e] = o[j][e];
+    }
     __syncthreads();
-    for (int e = tid; e < GQ * HD; e += kAttnThreads) {
-        const int j = e / HD, d = e % HD;
-        float acc = 0.0f;
+    // this chunk: M = max over half-warps, L and O rescaled to M (fixed half-warp order)
+    float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (HD + 2);
+    for (int idx = tid; idx < GQ * HD; idx += kAttnThreads) {
+        const int j = idx / HD, d = idx % HD;
+        float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NWA; ++w) acc += red[(w * GQ + j) * HD + d];
-        stat[j * (HD + 2) + 2 + d] = acc;
+        for (int h = 0; h < NH; ++h) M = fmaxf(M, cm[h * GQ + j]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            const float mh = cm[h * GQ + j];
+            const float w = mh == -INFINITY ? 0.0f : expf(mh - M);
+            L = fmaf(w, cl[h * GQ + j], L);
+            O = fmaf(w, co[(h * GQ + j) * HD + d], O);
+        }
+        if (active == 1) {
+            p.out[(size_t)(kvh * GQ + j) * HD + d] = __fdiv_rn(O, L);
+        } else {
+            if (d == 0) {
+                stat[j * (HD + 2)] = M;
+                stat[j * (HD + 2) + 1] = L;
+            }
+            stat[j * (HD + 2) + 2 + d] = O;
+        }
     }
+    pdl_trigger();
+    if (active == 1) return;
 
     // last active CTA of this KV head combines the chunks in chunk order
-    pdl_trigger();
     __threadfence();
     __syncthreads();
     __shared__ int last;
@@ -236,7 +260,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     if (!last) return;
     __threadfence();
     const float* base = p.part + (size_t)kvh * p.n_split * GQ * (HD + 2);
-    float* wgt = red;  // [GQ][active] chunk weights exp(m_r - M) / L
+    const int lane = tid & 31;
+    constexpr int NWA = kAttnThreads / 32;
     for (int j = warp; j < GQ; j += NWA) {
         float M = -INFINITY;
         for (int r = lane; r < active; r += 32) M = fmaxf(M, __ldcg(base + ((size_t)r * GQ + j) * (HD + 2)));
@@ -361,9 +386,8 @@ int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long 
 }
 
 size_t attention_smem(const AttnParams& p, int gq) {
-    const int hd = p.head_dim;
-    const size_t red = std::max((size_t)(kAttnThreads / 32) * gq * hd, (size_t)gq * p.n_split);
-    return sizeof(float) * ((size_t)gq * hd + 2 * hd + (size_t)gq * p.chunk_cap + red);
+    const size_t hd = p.head_dim, nh = kAttnThreads / 16;
+    return sizeof(float) * ((size_t)gq * hd + 2 * hd + 2 * nh * gq + nh * gq * hd + (size_t)gq * p.n_split);
 }
 
 template <int GQ, int VD>
@@ -377,9 +401,9 @@ int launch_attention_t(const AttnParams& p, size_t smem, cudaStream_t s, bool pd
 template <int GQ>
 int launch_attention_g(const AttnParams& p, size_t smem, cudaStream_t s, bool pdl) {
     switch (p.head_dim) {
-        case 64: return launch_attention_t<GQ, 2>(p, smem, s, pdl);
-        case 128: return launch_attention_t<GQ, 4>(p, smem, s, pdl);
-        case 256: return launch_attention_t<GQ, 8>(p, smem, s, pdl);
+        case 64: return launch_attention_t<GQ, 4>(p, smem, s, pdl);
+        case 128: return launch_attention_t<GQ, 8>(p, smem, s, pdl);
+        case 256: return launch_attention_t<GQ, 16>(p, smem, s, pdl);
         default: return fail(IAM_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
     }
 }

@@ -6,9 +6,9 @@
 
 namespace iam {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnTU = 4;          // tokens in flight per warp
-constexpr int kAttnMinChunk = 32;   // context tokens per CTA at least
+constexpr int kAttnThreads = 256;   // 16 half-warps
+constexpr int kAttnTU = 2;          // tokens per half-warp in flight
+constexpr int kAttnMinChunk = 32;   // context tokens per CTA at least (default of AttnParams::min_chunk)
 constexpr int kHeadThreads = 256;
 
 struct AttnParams {
@@ -22,7 +22,8 @@ struct AttnParams {
     float* out;            // [n_heads][head_dim]
     float* part;           // scratch [n_kv_heads][n_split][gq][head_dim + 2]
     int* ctr;              // [n_kv_heads] zero-initialised, self-resetting
-    int n_kv_heads, head_dim, max_ctx, n_split, chunk_cap;
+    int n_kv_heads, head_dim, max_ctx, n_split;
+    int min_chunk;         // context tokens per CTA at least
 };
 
 struct LMHeadParams {

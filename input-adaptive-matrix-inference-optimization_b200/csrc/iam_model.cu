@@ -163,7 +163,7 @@ struct iam_model_s {
     // attention scratch
     float* att_part = nullptr;
     int* att_ctr = nullptr;
-    int att_split = 32, chunk_cap = 0;
+    int att_split = 32, att_min_chunk = kAttnMinChunk;
     // launch plans for the current effort
     std::vector<BMBatch> plans;  // 4 per layer
     float plan_effort = -1.0f;
@@ -255,13 +255,11 @@ int alloc_runtime(iam_model_s* m) {
     }
     const int gq = c.n_heads / c.n_kv_heads;
     m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, m->n_kv_local)));
-    // a CTA scores at most max(ceil(max_ctx / att_split), kAttnMinChunk) tokens
-    m->chunk_cap = std::max((c.max_ctx + m->att_split - 1) / m->att_split, kAttnMinChunk);
+    if (const char* v = getenv("IAM_ATTN_MIN_CHUNK")) m->att_min_chunk = std::max(1, atoi(v));
     {
         AttnParams probe{};
         probe.head_dim = hd;
         probe.n_split = m->att_split;
-        probe.chunk_cap = m->chunk_cap;
         if (attention_smem(probe, gq) > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "model: max_ctx too large for attention");
     }
     if ((rc = dalloc(m, &m->att_part, (size_t)m->n_kv_local * m->att_split * gq * (hd + 2))) ||
@@ -609,7 +607,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         ap.head_dim = c.head_dim;
         ap.max_ctx = c.max_ctx;
         ap.n_split = m->att_split;
-        ap.chunk_cap = m->chunk_cap;
+        ap.min_chunk = m->att_min_chunk;
         if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
         if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
         for (int b = 1; b < 4; ++b) {
