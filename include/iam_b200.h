@@ -198,6 +198,10 @@ int iam_model_create_random_tp(iam_model_t* out, const iam_model_config* cfg, un
 int iam_model_load_tp(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device,
                       int rank, int world, const unsigned char* nccl_id);
 int iam_model_destroy(iam_model_t m);
+/* Synchronises the device and reports IAM_ERR_TIMEOUT when a tensor-parallel exchange of an
+ * earlier step gave up waiting for a peer (its outputs are then invalid); IAM_OK otherwise.
+ * (No counterpart in the reference: failure detection of the multi-GPU path.) */
+int iam_model_status(iam_model_t m);
 /* MistralModel::reset_caches (model.hpp:233-237): zero the KV cache and the position. */
 int iam_model_reset(iam_model_t m, void* stream);
 /* MistralModel::forward (model.hpp:152-231): one decode step of `token` at `pos`; logits_dev

@@ -215,6 +215,7 @@ _SIGNATURES.update({
     "iam_model_step_bytes": [_vp, _i32, _vp],
     "iam_model_profile_steps": [_vp, _f32, _i32, _vp, _vp, _i32, _vp, _vp],
     "iam_tp_unique_id": [_vp],
+    "iam_model_status": [_vp],
     "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
     "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
     "iam_model_load_tp": [_vp, ctypes.c_char_p, _vp, _i32, _i32, _i32, _vp],
@@ -288,6 +289,10 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def status(self):
+        """Raises IamError(IAM_ERR_TIMEOUT) if a tensor-parallel exchange gave up on a peer."""
+        check(self.lib.iam_model_status(self.h))
 
     def reset(self, stream=None):
         check(self.lib.iam_model_reset(self.h, _stream(stream)))

@@ -24,6 +24,7 @@
 #include "iam_bucketmul_launch.h"
 #include "iam_common.cuh"
 #include "iam_layers.h"
+#include "iam_tp.h"
 
 namespace iam {
 
@@ -177,6 +178,11 @@ struct iam_model_s {
     std::vector<void*> allocs;
     int n_heads_local = 0, n_kv_local = 0, ffn_local = 0;
     long long* tp_tmp = nullptr;  // 2 int64 of device scratch for host-side agreements
+    // one-shot NVLink collectives (IAM_TP_COLL=nccl: NCCL instead)
+    bool tp_p2p = true;
+    char* xwin = nullptr;         // this rank's window (exchanged activations, mailbox, flags)
+    TpWindow win{};
+    std::vector<void*> peer_maps;
 };
 
 namespace {
@@ -238,10 +244,41 @@ int alloc_runtime(iam_model_s* m) {
     std::vector<float> rt = rope_table(c);
     IAM_CUDA_TRY(cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float), cudaMemcpyHostToDevice));
     const int qn = c.n_heads * hd, kvn = c.n_kv_heads * hd;
-    if ((rc = dalloc(m, &m->x, c.dim)) || (rc = dalloc(m, &m->x1, c.dim)) || (rc = dalloc(m, &m->q, qn)) ||
-        (rc = dalloc(m, &m->k, kvn)) || (rc = dalloc(m, &m->v, kvn)) || (rc = dalloc(m, &m->att, qn)) ||
-        (rc = dalloc(m, &m->g, c.ffn_dim)) || (rc = dalloc(m, &m->u, c.ffn_dim)) ||
-        (rc = dalloc(m, &m->logits, c.vocab)) || (rc = dalloc(m, &m->pos, 4)) || (rc = dalloc(m, &m->token_used, 4)) || (rc = dalloc(m, &m->gen_count, 4)) ||
+    if (m->tp_world > 1 && m->tp_p2p) {
+        // the exchanged activations live in one window that the peers map (iam_tp.h)
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            const size_t o = off;
+            off += (bytes + 255) / 256 * 256;
+            return o;
+        };
+        const size_t o_att = take((size_t)qn * 4), o_g = take((size_t)c.ffn_dim * 4), o_u = take((size_t)c.ffn_dim * 4);
+        const size_t o_x1 = take((size_t)c.dim * 4), o_x = take((size_t)c.dim * 4), o_lg = take((size_t)c.vocab * 4);
+        TpWindow& w = m->win;
+        w.rank = m->tp_rank;
+        w.world = m->tp_world;
+        // the largest exchange: the o/down all-reduce (dim), the head all-gather, the gate+up
+        // all-gather (2 x ffn_local) or the logits all-gather (vocab_local)
+        w.mbox_floats = std::max(std::max(c.dim, qn / m->tp_world), std::max(2 * m->ffn_local, m->vocab_local));
+        w.epoch_off = take(4 * kTpCtas);
+        w.err_off = take(4);
+        w.mbox_off = take((size_t)2 * m->tp_world * w.mbox_floats * 8);
+        if ((rc = dalloc(m, &m->xwin, off))) return rc;
+        IAM_CUDA_TRY(cudaMemset(m->xwin, 0, off));
+        w.base[m->tp_rank] = m->xwin;
+        m->att = reinterpret_cast<float*>(m->xwin + o_att);
+        m->g = reinterpret_cast<float*>(m->xwin + o_g);
+        m->u = reinterpret_cast<float*>(m->xwin + o_u);
+        m->x1 = reinterpret_cast<float*>(m->xwin + o_x1);
+        m->x = reinterpret_cast<float*>(m->xwin + o_x);
+        m->logits = reinterpret_cast<float*>(m->xwin + o_lg);
+    } else if ((rc = dalloc(m, &m->x, c.dim)) || (rc = dalloc(m, &m->x1, c.dim)) || (rc = dalloc(m, &m->att, qn)) ||
+               (rc = dalloc(m, &m->g, c.ffn_dim)) || (rc = dalloc(m, &m->u, c.ffn_dim)) ||
+               (rc = dalloc(m, &m->logits, c.vocab))) {
+        return rc;
+    }
+    if ((rc = dalloc(m, &m->q, qn)) || (rc = dalloc(m, &m->k, kvn)) || (rc = dalloc(m, &m->v, kvn)) ||
+        (rc = dalloc(m, &m->pos, 4)) || (rc = dalloc(m, &m->token_used, 4)) || (rc = dalloc(m, &m->gen_count, 4)) ||
         (rc = dalloc(m, &m->key, 2)) || (rc = dalloc(m, &m->sel, (size_t)c.n_layers * NMAT)))
         return rc;
     IAM_CUDA_TRY(cudaMemset(m->pos, 0, 16));
@@ -271,6 +308,11 @@ int alloc_runtime(iam_model_s* m) {
 
 void free_model(iam_model_s* m) {
     if (m->gen_graph) cudaGraphExecDestroy(m->gen_graph);  // holds NCCL work: released first
+    if (!m->peer_maps.empty()) {
+        cudaDeviceSynchronize();
+        for (void* p : m->peer_maps) cudaIpcCloseMemHandle(p);
+        m->peer_maps.clear();
+    }
     if (m->comm) {
         cudaDeviceSynchronize();
         ncclResult_t st = ncclSuccess;
@@ -304,6 +346,10 @@ int nccl_done(iam_model_s* m, ncclResult_t r, const char* what) {
     }
 }
 
+size_t woff(const iam_model_s* m, const float* p) {
+    return (size_t)(reinterpret_cast<const char*>(p) - m->xwin);
+}
+
 int tp_allgather(iam_model_s* m, float* buf, size_t per_rank, cudaStream_t s) {
     return nccl_done(m, ncclAllGather(buf + (size_t)m->tp_rank * per_rank, buf, per_rank, ncclFloat, m->comm, s),
                      "ncclAllGather");
@@ -311,6 +357,38 @@ int tp_allgather(iam_model_s* m, float* buf, size_t per_rank, cudaStream_t s) {
 
 int tp_allreduce_sum(iam_model_s* m, float* buf, size_t n, cudaStream_t s) {
     return nccl_done(m, ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, m->comm, s), "ncclAllReduce");
+}
+
+// Maps every peer's window (CUDA IPC handles exchanged over the NCCL communicator).  Called
+// by every rank once all have built their shards.
+int tp_map_peers(iam_model_s* m) {
+    if (m->tp_world == 1 || !m->tp_p2p) return IAM_OK;
+    if (m->tp_world > kTpMaxWorld) return fail(IAM_ERR_UNSUPPORTED, "tensor parallel: at most 8 ranks");
+    cudaIpcMemHandle_t mine;
+    IAM_CUDA_TRY(cudaIpcGetMemHandle(&mine, m->xwin));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    unsigned char* dev = nullptr;
+    IAM_CUDA_TRY(cudaMalloc(&dev, hb * m->tp_world));
+    std::vector<unsigned char> all(hb * m->tp_world);
+    cudaError_t e = cudaMemcpy(dev + hb * m->tp_rank, &mine, hb, cudaMemcpyHostToDevice);
+    int rc = e == cudaSuccess ? IAM_OK : cuda_fail(e, "tp handle upload");
+    if (!rc) rc = nccl_done(m, ncclAllGather(dev + hb * m->tp_rank, dev, hb, ncclUint8, m->comm, 0), "handle all-gather");
+    if (!rc && (e = cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        rc = cuda_fail(e, "tp handle download");
+    cudaFree(dev);
+    for (int p = 0; p < m->tp_world && !rc; ++p) {
+        if (p == m->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + hb * p, hb);
+        void* ptr = nullptr;
+        if ((e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+            rc = cuda_fail(e, "cudaIpcOpenMemHandle (peer window)");
+        else {
+            m->peer_maps.push_back(ptr);
+            m->win.base[p] = static_cast<char*>(ptr);
+        }
+    }
+    return rc;
 }
 
 // Every rank of the group learns whether all ranks got here with rc == IAM_OK (a rank that
@@ -611,7 +689,13 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
         if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
         for (int b = 1; b < 4; ++b) {
-            if (m->tp_world > 1) {  // the exchange in front of launch b
+            if (m->tp_world > 1 && m->tp_p2p) {  // the exchange in front of launch b (NVLink one-shot)
+                if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+                if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
+                else if (b == 2) rc = tp_allreduce_sum(m->win, woff(m, m->x1), c.dim, s, pdl);
+                else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
+                if (rc) return rc;
+            } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
                 if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
                 if (b == 1) rc = tp_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
                 else if (b == 2) rc = tp_allreduce_sum(m, m->x1, c.dim, s);
@@ -629,7 +713,8 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         }
         if (m->tp_world > 1) {
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-            if ((rc = tp_allreduce_sum(m, m->x, c.dim, s))) return rc;
+            rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : tp_allreduce_sum(m, m->x, c.dim, s);
+            if (rc) return rc;
         }
     }
     LMHeadParams hp{};
@@ -640,11 +725,21 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     hp.dim = c.dim;
     hp.rows = m->vocab_local;
     hp.row0 = m->vocab0;
-    hp.logits = logits ? logits + m->vocab0 : nullptr;
+    // under the NVLink collectives the logits are gathered in the window, then copied out
+    float* lg = (logits && m->tp_world > 1 && m->tp_p2p) ? m->logits : logits;
+    hp.logits = lg ? lg + m->vocab0 : nullptr;
     hp.argmax_key = m->key;
     if ((rc = hook(hk, IAM_KERNEL_LM_HEAD, s))) return rc;
     if ((rc = launch_lm_head(hp, 2 * m->sm_count, s, pdl))) return rc;
-    if (m->tp_world > 1) {  // the greedy token: max of the packed (logit, index) keys
+    if (m->tp_world > 1 && m->tp_p2p) {
+        if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+        if ((rc = tp_keymax(m->win, m->key, s, pdl))) return rc;
+        if (logits) {
+            if ((rc = tp_allgather(m->win, woff(m, m->logits), (size_t)-1, m->vocab_local, s, pdl))) return rc;
+            if (logits != m->logits)
+                IAM_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToDevice, s));
+        }
+    } else if (m->tp_world > 1) {  // the greedy token: max of the packed (logit, index) keys
         if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
         if ((rc = nccl_done(m, ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s), "argmax all-reduce")))
             return rc;
@@ -679,6 +774,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int ran
     m->tp_world = world;
     if (const char* v = getenv("IAM_PDL")) m->pdl = atoi(v) != 0;
     if (const char* v = getenv("IAM_TP_TIMEOUT_S")) m->tp_timeout_s = atof(v);
+    if (const char* v = getenv("IAM_TP_COLL")) m->tp_p2p = std::string(v) != "nccl";
     m->n_heads_local = cfg->n_heads / world;
     m->n_kv_local = cfg->n_kv_heads / world;
     m->ffn_local = cfg->ffn_dim / world;
@@ -745,6 +841,7 @@ int create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long l
     cudaFree(btmp);
     if (!rc) rc = alloc_runtime(m);
     rc = tp_agree(m, rc);
+    if (!rc) rc = tp_agree(m, tp_map_peers(m));
     if (rc) {
         free_model(m);
         return rc;
@@ -787,6 +884,7 @@ int load_model(iam_model_t* out, const char* weights_dir, const iam_model_config
     }
     if (!rc) rc = alloc_runtime(m);
     rc = tp_agree(m, rc);
+    if (!rc) rc = tp_agree(m, tp_map_peers(m));
     if (rc) {
         free_model(m);
         return rc;
@@ -1038,6 +1136,17 @@ int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, s
     if (!host_dst) return IAM_OK;
     if (capacity_bytes < bytes) return fail(IAM_ERR_ARG, "iam_model_read_weight: buffer too small");
     IAM_CUDA_TRY(cudaMemcpy(host_dst, src, bytes, cudaMemcpyDeviceToHost));
+    return IAM_OK;
+}
+
+int iam_model_status(iam_model_t m) {
+    if (!m) return fail(IAM_ERR_ARG, "iam_model_status: null model");
+    IAM_CUDA_TRY(cudaDeviceSynchronize());
+    if (m->xwin) {
+        uint32_t err = 0;
+        IAM_CUDA_TRY(cudaMemcpy(&err, m->xwin + m->win.err_off, sizeof(err), cudaMemcpyDeviceToHost));
+        if (err) return fail(IAM_ERR_TIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+    }
     return IAM_OK;
 }
 

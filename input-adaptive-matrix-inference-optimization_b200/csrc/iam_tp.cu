@@ -1,0 +1,157 @@
+// iam_tp.cu -- one-shot NVLink collectives for the tensor-parallel decode step (see iam_tp.h).
+//
+// Low-latency protocol: every element travels as one 8-byte store {value bits, epoch} into
+// the receiver's mailbox (an aligned 8-byte store is seen whole, so no fence or separate flag
+// is needed); the receiver polls each of its elements (bounded) until the epoch word matches.
+// Every launch has kTpCtas CTAs and each advances its own copy of the epoch, so all copies
+// hold the number of collective calls so far: an epoch names one call on every element, and
+// every rank makes the same sequence of calls.  The mailbox is double-buffered by epoch parity: a sender can only reach
+// epoch e + 2 after every peer finished the launch of epoch e that read the same half.
+#include "iam_common.cuh"
+#include "iam_tp.h"
+
+namespace iam {
+
+namespace {
+
+constexpr long long kSpinLimit = 1LL << 21;  // polls of one element before the wait gives up (~1 s)
+
+IAM_DEV void st_ll(uint2* p, uint32_t bits, uint32_t epoch) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(bits), "r"(epoch) : "memory");
+}
+
+IAM_DEV uint2 ld_ll(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+IAM_DEV uint2* mbox_of(const TpWindow& w, int owner, uint32_t epoch, int src) {
+    return reinterpret_cast<uint2*>(w.base[owner] + w.mbox_off) +
+           ((size_t)(epoch & 1u) * w.world + src) * (size_t)w.mbox_floats;
+}
+
+// Epoch of this launch for slice c (read by the whole CTA).
+IAM_DEV uint32_t begin_epoch(const TpWindow& w, int c, uint32_t* s_epoch) {
+    if (threadIdx.x == 0) *s_epoch = reinterpret_cast<uint32_t*>(w.base[w.rank] + w.epoch_off)[c] + 1u;
+    __syncthreads();
+    return *s_epoch;
+}
+
+IAM_DEV void end_epoch(const TpWindow& w, int c, uint32_t epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) reinterpret_cast<uint32_t*>(w.base[w.rank] + w.epoch_off)[c] = epoch;
+}
+
+// Sends element i of this rank to every peer's mailbox slot (this rank, i).
+IAM_DEV void send(const TpWindow& w, uint32_t epoch, int i, float v) {
+    for (int p = 0; p < w.world; ++p)
+        if (p != w.rank) st_ll(mbox_of(w, p, epoch, w.rank) + i, __float_as_uint(v), epoch);
+}
+
+// Element i from rank r (bounded wait); on a timeout the error word is set and 0 returned.
+// Once this rank has given up on any wait, later exchanges do not wait at all (their outputs
+// are invalid anyway; the host learns of it from iam_model_status).
+IAM_DEV float recv(const TpWindow& w, uint32_t epoch, int r, int i) {
+    volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(w.base[w.rank] + w.err_off);
+    const uint2* q = mbox_of(w, w.rank, epoch, r) + i;
+    long long n = 0;
+    for (;;) {
+        const uint2 v = ld_ll(q);
+        if (v.y == epoch) return __uint_as_float(v.x);
+        if (++n > kSpinLimit || *err != 0u) {
+            *err = 1u;
+            return 0.0f;
+        }
+        if (n > 64) __nanosleep(32);
+    }
+}
+
+__global__ void __launch_bounds__(kTpThreads) tp_allgather_kernel(TpWindow w, size_t off_a, size_t off_b, int chunk) {
+    pdl_wait();
+    __shared__ uint32_t s_epoch;
+    const int c = blockIdx.x;
+    const uint32_t epoch = begin_epoch(w, c, &s_epoch);
+    const int nb = off_b == (size_t)-1 ? 1 : 2;
+    const int n = nb * chunk;  // element e: buffer e / chunk, index e % chunk
+    const int per = (n + kTpCtas - 1) / kTpCtas;
+    const int e0 = min(n, c * per), e1 = min(n, e0 + per);
+    const size_t mine = (size_t)w.rank * chunk;
+    for (int e = e0 + threadIdx.x; e < e1; e += kTpThreads) {
+        const size_t off = e < chunk ? off_a : off_b;
+        send(w, epoch, e, reinterpret_cast<const float*>(w.base[w.rank] + off)[mine + e % chunk]);
+    }
+    for (int e = e0 + threadIdx.x; e < e1; e += kTpThreads) {
+        float* dst = reinterpret_cast<float*>(w.base[w.rank] + (e < chunk ? off_a : off_b));
+        for (int r = 0; r < w.world; ++r)
+            if (r != w.rank) dst[(size_t)r * chunk + e % chunk] = recv(w, epoch, r, e);
+    }
+    pdl_trigger();
+    end_epoch(w, c, epoch);
+}
+
+__global__ void __launch_bounds__(kTpThreads) tp_allreduce_kernel(TpWindow w, size_t off, int n) {
+    pdl_wait();
+    __shared__ uint32_t s_epoch;
+    const int c = blockIdx.x;
+    const uint32_t epoch = begin_epoch(w, c, &s_epoch);
+    const int per = (n + kTpCtas - 1) / kTpCtas;
+    const int i0 = min(n, c * per), i1 = min(n, i0 + per);
+    float* buf = reinterpret_cast<float*>(w.base[w.rank] + off);
+    for (int i = i0 + threadIdx.x; i < i1; i += kTpThreads) send(w, epoch, i, buf[i]);
+    for (int i = i0 + threadIdx.x; i < i1; i += kTpThreads) {
+        float acc = 0.0f;
+        for (int r = 0; r < w.world; ++r) {
+            const float v = r == w.rank ? buf[i] : recv(w, epoch, r, i);
+            acc = r == 0 ? v : acc + v;  // rank order: the same bits on every rank
+        }
+        buf[i] = acc;
+    }
+    pdl_trigger();
+    end_epoch(w, c, epoch);
+}
+
+// The packed argmax key (64 bits) travels as two elements: high and low words.
+__global__ void __launch_bounds__(kTpThreads) tp_keymax_kernel(TpWindow w, unsigned long long* key) {
+    pdl_wait();
+    __shared__ uint32_t s_epoch;
+    const int c = blockIdx.x;  // every CTA advances its epoch; CTA 0 does the work
+    const uint32_t epoch = begin_epoch(w, c, &s_epoch);
+    if (c == 0 && threadIdx.x == 0) {
+        const unsigned long long k = *key;
+        send(w, epoch, 0, __uint_as_float((uint32_t)(k >> 32)));
+        send(w, epoch, 1, __uint_as_float((uint32_t)k));
+        unsigned long long m = k;
+        for (int r = 0; r < w.world; ++r) {
+            if (r == w.rank) continue;
+            const unsigned long long hi = __float_as_uint(recv(w, epoch, r, 0));
+            const unsigned long long lo = __float_as_uint(recv(w, epoch, r, 1));
+            const unsigned long long kr = (hi << 32) | lo;
+            m = kr > m ? kr : m;
+        }
+        *key = m;
+    }
+    pdl_trigger();
+    end_epoch(w, c, epoch);
+}
+
+}  // namespace
+
+int tp_allgather(const TpWindow& w, size_t off_a, size_t off_b, int chunk, cudaStream_t s, bool pdl) {
+    if ((off_b == (size_t)-1 ? 1 : 2) * chunk > w.mbox_floats) return fail(IAM_ERR_UNSUPPORTED, "tp all-gather larger than the mailbox");
+    IAM_CUDA_TRY(launch_ex(tp_allgather_kernel, dim3(kTpCtas), dim3(kTpThreads), 0, s, pdl, w, off_a, off_b, chunk));
+    return IAM_OK;
+}
+
+int tp_allreduce_sum(const TpWindow& w, size_t off, int n, cudaStream_t s, bool pdl) {
+    if (n > w.mbox_floats) return fail(IAM_ERR_UNSUPPORTED, "tp all-reduce larger than the mailbox");
+    IAM_CUDA_TRY(launch_ex(tp_allreduce_kernel, dim3(kTpCtas), dim3(kTpThreads), 0, s, pdl, w, off, n));
+    return IAM_OK;
+}
+
+int tp_keymax(const TpWindow& w, unsigned long long* key, cudaStream_t s, bool pdl) {
+    IAM_CUDA_TRY(launch_ex(tp_keymax_kernel, dim3(kTpCtas), dim3(kTpThreads), 0, s, pdl, w, key));
+    return IAM_OK;
+}
+
+}  // namespace iam

@@ -1,0 +1,37 @@
+// iam_tp.h -- one-shot collectives of the tensor-parallel decode step over NVLink peer memory.
+//
+// Every rank holds one "window" allocation (the exchanged activations, a double-buffered
+// mailbox of 8-byte {value, epoch} elements, per-CTA epochs, an error word); the peers map it
+// through CUDA IPC.  A collective is one launch of kTpCtas CTAs: each element of this rank's
+// data is stored, with the call's epoch beside it, into every peer's mailbox; each rank polls
+// its own mailbox (bounded) until the epochs match.  No multicast, no NVLS: plain peer stores.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace iam {
+
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpCtas = 8;       // CTAs of every collective launch (one epoch copy each)
+constexpr int kTpThreads = 256;
+
+struct TpWindow {
+    char* base[kTpMaxWorld];  // every rank's window (base[rank] is this rank's own)
+    int rank, world;
+    size_t epoch_off;         // u32 [kTpCtas]: this rank's epoch per slice
+    size_t err_off;           // u32: set when a wait gave up
+    size_t mbox_off;          // uint2 [2][world][mbox_floats]: {value bits, epoch} from rank r
+    int mbox_floats;          // elements per mailbox slot
+};
+
+// Rank r's chunk [r*chunk, (r+1)*chunk) of the float buffer(s) at window offset off_a (and
+// off_b unless it is SIZE_MAX) is copied to the same place in every peer.
+int tp_allgather(const TpWindow& w, size_t off_a, size_t off_b, int chunk, cudaStream_t s, bool pdl);
+// buf[0, n) at window offset off := sum over ranks, added in rank order (identical on all ranks).
+int tp_allreduce_sum(const TpWindow& w, size_t off, int n, cudaStream_t s, bool pdl);
+// *key := max over ranks (the packed greedy argmax key).
+int tp_keymax(const TpWindow& w, unsigned long long* key, cudaStream_t s, bool pdl);
+
+}  // namespace iam
