@@ -440,7 +440,11 @@ def run_decode(args, rank, world):
                      "ms_per_step_by_kernel": {k: round(v, 4) for k, v in by_kind.items()}},
         "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab},
-        "gpu_launches": world * args.steps * (2 + 5 * cfg.n_layers + 2),  # ours; NCCL's own kernels not counted
+        # ours per step and rank: embed, key clear, 32 x (4 bucketMul + attention), LM head,
+        # advance; under TP 32 x 4 exchanges + the argmax-key exchange (NVLink one-shot kernels)
+        "gpu_launches": world * args.steps * (2 + 5 * cfg.n_layers + 2 +
+                                              ((4 * cfg.n_layers + 1) if world > 1 and
+                                               os.environ.get("IAM_TP_COLL", "p2p") != "nccl" else 0)),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU port runs on rank 0 at N=1 only
