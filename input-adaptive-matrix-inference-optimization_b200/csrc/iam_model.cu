@@ -350,12 +350,12 @@ size_t woff(const iam_model_s* m, const float* p) {
     return (size_t)(reinterpret_cast<const char*>(p) - m->xwin);
 }
 
-int tp_allgather(iam_model_s* m, float* buf, size_t per_rank, cudaStream_t s) {
+int nccl_allgather(iam_model_s* m, float* buf, size_t per_rank, cudaStream_t s) {
     return nccl_done(m, ncclAllGather(buf + (size_t)m->tp_rank * per_rank, buf, per_rank, ncclFloat, m->comm, s),
                      "ncclAllGather");
 }
 
-int tp_allreduce_sum(iam_model_s* m, float* buf, size_t n, cudaStream_t s) {
+int nccl_allreduce_sum(iam_model_s* m, float* buf, size_t n, cudaStream_t s) {
     return nccl_done(m, ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, m->comm, s), "ncclAllReduce");
 }
 
@@ -697,8 +697,8 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
                 if (rc) return rc;
             } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
                 if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-                if (b == 1) rc = tp_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
-                else if (b == 2) rc = tp_allreduce_sum(m, m->x1, c.dim, s);
+                if (b == 1) rc = nccl_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
+                else if (b == 2) rc = nccl_allreduce_sum(m, m->x1, c.dim, s);
                 else {
                     if ((rc = nccl_done(m, ncclGroupStart(), "ncclGroupStart"))) return rc;
                     ncclAllGather(m->g + (size_t)m->tp_rank * m->ffn_local, m->g, m->ffn_local, ncclFloat, m->comm, s);
@@ -713,7 +713,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         }
         if (m->tp_world > 1) {
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-            rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : tp_allreduce_sum(m, m->x, c.dim, s);
+            rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
             if (rc) return rc;
         }
     }
@@ -743,7 +743,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
         if ((rc = nccl_done(m, ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s), "argmax all-reduce")))
             return rc;
-        if (logits && (rc = tp_allgather(m, logits, m->vocab_local, s))) return rc;
+        if (logits && (rc = nccl_allgather(m, logits, m->vocab_local, s))) return rc;
     }
     return IAM_OK;
 }
