@@ -245,6 +245,10 @@ int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, s
 /* Selected bucket rows summed over the 7*n_layers bucketMuls of the last step (under tensor
  * parallelism a collective call: every rank calls it and all get the whole-model total). */
 int iam_model_selected_rows(iam_model_t m, long long* total);
+/* Selected bucket rows of each bucketMul of the last step: counts[7*layer + m], m in q, k, v,
+ * o, gate, up, down (this rank's rows under tensor parallelism: the whole selection for the
+ * column-parallel matrices, its inputs' share for o and down).  capacity >= 7*n_layers. */
+int iam_model_selected_rows_by_matrix(iam_model_t m, int* counts, int capacity);
 /* Algorithmic bytes of the last step at KV length `context`: per bucketMul
  * 2|S|C + 2R + 4N + 2*min(N,4096) + 4M, plus K/V reads and the dense LM head (this rank's
  * share under tensor parallelism). */

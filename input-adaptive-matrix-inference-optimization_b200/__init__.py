@@ -216,6 +216,7 @@ _SIGNATURES.update({
     "iam_model_profile_steps": [_vp, _f32, _i32, _vp, _vp, _i32, _vp, _vp],
     "iam_tp_unique_id": [_vp],
     "iam_model_status": [_vp],
+    "iam_model_selected_rows_by_matrix": [_vp, _vp, _i32],
     "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
     "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
     "iam_model_load_tp": [_vp, ctypes.c_char_p, _vp, _i32, _i32, _i32, _vp],
@@ -324,6 +325,14 @@ class Model:
         t = ctypes.c_longlong()
         check(self.lib.iam_model_selected_rows(self.h, ctypes.byref(t)))
         return t.value
+
+    def selected_rows_by_matrix(self):
+        """-> int32 array [n_layers, 7] of the last step's selected rows (q, k, v, o, gate, up, down)."""
+        import numpy as np
+        n = self.cfg.n_layers * len(MATRIX_NAMES)
+        out = np.zeros(n, np.int32)
+        check(self.lib.iam_model_selected_rows_by_matrix(self.h, out.ctypes.data_as(ctypes.c_void_p), n))
+        return out.reshape(self.cfg.n_layers, len(MATRIX_NAMES))
 
     def step_bytes(self, context):
         t = ctypes.c_longlong()

@@ -1139,6 +1139,14 @@ int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, s
     return IAM_OK;
 }
 
+int iam_model_selected_rows_by_matrix(iam_model_t m, int* counts, int capacity) {
+    if (!m || !counts) return fail(IAM_ERR_ARG, "iam_model_selected_rows_by_matrix: null argument");
+    const int n = m->cfg.n_layers * NMAT;
+    if (capacity < n) return fail(IAM_ERR_ARG, "iam_model_selected_rows_by_matrix: capacity < 7 * n_layers");
+    IAM_CUDA_TRY(cudaMemcpy(counts, m->sel, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost));
+    return IAM_OK;
+}
+
 int iam_model_status(iam_model_t m) {
     if (!m) return fail(IAM_ERR_ARG, "iam_model_status: null model");
     IAM_CUDA_TRY(cudaDeviceSynchronize());
