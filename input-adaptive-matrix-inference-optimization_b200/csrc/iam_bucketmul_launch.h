@@ -71,6 +71,7 @@ struct BMBatch {
     int mode;
     int xmode;
     int pdl;  // launched with programmatic stream serialization (waits on its predecessor in-kernel)
+    int cluster;  // cluster size the plan was made for (0: the caller's)
 };
 
 // Scratch a problem needs beyond its inputs and outputs (device memory the caller owns).

@@ -562,11 +562,28 @@ void fill_problem(iam_model_s* m, BMProblem& p, const Matrix& mat, float effort,
     p.split_sel = m->split_sel[slot];
 }
 
+// Plans a batch for clusters of m->G CTAs; when that leaves more than a fifth of the SMs idle
+// (column tiles x splits quantise badly, e.g. gate+up: 14 tiles) and clusters of 2 fill more,
+// the batch is planned for clusters of 2 instead (IAM_BM_CLUSTER pins the size).
+void plan_batch(iam_model_s* m, BMBatch& b) {
+    const BMBatch spec = b;
+    bm_plan(b, m->vec, m->G, bm_max_active_clusters(m->vec, m->G));
+    b.cluster = m->G;
+    if (getenv("IAM_BM_CLUSTER") || m->G == 2) return;
+    const int ctas = bm_total_clusters(b) * m->G;
+    if (ctas >= 0.8 * m->sm_count) return;
+    BMBatch alt = spec;
+    bm_plan(alt, m->vec, 2, bm_max_active_clusters(m->vec, 2));
+    if (bm_total_clusters(alt) * 2 > ctas) {
+        b = alt;
+        b.cluster = 2;
+    }
+}
+
 int build_plans(iam_model_s* m, float effort) {
     if (m->plan_effort == effort && !m->plans.empty()) return IAM_OK;
     const iam_model_config& c = m->cfg;
     m->plans.assign((size_t)c.n_layers * 4, BMBatch{});
-    const int mac = bm_max_active_clusters(m->vec, m->G);
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = m->layers[l];
         int* sel = m->sel + l * NMAT;
@@ -584,7 +601,7 @@ int build_plans(iam_model_s* m, float effort) {
             qkv.p[i].norm_n = c.dim;
             qkv.p[i].count_out = sel + MQ + i;
         }
-        bm_plan(qkv, m->vec, m->G, mac);
+        plan_batch(m, qkv);
 
         BMBatch& o = m->plans[l * 4 + 1];
         memset(&o, 0, sizeof(o));
@@ -595,7 +612,7 @@ int build_plans(iam_model_s* m, float effort) {
         o.p[0].x = m->att;  // every head (gathered under tensor parallelism)
         o.p[0].residual = m->tp_rank == 0 ? m->x : nullptr;  // added once; the all-reduce sums the ranks
         o.p[0].count_out = sel + MO;
-        bm_plan(o, m->vec, m->G, mac);
+        plan_batch(m, o);
 
         BMBatch& gu = m->plans[l * 4 + 2];
         memset(&gu, 0, sizeof(gu));
@@ -612,7 +629,7 @@ int build_plans(iam_model_s* m, float effort) {
             gu.p[i].norm_n = c.dim;
             gu.p[i].count_out = sel + MG + i;
         }
-        bm_plan(gu, m->vec, m->G, mac);
+        plan_batch(m, gu);
 
         BMBatch& d = m->plans[l * 4 + 3];
         memset(&d, 0, sizeof(d));
@@ -624,7 +641,7 @@ int build_plans(iam_model_s* m, float effort) {
         d.p[0].x2 = m->u;
         d.p[0].residual = m->tp_rank == 0 ? m->x1 : nullptr;
         d.p[0].count_out = sel + MD;
-        bm_plan(d, m->vec, m->G, mac);
+        plan_batch(m, d);
     }
     m->plan_effort = effort;
     return IAM_OK;
@@ -668,7 +685,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     for (int l = 0; l < c.n_layers; ++l) {
         if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
         m->plans[l * 4 + 0].pdl = pdl;
-        if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->G, s))) return rc;
+        if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->plans[l * 4 + 0].cluster, s))) return rc;
         AttnParams ap{};
         ap.q = m->q;
         ap.k = m->k;
@@ -709,7 +726,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
             }
             if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
             m->plans[l * 4 + b].pdl = pdl;
-            if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->G, s))) return rc;
+            if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->plans[l * 4 + b].cluster, s))) return rc;
         }
         if (m->tp_world > 1) {
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
