@@ -293,9 +293,23 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
     b.nprob = 1;
     b.mode = kModeFused;
     const int vec = pick_vec(b);
+    const BMBatch spec = b;
     bm_plan(b, vec, G, bm_max_active_clusters(vec, G));
-    if (!plan_fits(b, G)) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full: plan exceeds scratch");
-    return bm_launch(b, vec, G, (cudaStream_t)stream);
+    int g_used = G;
+    // as the decode step's plans: clusters of 2 when clusters of G leave a fifth of the SMs idle
+    int dev = 0, sms = 0;
+    if (!getenv("IAM_BM_CLUSTER") && G != 2 && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        bm_total_clusters(b) * G < 0.8 * sms) {
+        BMBatch alt = spec;
+        bm_plan(alt, vec, 2, bm_max_active_clusters(vec, 2));
+        if (bm_total_clusters(alt) * 2 > bm_total_clusters(b) * G) {
+            b = alt;
+            g_used = 2;
+        }
+    }
+    if (!plan_fits(b, g_used)) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full: plan exceeds scratch");
+    return bm_launch(b, vec, g_used, (cudaStream_t)stream);
 }
 
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev) {

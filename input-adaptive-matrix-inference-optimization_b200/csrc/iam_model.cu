@@ -291,6 +291,9 @@ int alloc_runtime(iam_model_s* m) {
         IAM_CUDA_TRY(cudaMemset(m->ctr[s], 0, 4096 * sizeof(int)));
     }
     const int gq = c.n_heads / c.n_kv_heads;
+    // chunks per KV head: about 2 CTAs per SM at long context (short contexts use fewer: a
+    // chunk holds at least att_min_chunk tokens; 4 per SM and 4 tokens per half-warp in flight
+    // measured slower at 8192 tokens)
     m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, m->n_kv_local)));
     if (const char* v = getenv("IAM_ATTN_MIN_CHUNK")) m->att_min_chunk = std::max(1, atoi(v));
     {
