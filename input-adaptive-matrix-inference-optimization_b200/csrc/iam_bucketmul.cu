@@ -4,15 +4,19 @@
 //
 // One launch runs up to kMaxProblems bucketMuls.  Grid = clusters of G CTAs; a cluster owns
 // one column tile of one problem and one of n_split input ranges.  Per CTA (rank g):
-//   1. cutoff: block_find_cutoff over x[0:P] (every CTA, identical result);
-//   2. selection masks for its share of the cluster's inputs (block_masks), then its
+//   0. weights-only prologue (the probes and this CTA's stats segment towards L2), then the
+//      programmatic-dependent-launch wait for the previous kernel of the stream;
+//   1. cutoff: block_find_cutoff over x[0:P] by 4 warps (every CTA, identical result) while
+//      the other warps compute the row importances of the CTA's inputs;
+//   2. selection masks for its share of the cluster's inputs (block_masks_pre), then its
 //      selected rows as 16-bit offsets in its own shared memory; one cluster barrier; a
 //      prefix over the G counts read through DSMEM numbers the cluster's rows 0..S-1;
 //   3. the CTA takes rows [S*g/G, S*(g+1)/G) of that numbering, wherever they live: it
 //      stages {row*C, x(row)} for 2048 rows at a time (row offsets read from the owner's
-//      shared memory through DSMEM, next chunk fetched during the current one), and each
-//      lane streams VEC-wide slices of its rows with register double-buffered loads,
-//      adding x*w into lane-private per-slot accumulators in shared memory;
+//      shared memory through DSMEM, next chunk fetched during the current one); each lane
+//      keeps a ring of kD rows of VEC-wide weight slices in registers and adds x*w into
+//      lane-private per-slot accumulators in shared memory, addressed with one shift and
+//      one LOP3 per weight (accumulate_sh);
 //   4. lane accumulators -> a partial tile per CTA -> fixed-order DSMEM sum across the
 //      cluster; with n_split > 1 the partial tiles go to global scratch and the last cluster
 //      to arrive at each slice adds them in split order -> out (+ residual).

@@ -296,48 +296,6 @@ struct ScanShared {
     int tot[2][NT / 32];
 };
 
-// prepareDispatch predicate (bucketMul.cl:351-386) for inputs [i0, i1) of one expert: bit r
-// of masks[i - i0] is set iff row row0 + 16*i + r is selected, i.e.
-// 1e5*|x[i]*stats[row][stride-1]| >= cutoff.  Returns the number of selected rows (same in
-// all threads).
-template <int NT, class XP>
-__device__ int block_masks(const XP& xp, const uint16_t* __restrict__ stats, int stride,
-                           long long row0, int n_rows_valid, int i0, int i1, float cutoff,
-                           uint16_t* __restrict__ masks, ScanShared<NT>& sm) {
-    constexpr int NW = NT / 32;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int cnt = 0;
-    for (int i = i0 + tid; i < i1; i += NT) {
-        const float xi = xp(i);
-        const int rmax = min(16, n_rows_valid - i * 16);
-        const uint16_t* sp = stats + (row0 + (long long)i * 16) * stride + (stride - 1);
-        unsigned mask = 0u;
-        if (stride == 1 && rmax == 16 && ((reinterpret_cast<uintptr_t>(sp) & 15u) == 0)) {
-            const uint4 a = __ldg(reinterpret_cast<const uint4*>(sp));
-            const uint4 b = __ldg(reinterpret_cast<const uint4*>(sp + 8));
-            const uint32_t wds[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                const uint32_t hb = (r & 1) ? (wds[r >> 1] >> 16) : (wds[r >> 1] & 0xffffu);
-                if (importance(xi, h2f(hb)) >= cutoff) mask |= 1u << r;  // ">=" (:380)
-            }
-        } else {
-            for (int r = 0; r < rmax; ++r)
-                if (importance(xi, h2f(__ldg(sp + r * stride))) >= cutoff) mask |= 1u << r;
-        }
-        masks[i - i0] = (uint16_t)mask;
-        cnt += __popc(mask);
-    }
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-    if (lane == 0) sm.tot[0][warp] = cnt;
-    __syncthreads();
-    int total = 0;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) total += sm.tot[0][w];
-    __syncthreads();
-    return total;
-}
-
 // The 16 row importances 1e5*|x[i]*stats[row]| of one input (-1 for rows past
 // n_rows_valid: never selected, every cutoff is >= 0).
 template <class XP>
@@ -358,9 +316,12 @@ IAM_DEV void input_importances(const XP& xp, const uint16_t* __restrict__ stats,
     }
 }
 
-// block_masks with the importances of inputs [i0, i0 + npre) computed beforehand (by the
-// warps outside the cutoff search, during the search): thread NWC*32 + t holds input i0 + t
-// in pimp when pin >= 0.  Inputs past i0 + npre are done here by every thread.
+// prepareDispatch predicate (bucketMul.cl:351-386) for inputs [i0, i1) of one expert: bit r
+// of masks[i - i0] is set iff row row0 + 16*i + r is selected, i.e.
+// 1e5*|x[i]*stats[row][stride-1]| >= cutoff.  Returns the number of selected rows (same in
+// all threads).  The importances of inputs [i0, i0 + npre) were computed beforehand (by the
+// warps outside the cutoff search, during the search): thread 128 + t holds input i0 + t in
+// pimp when pin >= 0.  Inputs past i0 + npre are done here by every thread.
 template <int NT, class XP>
 __device__ int block_masks_pre(const XP& xp, const uint16_t* __restrict__ stats, int stride, long long row0,
                                int n_rows_valid, int i0, int i1, int npre, float cutoff, int pin,
@@ -394,47 +355,8 @@ __device__ int block_masks_pre(const XP& xp, const uint16_t* __restrict__ stats,
     return total;
 }
 
-// Writes the selected rows of inputs [i0, i1) (masks from block_masks) to rows_out in
-// ascending row order.
-template <int NT>
-__device__ void block_write_rows(const uint16_t* __restrict__ masks, long long row0, int i0,
-                                 int i1, int32_t* __restrict__ rows_out, ScanShared<NT>& sm) {
-    constexpr int NW = NT / 32;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int base = 0, round = 0;
-    for (int ib = i0; ib < i1; ib += NT, ++round) {
-        const int i = ib + tid;
-        unsigned mask = (i < i1) ? masks[i - i0] : 0u;
-        const int n = __popc(mask);
-        int inc = n;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-        }
-        const int par = round & 1;
-        if (lane == 31) sm.tot[par][warp] = inc;
-        __syncthreads();
-        int pre = 0, total = 0;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const int t = sm.tot[par][w];
-            pre += (w < warp) ? t : 0;
-            total += t;
-        }
-        int p = base + pre + inc - n;
-        const int32_t rbase = (int32_t)(row0 + (long long)i * 16);
-        while (mask) {
-            const int r = __ffs(mask) - 1;
-            mask &= mask - 1u;
-            rows_out[p++] = rbase + r;
-        }
-        base += total;
-    }
-    __syncthreads();
-}
-
-// Writes the selected rows of inputs [i0, i1) as 16-bit offsets from row 16*i0 (ascending)
+// Writes the selected rows of inputs [i0, i1) (masks from block_masks_pre) as 16-bit offsets
+// from row 16*i0 (ascending)
 // into a shared-memory list (peers of the cluster read it through DSMEM).
 template <int NT>
 __device__ void block_write_rows_local(const uint16_t* __restrict__ masks, int i0, int i1,
@@ -555,21 +477,5 @@ IAM_DEV void accumulate_sh(uint32_t acc_lane, const typename VecLoad<VEC>::T& w,
     accumulate_sh_impl<VEC>(acc_lane, w, x, std::make_integer_sequence<int, VEC>{});
 }
 
-// Adds x * w_k into this lane's private slot accumulators acc[(slot*VEC + k) * 32].  The
-// VEC addresses of one call are distinct (k differs), so all loads are issued before any
-// store; successive calls may alias and stay in program order.
-template <int VEC>
-IAM_DEV void accumulate(float* __restrict__ acc, const typename VecLoad<VEC>::T& w, float x) {
-    int off[VEC];
-    float old[VEC];
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) off[k] = ((int)((VecLoad<VEC>::bits(w, k) & 15u) * VEC + k)) << 5;
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) old[k] = acc[off[k]];
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) old[k] = fmaf(x, h2f(VecLoad<VEC>::bits(w, k)), old[k]);
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) acc[off[k]] = old[k];
-}
 
 }  // namespace iam
