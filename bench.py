@@ -544,15 +544,18 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":  # rank 0 alone times the reference's CPU path: no collective at all
+        res = run_reference(args, rank, world)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+        return
     if world > 1:
         import datetime
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        if args.impl == "reference":
-            res = run_reference(args, rank, world)
-        elif args.workload == "decode":
+        if args.workload == "decode":
             res = run_decode(args, rank, world)
         else:
             res = run_bucketmul(args, rank, world)
