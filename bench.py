@@ -297,8 +297,11 @@ def cpu_baseline_bucketmul(sets, effort, budget_s=10.0, steps=None):
 PROMPT_LEN = 128
 
 
-def mistral_cfg(iam, max_ctx):
-    return iam.ModelConfig.make(**dict(iam.MISTRAL_7B, max_ctx=max_ctx))
+def mistral_cfg(iam, max_ctx, n_layers=None):
+    d = dict(iam.MISTRAL_7B, max_ctx=max_ctx)
+    if n_layers:
+        d["n_layers"] = n_layers
+    return iam.ModelConfig.make(**d)
 
 
 def prompt_tokens(vocab):
@@ -318,7 +321,7 @@ def run_decode(args, rank, world):
     # random fp16 KV prefix, decoding starts after it
     start = args.kv_prefix if args.kv_prefix > 0 else PROMPT_LEN
     max_ctx = start + args.warmup + args.steps + n_sweep * len(sweep) + n_prof + n_e2e + 8
-    cfg = mistral_cfg(iam, max_ctx)
+    cfg = mistral_cfg(iam, max_ctx, args.layers)
     tp = None
     if world > 1:  # one decode stream, tensor-parallel over the ranks (NCCL inside the library)
         uid = [iam.tp_unique_id() if rank == 0 else None]
@@ -423,7 +426,8 @@ def run_decode(args, rank, world):
                                 f"{args.kv_prefix} tokens") if args.kv_prefix > 0 else
                                ("decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
                                 "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)"),
-                   "model": "Mistral-7B (random init)", "effort": args.effort, "global_batch": 1,
+                   "model": "Mistral-7B (random init)" + (f", {cfg.n_layers} layers" if args.layers else ""),
+                   "effort": args.effort, "global_batch": 1,
                    "seq_len": ctx_end, "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token",
                    "tokens_per_s_by_effort": sweep_res, "selected_rows_per_step": sel_rows,
@@ -537,6 +541,8 @@ def main():
     ap.add_argument("--effort", type=float, default=0.25)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers of the decode model (default 32; fewer only for small profiling captures)")
     ap.add_argument("--kv-prefix", type=int, default=0,
                     help="decode after a random KV prefix of this many tokens (config 5: 8192) instead of the prompt")
     args = ap.parse_args()

@@ -102,7 +102,7 @@ IAM_DEV void load_halves(const uint16_t* p, float* o) {
 // order.  The new token's K/V (RoPE'd, rounded through fp16) are appended by the CTA whose
 // chunk holds pos and used from shared memory for that token.
 template <int GQ, int VD>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
     constexpr int HD = 16 * VD;
     constexpr int NH = kAttnThreads / 16;  // half-warps
@@ -161,26 +161,57 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
         for (int e = 0; e < VD; ++e) o[j][e] = 0.0f;
     }
     // warp-uniform trip count (the dot-product shuffles use the full warp); each half-warp
-    // takes TU tokens of its warp's group of 2*TU, masking those past the chunk
+    // takes TU tokens of its warp's group of 2*TU, masking those past the chunk.  The K/V of
+    // the next group are loaded before the current group is scored (software pipeline).
     const int warp = tid >> 5, hwin = (tid >> 4) & 1;
     constexpr int NWT = kAttnThreads / 32;
-    for (int wb = t0 + warp * 2 * TU; wb < t1; wb += NWT * 2 * TU) {
+    // K/V travel as raw fp16 words (VD/2 per token) and are widened at use
+    constexpr int VW = VD / 2;
+    auto load_group = [&](int wb, uint32_t (&kw)[TU][VW], uint32_t (&vw)[TU][VW]) {
         const int tb = wb + hwin * TU;
-        float kv[TU][VD], vv[TU][VD];
 #pragma unroll
         for (int u = 0; u < TU; ++u) {
             const int t = tb + u;
             if (t < t1 && t != pos) {
-                load_halves<VD>(kc + (size_t)t * HD + hl * VD, kv[u]);
-                load_halves<VD>(vc + (size_t)t * HD + hl * VD, vv[u]);
-            } else {
+                const uint32_t* kp = reinterpret_cast<const uint32_t*>(kc + (size_t)t * HD + hl * VD);
+                const uint32_t* vp = reinterpret_cast<const uint32_t*>(vc + (size_t)t * HD + hl * VD);
+                if constexpr (VW % 4 == 0) {
 #pragma unroll
-                for (int e = 0; e < VD; ++e) {
-                    kv[u][e] = t < t1 ? knew[hl * VD + e] : 0.0f;
-                    vv[u][e] = t < t1 ? vnew[hl * VD + e] : 0.0f;
+                    for (int c = 0; c < VW; c += 4) {
+                        const uint4 a = *reinterpret_cast<const uint4*>(kp + c);
+                        const uint4 b = *reinterpret_cast<const uint4*>(vp + c);
+                        kw[u][c] = a.x; kw[u][c + 1] = a.y; kw[u][c + 2] = a.z; kw[u][c + 3] = a.w;
+                        vw[u][c] = b.x; vw[u][c + 1] = b.y; vw[u][c + 2] = b.z; vw[u][c + 3] = b.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < VW; ++c) {
+                        kw[u][c] = kp[c];
+                        vw[u][c] = vp[c];
+                    }
+                }
+            } else {  // the new token (its fp16-rounded k/v from shared memory) or past the chunk
+#pragma unroll
+                for (int c = 0; c < VW; ++c) {
+                    const int d = hl * VD + 2 * c;
+                    kw[u][c] = t < t1 ? (uint32_t)__half_as_ushort(__float2half_rn(knew[d])) |
+                                            ((uint32_t)__half_as_ushort(__float2half_rn(knew[d + 1])) << 16)
+                                      : 0u;
+                    vw[u][c] = t < t1 ? (uint32_t)__half_as_ushort(__float2half_rn(vnew[d])) |
+                                            ((uint32_t)__half_as_ushort(__float2half_rn(vnew[d + 1])) << 16)
+                                      : 0u;
                 }
             }
         }
+    };
+    auto half_at = [](const uint32_t (&w)[VW], int e) { return h2f((e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xffffu)); };
+    uint32_t kw[TU][VW], vw[TU][VW];
+    int wb = t0 + warp * 2 * TU;
+    if (wb < t1) load_group(wb, kw, vw);
+    for (; wb < t1; wb += NWT * 2 * TU) {
+        const int tb = wb + hwin * TU;
+        uint32_t kn[TU][VW], vn[TU][VW];
+        if (wb + NWT * 2 * TU < t1) load_group(wb + NWT * 2 * TU, kn, vn);
         float sc[TU][GQ];
 #pragma unroll
         for (int u = 0; u < TU; ++u)
@@ -188,7 +219,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
             for (int j = 0; j < GQ; ++j) {
                 float d = 0.0f;
 #pragma unroll
-                for (int e = 0; e < VD; ++e) d = fmaf(qv[j][e], kv[u][e], d);
+                for (int e = 0; e < VD; ++e) d = fmaf(qv[j][e], half_at(kw[u], e), d);
 #pragma unroll
                 for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);  // 16-lane groups
                 sc[u][j] = (tb + u < t1) ? __fdiv_rn(d, scale_div) : -INFINITY;
@@ -208,10 +239,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
                 const float pu = expf(sc[u][j] - mx);
                 l[j] += pu;
 #pragma unroll
-                for (int e = 0; e < VD; ++e) o[j][e] = fmaf(pu, vv[u][e], o[j][e]);
+                for (int e = 0; e < VD; ++e) o[j][e] = fmaf(pu, half_at(vw[u], e), o[j][e]);
             }
             m[j] = mx;
         }
+#pragma unroll
+        for (int u = 0; u < TU; ++u)
+#pragma unroll
+            for (int c = 0; c < VW; ++c) {
+                kw[u][c] = kn[u][c];
+                vw[u][c] = vn[u][c];
+            }
     }
 #pragma unroll
     for (int j = 0; j < GQ; ++j) {
