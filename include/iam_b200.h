@@ -198,6 +198,13 @@ int iam_model_create_random_tp(iam_model_t* out, const iam_model_config* cfg, un
 int iam_model_load_tp(iam_model_t* out, const char* weights_dir, const iam_model_config* cfg, int device,
                       int rank, int world, const unsigned char* nccl_id);
 int iam_model_destroy(iam_model_t m);
+/* Writes the model to weights_dir in the reference's on-disk layout -- exactly what
+ * iam_model_load and the reference's loader (binary_loader.hpp:141-193, model.hpp:84-127)
+ * read: per matrix {_buckets,_stats,_probes}.bin and _meta.txt as written by
+ * preprocess_layer_fixed_gpu.py:245-282 (stats with its 4 identical channels), fp16 .npy
+ * files for the norms, the embedding and an untied LM head.  The directory must exist.
+ * Single-GPU models only (IAM_ERR_UNSUPPORTED for a tensor-parallel rank). */
+int iam_model_save(iam_model_t m, const char* weights_dir);
 /* Synchronises the device and reports IAM_ERR_TIMEOUT when a tensor-parallel exchange of an
  * earlier step gave up waiting for a peer (its outputs are then invalid); IAM_OK otherwise.
  * (No counterpart in the reference: failure detection of the multi-GPU path.) */

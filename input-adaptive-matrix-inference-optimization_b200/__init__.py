@@ -216,6 +216,7 @@ _SIGNATURES.update({
     "iam_model_profile_steps": [_vp, _f32, _i32, _vp, _vp, _i32, _vp, _vp],
     "iam_tp_unique_id": [_vp],
     "iam_model_status": [_vp],
+    "iam_model_save": [_vp, ctypes.c_char_p],
     "iam_model_selected_rows_by_matrix": [_vp, _vp, _i32],
     "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
     "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
@@ -290,6 +291,10 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def save(self, weights_dir):
+        """Writes the model in the reference's on-disk layout (the directory must exist)."""
+        check(self.lib.iam_model_save(self.h, os.fsencode(weights_dir)))
 
     def status(self):
         """Raises IamError(IAM_ERR_TIMEOUT) if a tensor-parallel exchange gave up on a peer."""

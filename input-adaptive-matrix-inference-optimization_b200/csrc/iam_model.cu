@@ -1159,6 +1159,90 @@ int iam_model_read_weight(iam_model_t m, int layer, int which, void* host_dst, s
     return IAM_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// NumPy .npy (format 1.0) of fp16 values: the header dict padded to a multiple of 64 bytes.
+bool write_npy_f16(const std::string& path, const std::vector<uint16_t>& v, const std::vector<long>& shape) {
+    std::string dict = "{'descr': '<f2', 'fortran_order': False, 'shape': (";
+    for (size_t i = 0; i < shape.size(); ++i) dict += std::to_string(shape[i]) + (shape.size() == 1 ? "," : (i + 1 < shape.size() ? ", " : ""));
+    dict += "), }";
+    size_t total = 10 + dict.size() + 1;
+    const size_t pad = (64 - total % 64) % 64;
+    dict += std::string(pad, ' ') + "\n";
+    std::ofstream f(path, std::ios::binary);
+    if (!f) return false;
+    const uint16_t hlen = (uint16_t)dict.size();
+    f.write("\x93NUMPY\x01\x00", 8);
+    f.put((char)(hlen & 0xff));
+    f.put((char)(hlen >> 8));
+    f.write(dict.data(), (std::streamsize)dict.size());
+    f.write(reinterpret_cast<const char*>(v.data()), (std::streamsize)(v.size() * 2));
+    return (bool)f;
+}
+
+bool write_u16(const std::string& path, const std::vector<uint16_t>& v) {
+    std::ofstream f(path, std::ios::binary);
+    if (!f) return false;
+    f.write(reinterpret_cast<const char*>(v.data()), (std::streamsize)(v.size() * 2));
+    return (bool)f;
+}
+
+int download(const uint16_t* src, size_t n, std::vector<uint16_t>& out) {
+    out.resize(n);
+    IAM_CUDA_TRY(cudaMemcpy(out.data(), src, n * 2, cudaMemcpyDeviceToHost));
+    return IAM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int iam_model_save(iam_model_t m, const char* weights_dir) {
+    if (!m || !weights_dir) return fail(IAM_ERR_ARG, "iam_model_save: null argument");
+    if (m->tp_world > 1) return fail(IAM_ERR_UNSUPPORTED, "iam_model_save: a tensor-parallel rank holds a shard only");
+    const iam_model_config& c = m->cfg;
+    const std::string dir(weights_dir);
+    std::vector<uint16_t> a, b;
+    int rc = IAM_OK;
+    for (int l = 0; l < c.n_layers && !rc; ++l) {
+        const Layer& L = m->layers[l];
+        for (int i = 0; i < NMAT && !rc; ++i) {
+            const Matrix& mt = L.m[i];
+            const std::string prefix = dir + "/layer" + std::to_string(l) + "_" + kMatNames[i] + "_proj_bucketmul_fp16";
+            const size_t R = (size_t)16 * mt.in_dim;
+            if ((rc = download(mt.buckets, R * mt.cols, a))) break;
+            if (!write_u16(prefix + "_buckets.bin", a)) rc = fail(IAM_ERR_IO, "cannot write " + prefix + "_buckets.bin");
+            if (rc || (rc = download(mt.stats, R, a))) break;
+            b.resize(R * 4);  // the file keeps 4 identical channels per row (preprocess_layer_fixed_gpu.py:217-221)
+            for (size_t r = 0; r < R; ++r) b[4 * r] = b[4 * r + 1] = b[4 * r + 2] = b[4 * r + 3] = a[r];
+            if (!write_u16(prefix + "_stats.bin", b)) rc = fail(IAM_ERR_IO, "cannot write " + prefix + "_stats.bin");
+            if (rc || (rc = download(mt.probes, (size_t)mt.in_dim, a))) break;
+            if (!write_u16(prefix + "_probes.bin", a)) rc = fail(IAM_ERR_IO, "cannot write " + prefix + "_probes.bin");
+            std::ofstream f(prefix + "_meta.txt");  // preprocess_layer_fixed_gpu.py:262-282
+            f << "# BucketMul Weight Metadata\n# All arrays are FP16 (2 bytes per element)\n\n"
+              << "buckets_shape: 1 " << R << " " << mt.cols << "\nstats_shape: 1 " << R << " 4\nprobes_shape: 1 " << mt.in_dim
+              << "\nin_dim: " << mt.in_dim << "\nout_dim: " << mt.out_dim << "\nbsize: 16\ndtype: float16\n";
+            if (!rc && !f) rc = fail(IAM_ERR_IO, "cannot write " + prefix + "_meta.txt");
+        }
+        const std::string lp = dir + "/layer" + std::to_string(l);
+        if (!rc && !(rc = download(L.attn_norm, c.dim, a)) && !write_npy_f16(lp + "_input_layernorm.npy", a, {c.dim}))
+            rc = fail(IAM_ERR_IO, "cannot write " + lp + "_input_layernorm.npy");
+        if (!rc && !(rc = download(L.ffn_norm, c.dim, a)) && !write_npy_f16(lp + "_post_attention_layernorm.npy", a, {c.dim}))
+            rc = fail(IAM_ERR_IO, "cannot write " + lp + "_post_attention_layernorm.npy");
+    }
+    if (!rc && !(rc = download(m->embed, (size_t)c.vocab * c.dim, a)) &&
+        !write_npy_f16(dir + "/embed_tokens.npy", a, {c.vocab, c.dim}))
+        rc = fail(IAM_ERR_IO, "cannot write " + dir + "/embed_tokens.npy");
+    if (!rc && !(rc = download(m->final_norm, c.dim, a)) && !write_npy_f16(dir + "/norm_weight.npy", a, {c.dim}))
+        rc = fail(IAM_ERR_IO, "cannot write " + dir + "/norm_weight.npy");
+    if (!rc && !c.tied_embeddings && !(rc = download(m->lm_head, (size_t)c.vocab * c.dim, a)) &&
+        !write_npy_f16(dir + "/lm_head.npy", a, {c.vocab, c.dim}))
+        rc = fail(IAM_ERR_IO, "cannot write " + dir + "/lm_head.npy");
+    return rc;
+}
+
 int iam_model_selected_rows_by_matrix(iam_model_t m, int* counts, int capacity) {
     if (!m || !counts) return fail(IAM_ERR_ARG, "iam_model_selected_rows_by_matrix: null argument");
     const int n = m->cfg.n_layers * NMAT;

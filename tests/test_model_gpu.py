@@ -123,6 +123,41 @@ def test_reference_file_layout_loads(small, iam, weights_mod, torch_mod, tmp_pat
     assert e.value.code == iam.IAM_ERR_IO
 
 
+def test_model_save_writes_the_reference_layout(small, iam, weights_mod, torch_mod, tmp_path):
+    """iam_model_save writes the reference's on-disk layout: the Python restatement of the
+    reference's reader accepts every file, the bytes equal the model's weights, and a model
+    loaded back from the directory gives bit-identical logits."""
+    torch = torch_mod
+    cfg, m, w = small
+    d = str(tmp_path)
+    m.save(d)
+    for l, lw in enumerate(w["layers"]):
+        for name in iam.MATRIX_NAMES:
+            back = weights_mod.load_bucketmul_binary(os.path.join(d, weights_mod.layer_weight_name(l, name)))
+            bw = lw[name]
+            np.testing.assert_array_equal(back.buckets.reshape(-1), np.asarray(bw.buckets).reshape(-1))
+            np.testing.assert_array_equal(back.stats.reshape(-1, 4)[:, 3], np.asarray(bw.stats).reshape(-1))
+            assert (back.stats.reshape(-1, 4) == back.stats.reshape(-1, 4)[:, :1]).all()  # 4 identical channels
+            np.testing.assert_array_equal(back.probes.reshape(-1), np.asarray(bw.probes).reshape(-1))
+            assert (back.in_dim, back.out_dim) == (bw.in_dim, bw.out_dim)
+        np.testing.assert_array_equal(weights_mod.load_npy_fp16(os.path.join(d, f"layer{l}_input_layernorm.npy")),
+                                      lw["attn_norm"].reshape(-1))
+    emb = np.load(os.path.join(d, "embed_tokens.npy"))
+    assert emb.dtype == np.float16 and emb.shape == (cfg.vocab, cfg.dim)
+    np.testing.assert_array_equal(emb.view(np.uint16).reshape(-1), w["embed"].reshape(-1))
+    m2 = iam.Model.load(d, cfg)
+    outs = []
+    for mm in (m, m2):
+        mm.reset()
+        logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+        for pos, tok in enumerate([11, 22, 33]):
+            mm.forward(tok, pos, 0.25, logits)
+        torch.cuda.synchronize()
+        outs.append(logits.cpu().numpy().view(np.uint32).copy())
+    m2.close()
+    assert (outs[0] == outs[1]).all()
+
+
 def test_model_rejects_bad_arguments(small, iam):
     cfg, m, _ = small
     for token, pos, effort in [(-1, 0, 0.5), (cfg.vocab, 0, 0.5), (1, cfg.max_ctx, 0.5), (1, 0, 0.0), (1, 0, 2.0)]:
