@@ -144,6 +144,34 @@ int iam_stats_pack(const uint16_t* stats4_dev, long long rows, uint16_t* stats1_
 int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buckets_dev,
                   uint16_t* stats4_dev, uint16_t* stats1_dev, uint16_t* probes_dev, void* stream);
 
+/* ------------------------------------------------------------------ dense tensor-core path */
+/* Replaces the reference's dense GEMV kernels basicMul / basicMul2 (matrix.cl:80-127:
+ * out[row] = sum_i v[i] * m[row][i], fp16 m, fp32 v) batched over tokens, on the tcgen05
+ * tensor cores.  A handle owns the activation split (fp16 hi / lo) and split-K scratch for up
+ * to max_tokens x max_in_dim activations and max_out_dim outputs. */
+typedef struct iam_dense_s* iam_dense_t;
+int iam_dense_create(int max_tokens, int max_in_dim, int max_out_dim, int device, iam_dense_t* out);
+int iam_dense_destroy(iam_dense_t h);
+/* y[t][o] = residual[t][o] (when residual_dev is not NULL; it may equal y_dev)
+ *           + sum_i W[o][i] * x[t][i]            for t < n_tokens, o < out_dim.
+ * w_dev fp16 [out_dim][in_dim] (in_dim % 8 == 0, 16-byte aligned); x_dev fp32 [n_tokens][in_dim];
+ * y_dev, residual_dev fp32 [n_tokens][out_dim].  precision 0: every activation enters as two
+ * fp16 halves (hi + lo, ~22 significant bits, fp32 accumulation); 1: one fp16 (11 bits).
+ * split_k 0 picks the K split from the SM count; >= 1 forces it (results are deterministic
+ * for every split: the K slices are summed in order).  Asynchronous on `stream`. */
+int iam_dense_gemm(iam_dense_t h, const uint16_t* w_dev, int out_dim, int in_dim, const float* x_dev,
+                   int n_tokens, const float* residual_dev, float* y_dev, int precision, int split_k,
+                   void* stream);
+/* Synchronises the device; IAM_ERR_TIMEOUT when a pipeline wait of a GEMM on this handle gave
+ * up since the last call (the flag is then cleared). */
+int iam_dense_status(iam_dense_t h);
+/* Dense fp16 matrix w_out [16*bucket_cols][in_dim] from the bucket layout
+ * buckets [16*in_dim][bucket_cols]: each packed word (value with its slot in the low 4 bits,
+ * preprocess_layer_fixed_gpu.py:196) returns to row 16*c + slot, column i.  This is the
+ * matrix bucketMul multiplies by when every bucket row is selected (bucketMul.cl:430-434). */
+int iam_dense_unpack(const uint16_t* buckets_dev, int in_dim, int bucket_cols, uint16_t* w_out_dev,
+                     void* stream);
+
 /* ------------------------------------------------------------------ decode model */
 /* Replaces MistralModel (model.hpp:84-237), TransformerLayer (transformer_layer.hpp:55-162),
  * Attention (attention.hpp:71-404) and FeedForward (feedforward.hpp:89-183).  The model

@@ -44,6 +44,11 @@ _SIGNATURES = {
     "iam_bucketmul_full_noalloc": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_stats_pack": [_vp, _i64, _vp, _vp],
     "iam_bucketize": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
+    "iam_dense_create": [_i32, _i32, _i32, _i32, _vp],
+    "iam_dense_destroy": [_vp],
+    "iam_dense_gemm": [_vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _vp],
+    "iam_dense_status": [_vp],
+    "iam_dense_unpack": [_vp, _i32, _i32, _vp, _vp],
 }
 _RESTYPES = {"iam_version": ctypes.c_char_p, "iam_last_error": ctypes.c_char_p}
 
@@ -176,6 +181,44 @@ def bucketize(w, buckets, stats4=None, stats1=None, probes=None, stream=None):
     out_dim, in_dim = w.shape
     check(load_library().iam_bucketize(_ptr(w), out_dim, in_dim, _ptr(buckets), _ptr(stats4), _ptr(stats1),
                                        _ptr(probes), _stream(stream)))
+
+
+def dense_unpack(buckets, w_out, in_dim=None, bucket_cols=None, stream=None):
+    """iam_dense_unpack: dense fp16 W'[16*cols][in] from buckets[16*in][cols] (every row selected)."""
+    rows, cols = buckets.shape
+    in_dim = rows // 16 if in_dim is None else in_dim
+    cols = cols if bucket_cols is None else bucket_cols
+    check(load_library().iam_dense_unpack(_ptr(buckets), in_dim, cols, _ptr(w_out), _stream(stream)))
+
+
+class Dense:
+    """Dense tensor-core products (iam_dense_*): y[t][o] = residual[t][o] + sum_i W[o][i] x[t][i],
+    the reference's basicMul (matrix.cl:80-93) batched over tokens.  W is fp16 bits
+    [out][in] (uint16/int16/float16 tensor), x / y / residual fp32 [tokens][...]."""
+
+    def __init__(self, max_tokens, max_in_dim, max_out_dim, device=0):
+        self.lib = load_library()
+        self.h = ctypes.c_void_p()
+        check(self.lib.iam_dense_create(max_tokens, max_in_dim, max_out_dim, device, ctypes.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            self.lib.iam_dense_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def gemm(self, w, x, y, residual=None, precision=0, split_k=0, stream=None):
+        out_dim, in_dim = w.shape
+        check(self.lib.iam_dense_gemm(self.h, _ptr(w), out_dim, in_dim, _ptr(x), x.shape[0], _ptr(residual),
+                                      _ptr(y), precision, split_k, _stream(stream)))
+
+    def status(self):
+        check(self.lib.iam_dense_status(self.h))
 
 
 # ---------------------------------------------------------------- decode model

@@ -45,6 +45,29 @@ def bucketize_fp16_packed(W, bsize=16):
                         probes.view(np.uint16).copy(), in_dim, out_dim, bsize)
 
 
+def dense_from_buckets(buckets):
+    """Dense uint16 W'[16*C][in] from buckets[16*in][C]: each packed word returns to row
+    16*c + slot (slot = its low 4 bits, preprocess_layer_fixed_gpu.py:196), column i.  bucketMul
+    with every bucket row selected multiplies by exactly this matrix (bucketMul.cl:430-434)."""
+    buckets = np.asarray(buckets, dtype=np.uint16)
+    R, C = buckets.shape
+    in_dim = R // 16
+    b = buckets.reshape(in_dim, 16, C)                        # [i][rank][c]
+    slot = (b & 0xF).astype(np.int64)
+    dense = np.zeros((C, 16, in_dim), dtype=np.uint16)        # [c][slot][i]
+    ii = np.broadcast_to(np.arange(in_dim)[:, None, None], b.shape)
+    cc = np.broadcast_to(np.arange(C)[None, None, :], b.shape)
+    dense[cc, slot, ii] = b
+    return dense.reshape(C * 16, in_dim)
+
+
+def dense_packed(W):
+    """The same matrix straight from W (float16 [out][in]): (bits & 0xFFF0) | (row & 15)."""
+    bits = np.asarray(W, dtype=np.float16).view(np.uint16)
+    rows = np.arange(bits.shape[0], dtype=np.uint16)[:, None]
+    return (bits & np.uint16(0xFFF0)) | (rows & np.uint16(0xF))
+
+
 def pack_fp16_with_index(value, position):
     """preprocess_layer_fixed_gpu.py:40-66."""
     bits = int(np.float16(value).view(np.uint16))

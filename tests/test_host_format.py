@@ -24,6 +24,17 @@ def test_save_load_roundtrip(weights_mod, tmp_path):
     assert (back.in_dim, back.out_dim, back.bsize) == (64, 256, 16)
 
 
+@pytest.mark.parametrize("case", ["bm_256x64.npz", "bm_128x512.npz", "bm_48x96_ties.npz", "bm_16x4096.npz"])
+def test_dense_unpack_restatement_on_reference_buckets(weights_mod, case):
+    """The dense matrix behind the dense tensor-core path: unpacking the reference's own bucket
+    layout (fixtures made by preprocess_layer_fixed_gpu.py) puts every packed word back at
+    (16*c + slot, i), i.e. W with its row's slot in the low 4 mantissa bits."""
+    g = golden(case)
+    dense = weights_mod.dense_from_buckets(g["buckets"])
+    assert dense.shape == g["W"].shape
+    np.testing.assert_array_equal(dense, weights_mod.dense_packed(g["W"].view(np.float16)))
+
+
 def test_truncated_file_is_rejected(weights_mod, tmp_path):
     g = golden("bm_256x64.npz")
     bw = weights_mod.bucketize_fp16_packed(g["W"].view(np.float16))
