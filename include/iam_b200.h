@@ -242,6 +242,17 @@ int iam_model_reset(iam_model_t m, void* stream);
 /* MistralModel::forward (model.hpp:152-231): one decode step of `token` at `pos`; logits_dev
  * (vocab floats, may be NULL) receives the logits. */
 int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* logits_dev, void* stream);
+/* Batched prefill on the dense tensor-core path: the n_tokens prompt tokens (host array) at
+ * positions [start_pos, start_pos + n_tokens) go through every layer at once, with every bucket
+ * row selected (the dense matmul of matrix.cl, basicMul :80-93, in place of bucketMul), and fill
+ * the KV cache.  The reference feeds a prompt through forward() one token at a time
+ * (test_generation.cpp:202-213); iam_model_forward does the same, at the chosen effort.
+ * logits_dev (vocab floats, may be NULL) receives the last token's logits; *next_token (may be
+ * NULL; the call then synchronises the stream) its greedy argmax.  The first call builds dense
+ * fp16 copies of the weights (as large as the bucket weights) and prefill scratch.
+ * Single-GPU models only (IAM_ERR_UNSUPPORTED for a tensor-parallel rank). */
+int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int start_pos, float* logits_dev,
+                      int* next_token, void* stream);
 /* Greedy generation on the device (the decode loop of test_generation.cpp:239-291 without
  * host round trips): step 0 decodes first_token at start_pos, every later step decodes the
  * previous step's argmax; the n_tokens generated ids land in tokens_dev.  Steps after the

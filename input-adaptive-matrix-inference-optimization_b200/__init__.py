@@ -250,6 +250,7 @@ _SIGNATURES.update({
     "iam_model_destroy": [_vp],
     "iam_model_reset": [_vp, _vp],
     "iam_model_forward": [_vp, _i32, _i32, _f32, _vp, _vp],
+    "iam_model_prefill": [_vp, _vp, _i32, _i32, _vp, _vp, _vp],
     "iam_model_generate": [_vp, _i32, _i32, _i32, _f32, _vp, _vp],
     "iam_model_set_kv": [_vp, _i32, _vp, _vp, _i32, _vp],
     "iam_model_fill_kv_random": [_vp, _i32, ctypes.c_ulonglong, _vp],
@@ -348,6 +349,15 @@ class Model:
 
     def forward(self, token, pos, effort, logits=None, stream=None):
         check(self.lib.iam_model_forward(self.h, token, pos, effort, _ptr(logits), _stream(stream)))
+
+    def prefill(self, tokens, start_pos=0, logits=None, stream=None):
+        """iam_model_prefill: the prompt through the dense tensor-core path in one pass; returns
+        the greedy next token."""
+        arr = (ctypes.c_int * len(tokens))(*[int(t) for t in tokens])
+        nxt = ctypes.c_int(-1)
+        check(self.lib.iam_model_prefill(self.h, arr, len(tokens), start_pos, _ptr(logits), ctypes.byref(nxt),
+                                         _stream(stream)))
+        return nxt.value
 
     def generate(self, first_token, start_pos, n_tokens, effort, tokens, stream=None):
         check(self.lib.iam_model_generate(self.h, first_token, start_pos, n_tokens, effort, _ptr(tokens),

@@ -23,7 +23,9 @@
 
 #include "iam_bucketmul_launch.h"
 #include "iam_common.cuh"
+#include "iam_dense.h"
 #include "iam_layers.h"
+#include "iam_prefill.h"
 #include "iam_tp.h"
 
 namespace iam {
@@ -44,6 +46,12 @@ struct Layer {
     uint16_t* attn_norm = nullptr;
     uint16_t* ffn_norm = nullptr;
     Matrix m[NMAT];
+};
+
+// Dense fp16 copies of a layer's matrices for the batched prefill (iam_dense_unpack layout:
+// every bucket row selected), rows stacked per launch: q|k|v, o, gate|up, down.
+struct DenseLayer {
+    uint16_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
 };
 
 // ------------------------------------------------------------------ tensor-parallel shards
@@ -183,6 +191,13 @@ struct iam_model_s {
     char* xwin = nullptr;         // this rank's window (exchanged activations, mailbox, flags)
     TpWindow win{};
     std::vector<void*> peer_maps;
+    // batched dense prefill (built by the first iam_model_prefill)
+    std::vector<DenseLayer> dense;
+    int pf_cap = 0;  // tokens per prefill chunk
+    int* pf_tok = nullptr;
+    float *pf_h = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_gu = nullptr, *pf_part = nullptr;
+    uint16_t *pf_hi = nullptr, *pf_lo = nullptr;
+    unsigned* pf_err = nullptr;
 };
 
 namespace {
@@ -770,6 +785,102 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
 
 bool effort_ok(float e) { return std::isfinite(e) && e > 0.0f && e <= 1.0f; }
 
+// Dense copies of every matrix and the chunk scratch of the prefill (once per model).
+int build_prefill(iam_model_s* m, cudaStream_t s) {
+    if (!m->dense.empty()) return IAM_OK;
+    const iam_model_config& c = m->cfg;
+    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim, f = c.ffn_dim, d = c.dim;
+    if (d % 8 || qn % 8 || f % 8) return fail(IAM_ERR_UNSUPPORTED, "prefill: dim, heads x head_dim and ffn_dim must be multiples of 8");
+    int rc;
+    std::vector<DenseLayer> dl(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        DenseLayer& D = dl[l];
+        const Layer& L = m->layers[l];
+        if ((rc = dalloc(m, &D.qkv, (size_t)(qn + 2 * kvn) * d)) || (rc = dalloc(m, &D.o, (size_t)d * qn)) ||
+            (rc = dalloc(m, &D.gu, (size_t)2 * f * d)) || (rc = dalloc(m, &D.down, (size_t)d * f)))
+            return rc;
+        struct Part { int which; uint16_t* dst; };
+        const Part parts[NMAT] = {{MQ, D.qkv},
+                                  {MK, D.qkv + (size_t)qn * d},
+                                  {MV, D.qkv + (size_t)(qn + kvn) * d},
+                                  {MO, D.o},
+                                  {MG, D.gu},
+                                  {MU, D.gu + (size_t)f * d},
+                                  {MD, D.down}};
+        for (const Part& p : parts) {
+            const Matrix& mat = L.m[p.which];
+            if ((rc = dense_unpack(mat.buckets, mat.in_dim, mat.cols, p.dst, mat.in_dim, s))) return rc;
+        }
+    }
+    int cap = 256;
+    if (const char* v = getenv("IAM_PREFILL_CHUNK")) cap = std::max(1, atoi(v));
+    cap = std::min(cap, c.max_ctx);
+    const size_t wide = (size_t)std::max(std::max(d, qn), f);
+    if ((rc = dalloc(m, &m->pf_tok, (size_t)cap)) || (rc = dalloc(m, &m->pf_h, (size_t)cap * d)) ||
+        (rc = dalloc(m, &m->pf_qkv, (size_t)cap * (qn + 2 * kvn))) || (rc = dalloc(m, &m->pf_att, (size_t)cap * qn)) ||
+        (rc = dalloc(m, &m->pf_gu, (size_t)cap * 2 * f)) || (rc = dalloc(m, &m->pf_hi, (size_t)cap * wide)) ||
+        (rc = dalloc(m, &m->pf_lo, (size_t)cap * wide)) ||
+        (rc = dalloc(m, &m->pf_part, (size_t)m->sm_count * kDenseBM * 128)) || (rc = dalloc(m, &m->pf_err, 1)))
+        return rc;
+    IAM_CUDA_TRY(cudaMemsetAsync(m->pf_err, 0, sizeof(unsigned), s));
+    m->pf_cap = cap;
+    m->dense.swap(dl);
+    return IAM_OK;
+}
+
+// y[t][:] (+)= W x[t] with x given as the hi / lo halves in m->pf_hi / m->pf_lo [n][k].
+int prefill_gemm(iam_model_s* m, const uint16_t* w, int out, int k, int n, float* y, const float* residual,
+                 cudaStream_t s) {
+    DenseProblem p{};
+    p.w = w;
+    p.m = out;
+    p.k = k;
+    p.ldw = k;
+    p.x_hi = m->pf_hi;
+    p.x_lo = m->pf_lo;
+    p.n = n;
+    p.y = y;
+    p.ldy = out;
+    p.residual = residual;
+    p.ldr = out;
+    p.partial = m->pf_part;
+    p.split = dense_auto_split(out, k, n, m->sm_count);
+    p.err = m->pf_err;
+    return dense_gemm(p, s);
+}
+
+// Prompt tokens [c0, c0 + n) at positions pos0 + t through every layer; leaves the residual
+// stream of its tokens in m->pf_h.
+int prefill_chunk(iam_model_s* m, const int* tokens_host, int n, int pos0, cudaStream_t s) {
+    const iam_model_config& c = m->cfg;
+    const int qn = c.n_heads * c.head_dim, kvn = c.n_kv_heads * c.head_dim, f = c.ffn_dim, d = c.dim;
+    const int ldq = qn + 2 * kvn;
+    int rc;
+    IAM_CUDA_TRY(cudaMemcpyAsync(m->pf_tok, tokens_host, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, s));
+    if ((rc = prefill_embed(m->embed, d, m->pf_tok, n, m->pf_h, s))) return rc;
+    const size_t layer_kv = (size_t)c.n_kv_heads * c.max_ctx * c.head_dim;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer& L = m->layers[l];
+        const DenseLayer& D = m->dense[l];
+        uint16_t* kc = m->k_cache + (size_t)l * layer_kv;
+        uint16_t* vc = m->v_cache + (size_t)l * layer_kv;
+        if ((rc = prefill_rms_split(m->pf_h, n, d, L.attn_norm, c.norm_eps, m->pf_hi, m->pf_lo, s)) ||
+            (rc = prefill_gemm(m, D.qkv, ldq, d, n, m->pf_qkv, nullptr, s)) ||
+            (rc = prefill_rope_kv(m->pf_qkv, n, ldq, c.n_heads, c.n_kv_heads, c.head_dim, m->rope, pos0, kc, vc,
+                                  c.max_ctx, s)) ||
+            (rc = prefill_attention(m->pf_qkv, ldq, n, c.n_heads, c.n_kv_heads, c.head_dim, kc, vc, c.max_ctx, pos0,
+                                    m->pf_att, qn, s)) ||
+            (rc = dense_split(m->pf_att, n, qn, qn, m->pf_hi, m->pf_lo, s)) ||
+            (rc = prefill_gemm(m, D.o, d, qn, n, m->pf_h, m->pf_h, s)) ||
+            (rc = prefill_rms_split(m->pf_h, n, d, L.ffn_norm, c.norm_eps, m->pf_hi, m->pf_lo, s)) ||
+            (rc = prefill_gemm(m, D.gu, 2 * f, d, n, m->pf_gu, nullptr, s)) ||
+            (rc = prefill_silu_split(m->pf_gu, n, f, m->pf_hi, m->pf_lo, s)) ||
+            (rc = prefill_gemm(m, D.down, d, f, n, m->pf_h, m->pf_h, s)))
+            return rc;
+    }
+    return IAM_OK;
+}
+
 int finish_create(iam_model_s* m, iam_model_t* out) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -980,6 +1091,48 @@ int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* lo
     if (pos < 0 || pos >= m->cfg.max_ctx) return fail(IAM_ERR_ARG, "iam_model_forward: pos out of range");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_forward: effort must be in (0, 1]");
     return enqueue_step(m, token, pos, effort, logits_dev ? logits_dev : m->logits, (cudaStream_t)stream);
+}
+
+int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int start_pos, float* logits_dev,
+                      int* next_token, void* stream) {
+    if (!m || !tokens_host) return fail(IAM_ERR_ARG, "iam_model_prefill: null argument");
+    if (m->tp_world > 1) return fail(IAM_ERR_UNSUPPORTED, "iam_model_prefill: single-GPU models only");
+    const iam_model_config& c = m->cfg;
+    if (n_tokens <= 0 || start_pos < 0 || (long long)start_pos + n_tokens > c.max_ctx)
+        return fail(IAM_ERR_ARG, "iam_model_prefill: positions outside [0, max_ctx)");
+    for (int i = 0; i < n_tokens; ++i)
+        if (tokens_host[i] < 0 || tokens_host[i] >= c.vocab) return fail(IAM_ERR_ARG, "iam_model_prefill: token out of range");
+    IAM_CUDA_TRY(cudaSetDevice(m->device));
+    const cudaStream_t s = (cudaStream_t)stream;
+    int rc = build_prefill(m, s);
+    if (rc) return rc;
+    int last_rows = 0;
+    for (int c0 = 0; c0 < n_tokens; c0 += m->pf_cap) {
+        last_rows = std::min(m->pf_cap, n_tokens - c0);
+        if ((rc = prefill_chunk(m, tokens_host + c0, last_rows, start_pos + c0, s))) return rc;
+    }
+    IAM_CUDA_TRY(cudaMemsetAsync(m->key, 0, sizeof(unsigned long long), s));
+    LMHeadParams hp{};
+    hp.W = m->lm_head;
+    hp.x = m->pf_h + (size_t)(last_rows - 1) * c.dim;
+    hp.gain = m->final_norm;
+    hp.eps = c.norm_eps;
+    hp.dim = c.dim;
+    hp.rows = m->vocab_local;
+    hp.row0 = m->vocab0;
+    hp.logits = logits_dev;
+    hp.argmax_key = m->key;
+    if ((rc = launch_lm_head(hp, 2 * m->sm_count, s, false))) return rc;
+    if (next_token) {
+        IAM_CUDA_TRY(cudaStreamSynchronize(s));
+        unsigned err = 0;
+        unsigned long long key = 0;
+        IAM_CUDA_TRY(cudaMemcpy(&err, m->pf_err, sizeof(err), cudaMemcpyDeviceToHost));
+        if (err) return fail(IAM_ERR_TIMEOUT, "iam_model_prefill: a dense-product pipeline wait gave up");
+        IAM_CUDA_TRY(cudaMemcpy(&key, m->key, sizeof(key), cudaMemcpyDeviceToHost));
+        *next_token = (int)(0xffffffffu - (unsigned)(key & 0xffffffffull));
+    }
+    return IAM_OK;
 }
 
 int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort, int* tokens_dev,

@@ -317,15 +317,35 @@ long ora_model_scratch_floats(const ora_config* c) {
     return 4 * d + 3 * q + 2 * kv + 3 * f + 4 * (c->head_dim / 2 + 1);
 }
 
+/* effort < 0: every bucket row selected (the dense path's product, bucketMul.cl:392-497 over
+ * the whole bucket matrix) instead of the cutoff search and dispatch. */
 static long ora_bm(const ora_bm_weight* w, const float* x, float effort, float* out,
                    int32_t* rows, int nthreads) {
+    if (effort < 0.0f) {
+        long n = 16L * w->in_dim;
+        for (long i = 0; i < n; ++i) rows[i] = (int32_t)i;
+        ora_bucket_mul(w->buckets, w->out_dim / 16, x, 0, rows, n, out, nthreads);
+        return n;
+    }
     return ora_bucketmul_full(x, w->stats, w->stats_stride, w->probes, w->buckets, 0, w->in_dim,
                               w->out_dim / 16, 16L * w->in_dim, effort, out, rows, NULL,
                               nthreads);
 }
 
+static int model_forward(const ora_model* m, int token, int pos, float effort, float* logits,
+                         long* sel_rows, int nthreads);
+
 int ora_model_forward(const ora_model* m, int token, int pos, float effort, float* logits,
                       long* sel_rows, int nthreads) {
+    return model_forward(m, token, pos, effort, logits, sel_rows, nthreads);
+}
+
+int ora_model_forward_dense(const ora_model* m, int token, int pos, float* logits, int nthreads) {
+    return model_forward(m, token, pos, -1.0f, logits, NULL, nthreads);
+}
+
+static int model_forward(const ora_model* m, int token, int pos, float effort, float* logits,
+                         long* sel_rows, int nthreads) {
     const ora_config* c = &m->cfg;
     long d = c->dim, qn = (long)c->n_heads * c->head_dim, kvn = (long)c->n_kv_heads * c->head_dim;
     long f = c->ffn_dim, hd = c->head_dim;

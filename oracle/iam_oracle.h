@@ -129,6 +129,11 @@ void ora_lm_head(const uint16_t* W, int rows, int cols, const float* x, float* l
 int ora_model_forward(const ora_model* m, int token, int pos, float effort, float* logits,
                       long* sel_rows, int nthreads);
 
+/* The same step with every bucket row of all 7*n_layers matmuls selected (no cutoff): the
+ * product the dense tensor-core path computes (its prefill is checked against this, token by
+ * token). */
+int ora_model_forward_dense(const ora_model* m, int token, int pos, float* logits, int nthreads);
+
 /* Size in floats of the scratch ora_model_forward allocates internally (for callers that
  * want to know the footprint). */
 long ora_model_scratch_floats(const ora_config* cfg);

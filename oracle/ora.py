@@ -58,6 +58,8 @@ def lib():
         L.ora_lm_head.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_int]
         L.ora_model_forward.restype = ctypes.c_int
         L.ora_model_forward.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, ctypes.c_int]
+        L.ora_model_forward_dense.restype = ctypes.c_int
+        L.ora_model_forward_dense.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -236,3 +238,9 @@ class OracleModel:
         best = lib().ora_model_forward(ctypes.byref(self.m), token, pos, effort, _p(logits), ctypes.byref(sel),
                                        nthreads)
         return best, logits, sel.value
+
+    def forward_dense(self, token, pos, nthreads=1):
+        """One step with every bucket row selected (the dense path's product)."""
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        best = lib().ora_model_forward_dense(ctypes.byref(self.m), token, pos, _p(logits), nthreads)
+        return best, logits
