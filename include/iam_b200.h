@@ -148,7 +148,7 @@ int iam_bucketize(const uint16_t* w_dev, int out_dim, int in_dim, uint16_t* buck
 /* Replaces the reference's dense GEMV kernels basicMul / basicMul2 (matrix.cl:80-127:
  * out[row] = sum_i v[i] * m[row][i], fp16 m, fp32 v) batched over tokens, on the tcgen05
  * tensor cores.  A handle owns the activation split (fp16 hi / lo) and split-K scratch for up
- * to max_tokens x max_in_dim activations and max_out_dim outputs. */
+ * to max_tokens (<= 65535) x max_in_dim activations and max_out_dim outputs. */
 typedef struct iam_dense_s* iam_dense_t;
 int iam_dense_create(int max_tokens, int max_in_dim, int max_out_dim, int device, iam_dense_t* out);
 int iam_dense_destroy(iam_dense_t h);

@@ -5,20 +5,22 @@
 // LM head).  Over the tokens of a prompt the same products form a GEMM, run here on the 5th
 // generation tensor cores:
 //
-//   * one CTA per (128 weight rows) x (BN tokens) tile [x K slice], 128 threads;
+//   * one CTA per (128 tokens) x (256 weight rows) tile [x K slice], 128 threads;
 //   * warp 0 lane 0 streams K in 64-element stages with TMA (cp.async.bulk.tensor.2d, 128-byte
-//     swizzle) into a ring of shared-memory stages: the weight tile [128][64] and the
-//     activation tiles hi / lo [BN][64]; "full" mbarriers carry the transaction bytes;
-//   * warp 1 lane 0 issues tcgen05.mma (kind::f16, M = 128, N = BN, K = 16, both operands
-//     K-major from shared memory) into fp32 accumulators in tensor memory (BN columns each):
-//     W * hi of even and of odd stages into two, W * lo into a third, so the sum carries ~22
-//     bits of each fp32 activation and no accumulator sees more than half of the K steps (the
-//     tensor core's accumulation rounding grows with the additions into one accumulator); a
+//     swizzle) into a ring of three 64 KB shared-memory stages: the activation tiles hi / lo
+//     [128][64] (operand A) and the weight tile [256][64] (operand B); "full" mbarriers carry
+//     the transaction bytes.  With the tokens as the MMA's M, one activation tile serves 256
+//     weight rows: the activations every CTA re-reads from L2 are half the weight bytes (hi
+//     and lo together equal them), where 128-row weight tiles made them twice the weight bytes;
+//   * warp 1 lane 0 issues tcgen05.mma (kind::f16, M = 128, N = 256, K = 16, both operands
+//     K-major from shared memory) into two fp32 accumulators in tensor memory (256 columns
+//     each, all 512 columns of the SM): hi x W and lo x W, so the sum carries ~22 bits of every
+//     fp32 activation and the small lo products never round against the large hi sum; a
 //     tcgen05.commit per stage frees the stage ("empty" mbarrier) once its MMAs have read it;
-//   * after the last commit all four warps read the accumulators back (tcgen05.ld 32x32b, warp
-//     w owns lanes 32(w%4)..+31 = weight rows), add them ((even + odd) + lo, IEEE fp32) and
-//     store Y (+ residual) row-contiguously, or a K-slice partial that a second, ordered pass
-//     sums (deterministic split-K).
+//   * after the last commit all four warps read the accumulators back (tcgen05.ld 32x32b: warp
+//     w owns lanes 32(w%4)..+31 = tokens, 16 output columns per load), add hi + lo (IEEE fp32)
+//     and store 16 consecutive outputs of their token (+ residual), or a K-slice partial that a
+//     second, ordered pass sums (deterministic split-K).
 //
 // Every wait on an mbarrier is bounded: after ~2 s the thread sets the error word and moves
 // on, so a broken pipeline ends the kernel instead of hanging it.
@@ -37,18 +39,21 @@ namespace {
 
 constexpr long long kDenseWaitCycles = 4000000000LL;  // ~2 s at the SM clock
 
-template <int BN>
+// One pipeline stage: the activation tiles hi / lo [kDenseBT][kDenseBK] (operand A, 16 KB each)
+// and the weight tile [kDenseBW][kDenseBK] (operand B, 32 KB), each 1024-byte aligned for the
+// 128-byte swizzle.
 struct Tile {
-    static constexpr int kA = kDenseBM * kDenseBK * 2;  // weight tile bytes (16 KB)
-    static constexpr int kB = BN * kDenseBK * 2;        // one activation tile (hi or lo)
-    static constexpr int kStage = kA + 2 * kB;
-    static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
-    // three fp32 accumulators of BN columns (tokens): hi products of even stages, of odd
-    // stages, and every lo product; allocated as the next power of two
-    static constexpr int kTmemCols = 3 * BN <= 256 ? 256 : 512;
+    static constexpr int kA = kDenseBT * kDenseBK * 2;  // one activation tile (hi or lo)
+    static constexpr int kB = kDenseBW * kDenseBK * 2;  // weight tile
+    static constexpr int kStage = 2 * kA + kB;          // 64 KB
+    static constexpr int kStages = 3;
+    // two fp32 accumulators of kDenseBW columns (outputs) x 128 lanes (tokens): the hi products
+    // and the lo products -- the whole tensor memory of the SM
+    static constexpr int kTmemCols = 2 * kDenseBW;
     static constexpr size_t kSmem = (size_t)kStages * kStage + 1024;  // + 1024-byte alignment slack
     static_assert(kA % 1024 == 0 && kB % 1024 == 0, "stage tiles must stay 1024-byte aligned");
-    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "BN: power of two, 32..256");
+    static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+    static_assert(kTmemCols == 512, "tensor memory columns");
 };
 
 IAM_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -149,11 +154,8 @@ IAM_DEV uint64_t sw128_desc(const void* tile) {
 }
 
 // Instruction descriptor of kind::f16: D fp32 (bits 4-5 = 1), A and B fp16 (formats 0),
-// both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-template <int BN>
-constexpr uint32_t idesc_f16_f32() {
-    return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kDenseBM >> 4) << 24);
-}
+// both K-major, N >> 3 at bit 17, M >> 4 at bit 24.  M = 128 tokens, N = 256 weight rows.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kDenseBW >> 3) << 17) | ((uint32_t)(kDenseBT >> 4) << 24);
 
 struct GemmArgs {
     int m, n, kb_total, kb_per_split, has_lo;
@@ -165,26 +167,37 @@ struct GemmArgs {
     unsigned* err;
 };
 
-template <int BN>
+// 16 consecutive floats of one row: vector stores when all are in range and dst is 16-byte
+// aligned, else element by element.
+IAM_DEV void store_row16(float* dst, const float (&v)[16], int count) {
+    if (count >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j < count) dst[j] = v[j];
+    }
+}
+
 __global__ void __launch_bounds__(128, 1)
     dense_gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap thi,
                       const __grid_constant__ CUtensorMap tlo, GemmArgs a) {
-    using T = Tile<BN>;
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[T::kStages];
-    __shared__ __align__(8) uint64_t empty_bar[T::kStages];
+    __shared__ __align__(8) uint64_t full_bar[Tile::kStages];
+    __shared__ __align__(8) uint64_t empty_bar[Tile::kStages];
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_slot;
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kDenseBM;
+    const int t0 = blockIdx.x * kDenseBT, o0 = blockIdx.y * kDenseBW;
     const int kb0 = blockIdx.z * a.kb_per_split;
     const int nkb = min(a.kb_total - kb0, a.kb_per_split);  // >= 1: the host sizes the grid so
-    const uint32_t stage_bytes = (uint32_t)(T::kA + (a.has_lo ? 2 : 1) * T::kB);
+    const uint32_t stage_bytes = (uint32_t)((a.has_lo ? 2 : 1) * Tile::kA + Tile::kB);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < T::kStages; ++s) {
+        for (int s = 0; s < Tile::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
@@ -192,7 +205,7 @@ __global__ void __launch_bounds__(128, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
-        tmem_alloc(&tmem_slot, T::kTmemCols);
+        tmem_alloc(&tmem_slot, Tile::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -205,31 +218,30 @@ __global__ void __launch_bounds__(128, 1)
     if (warp == 0 && lane == 0) {
         // producer: stage i of this slice into ring slot i % kStages once its MMAs are done
         for (int i = 0; i < nkb; ++i) {
-            const int s = i % T::kStages;
-            const uint32_t ph = (uint32_t)(i / T::kStages) & 1u;
+            const int s = i % Tile::kStages;
+            const uint32_t ph = (uint32_t)(i / Tile::kStages) & 1u;
             if (!mbar_wait(&empty_bar[s], ph ^ 1u, a.err)) break;
-            unsigned char* st = smem + (size_t)s * T::kStage;
+            unsigned char* st = smem + (size_t)s * Tile::kStage;
             mbar_expect_tx(&full_bar[s], stage_bytes);
             const int kx = (kb0 + i) * kDenseBK;
-            tma_load_2d(st, &tw, kx, m0, &full_bar[s]);
-            tma_load_2d(st + T::kA, &thi, kx, n0, &full_bar[s]);
-            if (a.has_lo) tma_load_2d(st + T::kA + T::kB, &tlo, kx, n0, &full_bar[s]);
+            tma_load_2d(st, &thi, kx, t0, &full_bar[s]);
+            if (a.has_lo) tma_load_2d(st + Tile::kA, &tlo, kx, t0, &full_bar[s]);
+            tma_load_2d(st + 2 * Tile::kA, &tw, kx, o0, &full_bar[s]);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA issuer: 4 K-steps of 16 per stage; hi into accumulator (i & 1), lo into the third
-        constexpr uint32_t idesc = idesc_f16_f32<BN>();
+        // MMA issuer: 4 K-steps of 16 per stage; hi products into columns [0, 256), lo into [256, 512)
         for (int i = 0; i < nkb; ++i) {
-            const int s = i % T::kStages;
-            const uint32_t ph = (uint32_t)(i / T::kStages) & 1u;
+            const int s = i % Tile::kStages;
+            const uint32_t ph = (uint32_t)(i / Tile::kStages) & 1u;
             if (!mbar_wait(&full_bar[s], ph, a.err)) break;
             tc_fence_after();
-            const unsigned char* st = smem + (size_t)s * T::kStage;
-            const uint64_t da = sw128_desc(st), dh = sw128_desc(st + T::kA), dl = sw128_desc(st + T::kA + T::kB);
+            const unsigned char* st = smem + (size_t)s * Tile::kStage;
+            const uint64_t dh = sw128_desc(st), dl = sw128_desc(st + Tile::kA), dw = sw128_desc(st + 2 * Tile::kA);
 #pragma unroll
             for (int kk = 0; kk < kDenseBK / 16; ++kk) {
-                tc_mma(tmem + (uint32_t)((i & 1) * BN), da + 2u * kk, dh + 2u * kk, idesc,
-                       (i >= 2 || kk > 0) ? 1u : 0u);
-                if (a.has_lo) tc_mma(tmem + 2u * BN, da + 2u * kk, dl + 2u * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+                const uint32_t acc = (i | kk) != 0 ? 1u : 0u;
+                tc_mma(tmem, dh + 2u * kk, dw + 2u * kk, kIdesc, acc);
+                if (a.has_lo) tc_mma(tmem + (uint32_t)kDenseBW, dl + 2u * kk, dw + 2u * kk, kIdesc, acc);
             }
             tc_commit(&empty_bar[s]);
         }
@@ -237,30 +249,35 @@ __global__ void __launch_bounds__(128, 1)
     }
     __syncwarp();
 
-    // epilogue: accumulator lanes = weight rows, columns = tokens
+    // epilogue: accumulator lanes = tokens, columns = weight rows; a thread stores 16
+    // consecutive outputs of its token per load
     mbar_wait(&done_bar, 0u, a.err);
     tc_fence_after();
     const int q = warp & 3;
-    const int m = m0 + q * 32 + lane;
+    const int t = t0 + q * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-    for (int c = 0; c < BN; c += 16) {
-        if (n0 + c >= a.n) break;  // warp-uniform
-        uint32_t r[16], r1[16], rl[16];
-        tmem_ld16(trow + (uint32_t)c, r);
-        if (nkb > 1) tmem_ld16(trow + (uint32_t)(BN + c), r1);  // odd stages exist (block-uniform)
-        if (a.has_lo) tmem_ld16(trow + (uint32_t)(2 * BN + c), rl);
-        if (m < a.m) {
+    if (t0 + q * 32 < a.n) {  // warp-uniform: this warp's 32 tokens hold at least one real one
+        for (int c = 0; c < kDenseBW; c += 16) {
+            const int o = o0 + c;
+            if (o >= a.m) break;  // warp-uniform
+            uint32_t rh[16], rl[16];
+            tmem_ld16(trow + (uint32_t)c, rh);
+            if (a.has_lo) tmem_ld16(trow + (uint32_t)(kDenseBW + c), rl);
+            if (t < a.n) {
+                const int cnt = min(16, a.m - o);
+                float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int t = n0 + c + j;
-                if (t < a.n) {
-                    float v = __uint_as_float(r[j]);
-                    if (nkb > 1) v += __uint_as_float(r1[j]);
-                    if (a.has_lo) v += __uint_as_float(rl[j]);
-                    if (a.partial != nullptr)
-                        a.partial[((size_t)blockIdx.z * a.n + t) * a.m + m] = v;
-                    else
-                        a.y[(size_t)t * a.ldy + m] = (a.residual ? a.residual[(size_t)t * a.ldr + m] : 0.0f) + v;
+                for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(rh[j]) + (a.has_lo ? __uint_as_float(rl[j]) : 0.0f);
+                if (a.partial != nullptr) {
+                    store_row16(a.partial + ((size_t)blockIdx.z * a.n + t) * a.m + o, v, cnt);
+                } else {
+                    if (a.residual) {
+                        const float* r = a.residual + (size_t)t * a.ldr + o;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (j < cnt) v[j] = r[j] + v[j];
+                    }
+                    store_row16(a.y + (size_t)t * a.ldy + o, v, cnt);
                 }
             }
         }
@@ -270,42 +287,70 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, T::kTmemCols);
+        tmem_dealloc(tmem, Tile::kTmemCols);
     }
 }
 
-// y[t][o] = residual[t][o] + sum over slices z (in order) of partial[z][t][o].
-__global__ void dense_reduce_kernel(const float* __restrict__ partial, int split, int n, int m, float* y, int ldy,
-                                    const float* residual, int ldr) {
+// y[t][o] = residual[t][o] + sum over slices z (in order) of partial[z][t][o].  Grid: (column
+// blocks of 4 x 256 outputs, tokens); `vec` = rows 16-byte aligned (float4 path).
+__global__ void __launch_bounds__(256) dense_reduce_kernel(const float* __restrict__ partial, int split, int n, int m,
+                                                            float* y, int ldy, const float* residual, int ldr,
+                                                            int vec) {
     pdl_wait();
-    const size_t total = (size_t)n * m;
-    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const int t = (int)(e / m), o = (int)(e % m);
-        float acc = partial[e];
-        for (int z = 1; z < split; ++z) acc += partial[(size_t)z * total + e];
-        y[(size_t)t * ldy + o] = (residual ? residual[(size_t)t * ldr + o] : 0.0f) + acc;
+    const int t = blockIdx.y;
+    const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (o < m) {
+        const size_t plane = (size_t)n * m;
+        const float* p = partial + (size_t)t * m + o;
+        float* dst = y + (size_t)t * ldy + o;
+        const float* r = residual ? residual + (size_t)t * ldr + o : nullptr;
+        if (vec && o + 4 <= m) {
+            float4 acc = *reinterpret_cast<const float4*>(p);
+            for (int z = 1; z < split; ++z) {
+                const float4 v = *reinterpret_cast<const float4*>(p + (size_t)z * plane);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            if (r) {
+                const float4 rv = *reinterpret_cast<const float4*>(r);
+                acc.x = rv.x + acc.x;
+                acc.y = rv.y + acc.y;
+                acc.z = rv.z + acc.z;
+                acc.w = rv.w + acc.w;
+            }
+            *reinterpret_cast<float4*>(dst) = acc;
+        } else {
+            for (int j = 0; j < 4 && o + j < m; ++j) {
+                float acc = p[j];
+                for (int z = 1; z < split; ++z) acc += p[(size_t)z * plane + j];
+                dst[j] = (r ? r[j] : 0.0f) + acc;
+            }
+        }
     }
     pdl_trigger();
 }
 
-__global__ void dense_split_kernel(const float* __restrict__ x, int n, int k, int ldx, uint16_t* __restrict__ hi,
-                                   uint16_t* __restrict__ lo) {
+// Grid: (column blocks of 4 x 256, tokens).  k % 4 == 0, x rows 16-byte aligned.
+__global__ void __launch_bounds__(256) dense_split_kernel(const float* __restrict__ x, int k, int ldx,
+                                                           uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
     pdl_wait();
-    const int k4 = k >> 2;
-    const size_t total = (size_t)n * k4;
-    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const int t = (int)(e / k4), i = (int)(e % k4) * 4;
+    const int t = blockIdx.y;
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i < k) {
         const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + i);
         const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y), h2 = __float2half_rn(v.z),
                      h3 = __float2half_rn(v.w);
         const size_t o = (size_t)t * k + i;
-        uint2 hv, lv;
+        uint2 hv;
         hv.x = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         hv.y = (uint32_t)__half_as_ushort(h2) | ((uint32_t)__half_as_ushort(h3) << 16);
         *reinterpret_cast<uint2*>(hi + o) = hv;
         if (lo != nullptr) {
             const __half l0 = __float2half_rn(v.x - __half2float(h0)), l1 = __float2half_rn(v.y - __half2float(h1)),
                          l2 = __float2half_rn(v.z - __half2float(h2)), l3 = __float2half_rn(v.w - __half2float(h3));
+            uint2 lv;
             lv.x = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
             lv.y = (uint32_t)__half_as_ushort(l2) | ((uint32_t)__half_as_ushort(l3) << 16);
             *reinterpret_cast<uint2*>(lo + o) = lv;
@@ -378,29 +423,18 @@ int make_map(CUtensorMap* map, const void* base, int inner, int rows, int ld, in
     return IAM_OK;
 }
 
-int grid_for(size_t items, int threads) {
-    int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t want = (items + threads - 1) / threads;
-    return (int)std::min<size_t>(want > 0 ? want : 1, (size_t)sms * 8);
-}
-
-int tokens_tile(int n) { return n <= 64 ? 64 : 128; }
-
-template <int BN>
 int launch_gemm(const DenseProblem& p, int split, int kb_total, int kb_per, cudaStream_t s, bool pdl) {
-    using T = Tile<BN>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(dense_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)T::kSmem);
+        attr_err = cudaFuncSetAttribute(dense_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)Tile::kSmem);
     });
     IAM_CUDA_TRY(attr_err);
     CUtensorMap tw, thi, tlo;
-    int rc = make_map(&tw, p.w, p.k, p.m, p.ldw, kDenseBM);
-    if (rc == IAM_OK) rc = make_map(&thi, p.x_hi, p.k, p.n, p.k, BN);
-    if (rc == IAM_OK) rc = make_map(&tlo, p.x_lo ? p.x_lo : p.x_hi, p.k, p.n, p.k, BN);
+    int rc = make_map(&tw, p.w, p.k, p.m, p.ldw, kDenseBW);
+    if (rc == IAM_OK) rc = make_map(&thi, p.x_hi, p.k, p.n, p.k, kDenseBT);
+    if (rc == IAM_OK) rc = make_map(&tlo, p.x_lo ? p.x_lo : p.x_hi, p.k, p.n, p.k, kDenseBT);
     if (rc != IAM_OK) return rc;
     GemmArgs a;
     a.m = p.m;
@@ -414,8 +448,8 @@ int launch_gemm(const DenseProblem& p, int split, int kb_total, int kb_per, cuda
     a.ldr = p.ldr;
     a.partial = split > 1 ? p.partial : nullptr;
     a.err = p.err;
-    const dim3 grid((p.n + BN - 1) / BN, (p.m + kDenseBM - 1) / kDenseBM, split);
-    IAM_CUDA_TRY(launch_ex(dense_gemm_kernel<BN>, grid, dim3(128), T::kSmem, s, pdl, tw, thi, tlo, a));
+    const dim3 grid((p.n + kDenseBT - 1) / kDenseBT, (p.m + kDenseBW - 1) / kDenseBW, split);
+    IAM_CUDA_TRY(launch_ex(dense_gemm_kernel, grid, dim3(128), Tile::kSmem, s, pdl, tw, thi, tlo, a));
     return IAM_OK;
 }
 
@@ -424,18 +458,17 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 int dense_split(const float* x, int n, int k, int ldx, uint16_t* hi, uint16_t* lo, cudaStream_t s, bool pdl) {
-    if (x == nullptr || hi == nullptr || n <= 0 || k <= 0) return fail(IAM_ERR_ARG, "dense_split: bad arguments");
+    if (x == nullptr || hi == nullptr || n <= 0 || k <= 0 || n > kDenseMaxTokens)
+        return fail(IAM_ERR_ARG, "dense_split: bad arguments");
     if (k % 4 != 0 || ldx % 4 != 0 || !aligned16(x) || (reinterpret_cast<uintptr_t>(hi) & 7u) ||
         (lo && (reinterpret_cast<uintptr_t>(lo) & 7u)))
         return fail(IAM_ERR_ARG, "dense_split: k and the row stride must be multiples of 4, x 16-byte aligned");
-    const size_t items = (size_t)n * (k / 4);
-    IAM_CUDA_TRY(launch_ex(dense_split_kernel, dim3(grid_for(items, 256)), dim3(256), 0, s, pdl, x, n, k, ldx, hi, lo));
+    IAM_CUDA_TRY(launch_ex(dense_split_kernel, dim3((k / 4 + 255) / 256, n), dim3(256), 0, s, pdl, x, k, ldx, hi, lo));
     return IAM_OK;
 }
 
 int dense_auto_split(int m, int k, int n, int sms) {
-    const int bn = tokens_tile(n);
-    const long tiles = (long)((m + kDenseBM - 1) / kDenseBM) * ((n + bn - 1) / bn);
+    const long tiles = (long)((m + kDenseBW - 1) / kDenseBW) * ((n + kDenseBT - 1) / kDenseBT);
     const int kb = (k + kDenseBK - 1) / kDenseBK;
     if (tiles >= sms) return 1;
     int split = (int)std::max(1L, (long)sms / tiles);
@@ -445,7 +478,8 @@ int dense_auto_split(int m, int k, int n, int sms) {
 }
 
 int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl) {
-    if (p.w == nullptr || p.x_hi == nullptr || p.y == nullptr || p.m <= 0 || p.k <= 0 || p.n <= 0)
+    if (p.w == nullptr || p.x_hi == nullptr || p.y == nullptr || p.m <= 0 || p.k <= 0 || p.n <= 0 ||
+        p.n > kDenseMaxTokens)
         return fail(IAM_ERR_ARG, "dense_gemm: bad arguments");
     if (p.k % 8 != 0 || p.ldw % 8 != 0 || p.ldw < p.k || !aligned16(p.w) || !aligned16(p.x_hi) ||
         (p.x_lo && !aligned16(p.x_lo)))
@@ -457,12 +491,11 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl) {
     int kb_per = (kb_total + split - 1) / split;
     split = (kb_total + kb_per - 1) / kb_per;  // every slice non-empty
     if (split > 1 && p.partial == nullptr) return fail(IAM_ERR_ARG, "dense_gemm: split-K needs a partial buffer");
-    const int rc = tokens_tile(p.n) == 64 ? launch_gemm<64>(p, split, kb_total, kb_per, s, pdl)
-                                          : launch_gemm<128>(p, split, kb_total, kb_per, s, pdl);
+    const int rc = launch_gemm(p, split, kb_total, kb_per, s, pdl);
     if (rc != IAM_OK || split == 1) return rc;
-    const size_t items = (size_t)p.n * p.m;
-    IAM_CUDA_TRY(launch_ex(dense_reduce_kernel, dim3(grid_for(items, 256)), dim3(256), 0, s, pdl,
-                           (const float*)p.partial, split, p.n, p.m, p.y, p.ldy, p.residual, p.ldr));
+    const int vec = p.m % 4 == 0 && p.ldy % 4 == 0 && aligned16(p.y) && (!p.residual || (p.ldr % 4 == 0 && aligned16(p.residual)));
+    IAM_CUDA_TRY(launch_ex(dense_reduce_kernel, dim3((p.m + 1023) / 1024, p.n), dim3(256), 0, s, pdl,
+                           (const float*)p.partial, split, p.n, p.m, p.y, p.ldy, p.residual, p.ldr, vec));
     return IAM_OK;
 }
 
@@ -507,8 +540,8 @@ int iam_dense_destroy(iam_dense_t h) {
 int iam_dense_create(int max_tokens, int max_in_dim, int max_out_dim, int device, iam_dense_t* out) {
     if (!out) return fail(IAM_ERR_ARG, "iam_dense_create: null out");
     *out = nullptr;
-    if (max_tokens <= 0 || max_in_dim <= 0 || max_out_dim <= 0 || max_in_dim % 8 != 0)
-        return fail(IAM_ERR_ARG, "iam_dense_create: sizes must be positive and max_in_dim % 8 == 0");
+    if (max_tokens <= 0 || max_tokens > kDenseMaxTokens || max_in_dim <= 0 || max_out_dim <= 0 || max_in_dim % 8 != 0)
+        return fail(IAM_ERR_ARG, "iam_dense_create: sizes must be positive, max_tokens <= 65535, max_in_dim % 8 == 0");
     int rc = iam_device_info(device, nullptr, nullptr, nullptr);
     if (rc) return rc;
     IAM_CUDA_TRY(cudaSetDevice(device));
@@ -518,9 +551,9 @@ int iam_dense_create(int max_tokens, int max_in_dim, int max_out_dim, int device
     h->max_in = max_in_dim;
     h->max_out = max_out_dim;
     cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device);
-    // the automatic split keeps tiles x split <= SMs, so its partials fit in SMs x 128 x 128
+    // the automatic split keeps tiles x split <= SMs, so its partials fit in SMs x one tile
     const size_t act = (size_t)max_tokens * max_in_dim;
-    h->partial_cap = (size_t)h->sms * kDenseBM * 128;
+    h->partial_cap = dense_partial_floats(h->sms);
     cudaError_t e = cudaMalloc(&h->hi, act * sizeof(uint16_t));
     if (e == cudaSuccess) e = cudaMalloc(&h->lo, act * sizeof(uint16_t));
     if (e == cudaSuccess) e = cudaMalloc(&h->partial, h->partial_cap * sizeof(float));

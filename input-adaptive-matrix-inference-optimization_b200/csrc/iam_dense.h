@@ -13,9 +13,14 @@
 
 namespace iam {
 
-constexpr int kDenseBM = 128;      // weight rows (outputs) per tile: the MMA's M
+constexpr int kDenseBT = 128;      // tokens per tile: the MMA's M (operand A = activations)
+constexpr int kDenseBW = 256;      // weight rows (outputs) per tile: the MMA's N (operand B = W)
 constexpr int kDenseBK = 64;       // K per pipeline stage: one 128-byte swizzle row of fp16
 constexpr int kDenseMaxSplit = 8;  // K slices of one tile at most (deterministic second pass)
+constexpr int kDenseMaxTokens = 65535;  // tokens per call (the element-wise passes grid them in y)
+
+// Split-K scratch (floats) that covers every split dense_auto_split picks on `sms` SMs.
+inline size_t dense_partial_floats(int sms) { return (size_t)sms * kDenseBT * kDenseBW; }
 
 struct DenseProblem {
     const uint16_t* w;      // [m][ldw] fp16, K contiguous (ldw >= k, ldw % 8 == 0, 16-byte aligned base)

@@ -820,7 +820,7 @@ int build_prefill(iam_model_s* m, cudaStream_t s) {
         (rc = dalloc(m, &m->pf_qkv, (size_t)cap * (qn + 2 * kvn))) || (rc = dalloc(m, &m->pf_att, (size_t)cap * qn)) ||
         (rc = dalloc(m, &m->pf_gu, (size_t)cap * 2 * f)) || (rc = dalloc(m, &m->pf_hi, (size_t)cap * wide)) ||
         (rc = dalloc(m, &m->pf_lo, (size_t)cap * wide)) ||
-        (rc = dalloc(m, &m->pf_part, (size_t)m->sm_count * kDenseBM * 128)) || (rc = dalloc(m, &m->pf_err, 1)))
+        (rc = dalloc(m, &m->pf_part, dense_partial_floats(m->sm_count))) || (rc = dalloc(m, &m->pf_err, 1)))
         return rc;
     IAM_CUDA_TRY(cudaMemsetAsync(m->pf_err, 0, sizeof(unsigned), s));
     m->pf_cap = cap;

@@ -31,6 +31,22 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(const uint16_t* __restr
     for (int i = threadIdx.x; i < dim; i += blockDim.x) o[i] = h2f(e[i]);
 }
 
+IAM_DEV void split_store4(float4 v, uint16_t* hi, uint16_t* lo, size_t o) {  // o % 4 == 0
+    const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y), h2 = __float2half_rn(v.z),
+                 h3 = __float2half_rn(v.w);
+    uint2 hv, lv;
+    hv.x = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+    hv.y = (uint32_t)__half_as_ushort(h2) | ((uint32_t)__half_as_ushort(h3) << 16);
+    lv.x = (uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(v.x, __half2float(h0)))) |
+           ((uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(v.y, __half2float(h1)))) << 16);
+    lv.y = (uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(v.z, __half2float(h2)))) |
+           ((uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(v.w, __half2float(h3)))) << 16);
+    *reinterpret_cast<uint2*>(hi + o) = hv;
+    *reinterpret_cast<uint2*>(lo + o) = lv;
+}
+
+// One CTA per row.  The sum of squares: 256 runs of dim/256 contiguous elements, then the
+// halving tree (levels 128..32 in shared memory, 16..1 with shuffles: the same pairs).
 __global__ void __launch_bounds__(256) rms_split_kernel(const float* __restrict__ h, int dim,
                                                          const uint16_t* __restrict__ gain, float eps,
                                                          uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
@@ -41,38 +57,70 @@ __global__ void __launch_bounds__(256) rms_split_kernel(const float* __restrict_
     if (dim % 256 == 0) {
         const int e = dim / 256;
         float s = 0.0f;
-        for (int i = tid * e; i < tid * e + e; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+        if (e % 4 == 0) {
+            const float4* xv = reinterpret_cast<const float4*>(x + tid * e);
+            for (int i = 0; i < e / 4; ++i) {
+                const float4 v = xv[i];
+                s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+                s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+                s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+                s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+            }
+        } else {
+            for (int i = tid * e; i < tid * e + e; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+        }
         part[tid] = s;
         __syncthreads();
-        for (int st = 128; st > 0; st >>= 1) {
+        for (int st = 128; st >= 32; st >>= 1) {
             if (tid < st) part[tid] = __fadd_rn(part[tid], part[tid + st]);
             __syncthreads();
+        }
+        if (tid < 32) {
+            float v = part[tid];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
+            if (tid == 0) part[0] = v;
         }
     } else if (tid == 0) {  // small widths: one running sum, as the reference's scalar path
         float s = 0.0f;
         for (int i = 0; i < dim; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
         part[0] = s;
     }
+    __syncthreads();
     if (tid == 0) s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(part[0], (float)dim), eps)));
     __syncthreads();
     const float scale = s_scale;
-    for (int i = tid; i < dim; i += 256) {
-        const float v = __fmul_rn(x[i], scale);
-        split_store(gain ? __fmul_rn(h2f(gain[i]), v) : v, hi, lo, (size_t)t * dim + i);
+    if (dim % 4 == 0) {
+        for (int i = tid * 4; i < dim; i += 256 * 4) {
+            const float4 xv = *reinterpret_cast<const float4*>(x + i);
+            float4 v = make_float4(__fmul_rn(xv.x, scale), __fmul_rn(xv.y, scale), __fmul_rn(xv.z, scale),
+                                   __fmul_rn(xv.w, scale));
+            if (gain) {
+                const uint2 g = *reinterpret_cast<const uint2*>(gain + i);
+                v.x = __fmul_rn(h2f(g.x & 0xffffu), v.x);
+                v.y = __fmul_rn(h2f(g.x >> 16), v.y);
+                v.z = __fmul_rn(h2f(g.y & 0xffffu), v.z);
+                v.w = __fmul_rn(h2f(g.y >> 16), v.w);
+            }
+            split_store4(v, hi, lo, (size_t)t * dim + i);
+        }
+    } else {
+        for (int i = tid; i < dim; i += 256) {
+            const float v = __fmul_rn(x[i], scale);
+            split_store(gain ? __fmul_rn(h2f(gain[i]), v) : v, hi, lo, (size_t)t * dim + i);
+        }
     }
 }
 
-__global__ void __launch_bounds__(256) rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int n_kv, int hd,
-                                                       const float* __restrict__ rope, int pos0,
-                                                       uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache,
-                                                       int max_ctx) {
-    const int t = blockIdx.x, p = pos0 + t, half = hd / 2;
-    float* row = qkv + (size_t)t * ld;
-    const float* cs = rope + (size_t)p * half * 2;
-    for (int e = threadIdx.x; e < (n_heads + n_kv) * half; e += blockDim.x) {
-        const int head = e / half, d = e % half;
-        const float c = cs[2 * d], s = cs[2 * d + 1];
-        float* base = row + (size_t)head * hd;  // k heads follow the q heads in the row
+// Grid (tokens, n_heads + 2 n_kv): block y < n_heads rotates query head y in place, the next
+// n_kv rotate the key heads into the cache, the last n_kv copy the value heads.  hd / 2 threads.
+__global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int n_kv, int hd,
+                               const float* __restrict__ rope, int pos0, uint16_t* __restrict__ k_cache,
+                               uint16_t* __restrict__ v_cache, int max_ctx) {
+    const int t = blockIdx.x, head = blockIdx.y, d = threadIdx.x, p = pos0 + t, half = hd / 2;
+    float* base = qkv + (size_t)t * ld + (size_t)head * hd;  // k heads follow the q heads, v the k
+    if (head < n_heads + n_kv) {
+        const float c = rope[((size_t)p * half + d) * 2], s = rope[((size_t)p * half + d) * 2 + 1];
         const float m0 = base[d], m1 = base[d + half];
         const float o0 = __fsub_rn(__fmul_rn(m0, c), __fmul_rn(m1, s));
         const float o1 = __fadd_rn(__fmul_rn(m1, c), __fmul_rn(m0, s));
@@ -84,11 +132,10 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(float* __restrict__ qkv, i
             kr[d] = __half_as_ushort(__float2half_rn(o0));
             kr[d + half] = __half_as_ushort(__float2half_rn(o1));
         }
-    }
-    const float* v = row + (size_t)(n_heads + n_kv) * hd;
-    for (int e = threadIdx.x; e < n_kv * hd; e += blockDim.x) {
-        const int kvh = e / hd, d = e % hd;
-        v_cache[((size_t)kvh * max_ctx + p) * hd + d] = __half_as_ushort(__float2half_rn(v[e]));
+    } else {
+        uint16_t* vr = v_cache + ((size_t)(head - n_heads - n_kv) * max_ctx + p) * hd;
+        vr[d] = __half_as_ushort(__float2half_rn(base[d]));
+        vr[d + half] = __half_as_ushort(__float2half_rn(base[d + half]));
     }
 }
 
@@ -175,18 +222,19 @@ __global__ void prefill_attention_kernel(const float* __restrict__ qkv, int ldq,
     for (int i = 0; i < VD; ++i) op[i] = acc[i] / l;
 }
 
-__global__ void silu_split_kernel(const float* __restrict__ gu, int n, int ffn, uint16_t* __restrict__ hi,
-                                  uint16_t* __restrict__ lo) {
-    const size_t total = (size_t)n * ffn;
-    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const size_t t = e / ffn, i = e % ffn;
-        const float g = gu[t * 2 * ffn + i], u = gu[t * 2 * ffn + ffn + i];
-        split_store(__fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, expf(-g))), hi, lo, e);
-    }
-}
-
-int blocks_for(size_t items) {
-    return (int)std::min<size_t>((items + 255) / 256, (size_t)148 * 16);
+// Grid (column blocks of 4 x 256, tokens); ffn % 4 == 0.
+__global__ void __launch_bounds__(256) silu_split_kernel(const float* __restrict__ gu, int ffn,
+                                                          uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+    const int t = blockIdx.y;
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i >= ffn) return;
+    const float4 g = *reinterpret_cast<const float4*>(gu + (size_t)t * 2 * ffn + i);
+    const float4 u = *reinterpret_cast<const float4*>(gu + (size_t)t * 2 * ffn + ffn + i);
+    const float4 a = make_float4(__fdiv_rn(__fmul_rn(u.x, g.x), __fadd_rn(1.0f, expf(-g.x))),
+                                 __fdiv_rn(__fmul_rn(u.y, g.y), __fadd_rn(1.0f, expf(-g.y))),
+                                 __fdiv_rn(__fmul_rn(u.z, g.z), __fadd_rn(1.0f, expf(-g.z))),
+                                 __fdiv_rn(__fmul_rn(u.w, g.w), __fadd_rn(1.0f, expf(-g.w))));
+    split_store4(a, hi, lo, (size_t)t * ffn + i);
 }
 
 }  // namespace
@@ -209,7 +257,9 @@ int prefill_rms_split(const float* h, int n, int dim, const uint16_t* gain, floa
 int prefill_rope_kv(float* qkv, int n, int ld, int n_heads, int n_kv, int hd, const float* rope, int pos0,
                     uint16_t* k_cache, uint16_t* v_cache, int max_ctx, cudaStream_t s) {
     if (n <= 0) return IAM_OK;
-    rope_kv_kernel<<<n, 256, 0, s>>>(qkv, ld, n_heads, n_kv, hd, rope, pos0, k_cache, v_cache, max_ctx);
+    if (hd % 2 || hd / 2 > 1024 || n > 65535) return fail(IAM_ERR_UNSUPPORTED, "prefill rope: head_dim / tokens");
+    rope_kv_kernel<<<dim3(n, n_heads + 2 * n_kv), hd / 2, 0, s>>>(qkv, ld, n_heads, n_kv, hd, rope, pos0, k_cache,
+                                                                 v_cache, max_ctx);
     IAM_CUDA_TRY(cudaGetLastError());
     return IAM_OK;
 }
@@ -233,7 +283,8 @@ int prefill_attention(const float* qkv, int ldq, int n, int n_heads, int n_kv, i
 
 int prefill_silu_split(const float* gu, int n, int ffn, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
     if (n <= 0) return IAM_OK;
-    silu_split_kernel<<<blocks_for((size_t)n * ffn), 256, 0, s>>>(gu, n, ffn, hi, lo);
+    if (ffn % 4 || n > 65535) return fail(IAM_ERR_UNSUPPORTED, "prefill silu: ffn % 4 / tokens");
+    silu_split_kernel<<<dim3((ffn / 4 + 255) / 256, n), 256, 0, s>>>(gu, ffn, hi, lo);
     IAM_CUDA_TRY(cudaGetLastError());
     return IAM_OK;
 }
