@@ -2,7 +2,7 @@
 """bench.py -- B200 benchmark of the Effort-style dynamic-sparse decode path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode|bucketmul] [--effort 0.25]
+                  [--workload decode|bucketmul|prefill] [--effort 0.25]
 
 Prints ONE JSON line (rank 0).
 
@@ -20,6 +20,14 @@ captured step.  Weights (13.9 GB) exceed the 126 MB L2 by two orders of magnitud
 
 `bucketmul`: one step = the 7 bucketMuls of one Mistral layer on
 alternating weight sets; value = effective GB/s.
+
+`prefill`: one step = the config-4 prompt (128 tokens) ingested in one batched pass on the dense
+tensor-core path (iam_model_prefill: every bucket row selected, tcgen05 products); value =
+prompt tokens/s.  The roofline is the dense GEMM kernel's tensor throughput: 2 x tokens x
+(out x in) flops per product over the GEMM launches' CUDA-event time at the prefill's shapes
+(the fp16 hi + lo activation split doubles the tensor work; flops are counted once).  The
+reference ingests a prompt one forward() at a time (test_generation.cpp:202-213); the decode
+line reports that time beside the batched prefill.
 
 `--impl reference` times the CPU restatement of the reference's kernels (oracle/, every
 host thread) on the same workload.
@@ -417,6 +425,16 @@ def run_decode(args, rank, world):
         e2e_s = float(t[0])
     e2e_tok_s = n_e2e / e2e_s
 
+    prefill = None
+    if world == 1:  # the prompt again, in one batched pass on the dense tensor-core path
+        prompt = prompt_tokens(cfg.vocab)
+        model.prefill(prompt, 0, None)  # builds the dense weight copies once
+        pf_ms = time_prefill(model, prompt, 3)
+        prefill = {"prompt_tokens": len(prompt), "ms": round(pf_ms, 3),
+                   "tokens_per_s": round(len(prompt) / (pf_ms * 1e-3), 1),
+                   "path": "iam_model_prefill (every bucket row selected, tcgen05 products)",
+                   "note": "the timed decode above ingested the prompt token by token (the reference's way)"}
+
     res = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -451,10 +469,178 @@ def run_decode(args, rank, world):
                                                os.environ.get("IAM_TP_COLL", "p2p") != "nccl" else 0)),
         "clocks": clk.summary(),
     }
+    if prefill:
+        res["prefill"] = prefill
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU port runs on rank 0 at N=1 only
         res["cpu_baseline"] = cpu_baseline_decode(model, cfg, args.effort, budget_s=args.cpu_seconds)
     model.close()  # its captured graph holds NCCL work: released before the process group
     return res
+
+
+def dense_split_for(m, k, n, sms=148):
+    """The split-K the library picks for one dense product (dense_auto_split in iam_dense.cu)."""
+    tiles = -(-m // 256) * -(-n // 128)
+    kb = -(-k // 64)
+    if tiles >= sms:
+        return 1
+    split = min(max(1, sms // tiles), 8, max(1, kb // 4))
+    per = -(-kb // split)
+    return -(-kb // per)
+
+
+def prefill_shapes(cfg):
+    qn, kvn = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+    return [(qn + 2 * kvn, cfg.dim), (cfg.dim, qn), (2 * cfg.ffn_dim, cfg.dim), (cfg.dim, cfg.ffn_dim)]
+
+
+def time_prefill(model, tokens, reps):
+    import torch
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(reps):
+        model.prefill(tokens, 0, None)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def gemm_roofline(iam, torch, dev, cfg, n, reps=5):
+    """CUDA-event time of the dense GEMM launches of one prefill layer at n tokens (random
+    weights of the same shapes: the kernel's time depends on the shapes only)."""
+    shapes = prefill_shapes(cfg)
+    d = iam.Dense(max_tokens=n, max_in_dim=max(k for _, k in shapes), max_out_dim=max(m for m, _ in shapes),
+                  device=dev.index)
+    flops, ms = 0.0, 0.0
+    for m, k in shapes:
+        w = (torch.randn(m, k, device=dev) * 0.02).half()
+        x = torch.randn(n, k, device=dev)
+        y = torch.empty(n, m, device=dev)
+        d.gemm(w, x, y)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            d.gemm(w, x, y)
+        b.record()
+        torch.cuda.synchronize()
+        ms += a.elapsed_time(b) / reps
+        flops += 2.0 * n * m * k
+        del w, x, y
+    d.status()
+    d.close()
+    return flops, ms
+
+
+def run_prefill(args, rank, world):
+    """Batched dense prefill of the config-4 prompt; under torchrun every rank runs its own
+    replica (the prefill does not shard) and value is the sum over ranks."""
+    import torch
+    iam = load_pkg()
+    dev = torch.device(f"cuda:{int(os.environ.get('LOCAL_RANK', 0))}")
+    torch.cuda.set_device(dev)
+    cfg = mistral_cfg(iam, PROMPT_LEN + 8, args.layers)
+    model = iam.Model.random(cfg, seed=0, device=dev.index)
+    tokens = prompt_tokens(cfg.vocab)
+    P = len(tokens)
+    t_dense = time.perf_counter()
+    model.prefill(tokens, 0, None)  # builds the dense weight copies once
+    torch.cuda.synchronize()
+    dense_build_s = time.perf_counter() - t_dense
+    time_prefill(model, tokens, args.warmup)
+    if world > 1:
+        torch.distributed.barrier()
+    with ClockSampler(dev.index) as clk:
+        ms = time_prefill(model, tokens, args.steps)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t[0])
+    tok_s = world * P / (ms * 1e-3)
+    # the reference's way: the same prompt through the decode step, one token at a time
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for pos, tok in enumerate(tokens):
+        model.forward(tok, pos, args.effort, logits)
+    b.record()
+    torch.cuda.synchronize()
+    tbt_ms = a.elapsed_time(b)
+    # e2e: host tokens in, the last token's logits back to pinned host memory
+    host_logits = torch.empty(cfg.vocab, dtype=torch.float32).pin_memory()
+    reps = max(3, min(args.steps, 10))
+    torch.cuda.synchronize()
+    e0 = time.perf_counter()
+    for _ in range(reps):
+        model.prefill(tokens, 0, logits)
+        host_logits.copy_(logits, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_tok_s = world * P * reps / (time.perf_counter() - e0)
+    flops, gemm_ms = gemm_roofline(iam, torch, dev, cfg, P)
+    peak = measured_tensor_peak()
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
+    splits = [dense_split_for(m, k, P) for m, k in prefill_shapes(cfg)]
+    launches = 1 + cfg.n_layers * (4 + sum(1 for sp in splits if sp > 1) + 2 + 1 + 1 + 1 + 1) + 2
+    res = {
+        "metric": METRIC, "value": round(tok_s, 1), "unit": "prompt tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x (f16 hi + f16 lo), f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": ("prefill: config 4 prompt (128 tokens, seed 1) through the 32-layer Mistral-7B "
+                                "shape in one batched pass on the dense tensor-core path"),
+                   "model": "Mistral-7B (random init)" + (f", {cfg.n_layers} layers" if args.layers else ""),
+                   "prompt_tokens": P, "global_batch": 1, "seq_len": P,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 13.9 GB of dense weights streamed per prefill",
+                   "token_by_token_ms": round(tbt_ms, 2),
+                   "token_by_token_effort": args.effort,
+                   "speedup_vs_token_by_token": round(tbt_ms / ms, 1),
+                   "dense_weights_build_s": round(dense_build_s, 2)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
+                     "frac": round(achieved / peak[0], 4), "traffic": None, "peak_source": peak[1],
+                     "kernel": "dense_gemm_kernel",
+                     "flops_per_layer": flops, "gemm_ms_per_layer": round(gemm_ms, 4),
+                     "note": "flops counted once per product; the hi + lo activation halves run two MMAs each"},
+        "e2e": {"value": round(e2e_tok_s, 1), "unit": "prompt tokens/s", "h2d_bytes_per_step": 4 * P,
+                "d2h_bytes_per_step": 4 * cfg.vocab},
+        "gpu_launches": world * args.steps * launches,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_prefill(model, cfg, budget_s=args.cpu_seconds)
+    model.close()
+    return res
+
+
+def measured_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            v = json.load(f).get("bf16_tflops")
+        if v:
+            return float(v), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        pass
+    return 1590.0, "fallback (1.59 PFLOP/s)"
+
+
+def cpu_baseline_prefill(model, cfg, budget_s=10.0, tokens=2):
+    """The oracle's dense decode step (every bucket row selected) on every host core, token by
+    token: the reference's way of ingesting a prompt, on its CPU restatement."""
+    sys.path.insert(0, ROOT)
+    from oracle import ora
+    om = ora.OracleModel(cfg.as_dict(), model.export_weights())
+    threads = os.cpu_count() or 1
+    prompt = prompt_tokens(cfg.vocab)
+    t0 = time.perf_counter()
+    n = 0
+    for pos, tok in enumerate(prompt):
+        om.forward_dense(tok, pos, nthreads=threads)
+        n += 1
+        if n >= tokens or time.perf_counter() - t0 >= budget_s:
+            break
+    sec = time.perf_counter() - t0
+    return {"value": round(n / sec, 3), "unit": "prompt tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} prompt tokens of config 4 through the oracle's dense decode step ({cfg.n_layers} layers)"}
 
 
 def cpu_baseline_decode(model, cfg, effort, budget_s=10.0, steps=None):
@@ -536,7 +722,7 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "bucketmul"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "bucketmul", "prefill"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--effort", type=float, default=0.25)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -563,6 +749,8 @@ def main():
     try:
         if args.workload == "decode":
             res = run_decode(args, rank, world)
+        elif args.workload == "prefill":
+            res = run_prefill(args, rank, world)
         else:
             res = run_bucketmul(args, rank, world)
         if rank == 0 and res is not None:

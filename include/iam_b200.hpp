@@ -167,6 +167,15 @@ class MistralModel {
         check(iam_model_reset(handle, gpu->stream), "MistralModel::reset_caches");
         gpu->eval();
     }
+    // The whole prompt in one batched pass on the dense tensor-core path, in place of one
+    // forward() per prompt token (test_generation.cpp:202-213); returns the greedy next token.
+    int prefill(const int* tokens, int n_tokens, int start_pos, BufferWrapper<float>* logits_out) {
+        int next = -1;
+        check(iam_model_prefill(handle, tokens, n_tokens, start_pos, logits_out ? logits_out->buffer : nullptr,
+                                &next, gpu->stream),
+              "MistralModel::prefill");
+        return next;
+    }
 };
 
 }  // namespace iam_shim
