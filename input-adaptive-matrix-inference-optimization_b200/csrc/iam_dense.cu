@@ -165,6 +165,9 @@ struct GemmArgs {
     int ldr;
     float* partial;  // split-K: [split][n][m]; null when the tile writes y directly
     unsigned* err;
+    uint16_t* silu_hi;  // SiLU epilogue (see DenseProblem); null: plain store
+    uint16_t* silu_lo;
+    int ld_silu;
 };
 
 // 16 consecutive floats of one row: vector stores when all are in range and dst is 16-byte
@@ -256,7 +259,43 @@ __global__ void __launch_bounds__(128, 1)
     const int q = warp & 3;
     const int t = t0 + q * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-    if (t0 + q * 32 < a.n) {  // warp-uniform: this warp's 32 tokens hold at least one real one
+    if (a.silu_hi != nullptr && t0 + q * 32 < a.n) {
+        // columns [0, 128) hold the gate rows, [128, 256) the up rows of the same FFN columns
+        const int f0 = blockIdx.y * (kDenseBW / 2);
+        for (int c = 0; c < kDenseBW / 2; c += 16) {
+            uint32_t gh[16], gl[16], uh[16], ul[16];
+            tmem_ld16(trow + (uint32_t)c, gh);
+            tmem_ld16(trow + (uint32_t)(kDenseBW / 2 + c), uh);
+            if (a.has_lo) {
+                tmem_ld16(trow + (uint32_t)(kDenseBW + c), gl);
+                tmem_ld16(trow + (uint32_t)(kDenseBW + kDenseBW / 2 + c), ul);
+            }
+            if (t < a.n) {
+                uint32_t hw[8], lw[8];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    float av[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const float g = __uint_as_float(gh[j + u]) + (a.has_lo ? __uint_as_float(gl[j + u]) : 0.0f);
+                        const float up = __uint_as_float(uh[j + u]) + (a.has_lo ? __uint_as_float(ul[j + u]) : 0.0f);
+                        av[u] = __fdiv_rn(__fmul_rn(up, g), __fadd_rn(1.0f, expf(-g)));  // matrix.cl:31
+                    }
+                    const __half h0 = __float2half_rn(av[0]), h1 = __float2half_rn(av[1]);
+                    hw[j / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                    lw[j / 2] = (uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(av[0], __half2float(h0)))) |
+                                ((uint32_t)__half_as_ushort(__float2half_rn(__fsub_rn(av[1], __half2float(h1)))) << 16);
+                }
+                const size_t o = (size_t)t * a.ld_silu + f0 + c;  // 32-byte aligned: ld_silu % 16 == 0
+                uint4* dh = reinterpret_cast<uint4*>(a.silu_hi + o);
+                uint4* dl = reinterpret_cast<uint4*>(a.silu_lo + o);
+                dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+            }
+        }
+    } else if (t0 + q * 32 < a.n) {  // warp-uniform: this warp's 32 tokens hold at least one real one
         for (int c = 0; c < kDenseBW; c += 16) {
             const int o = o0 + c;
             if (o >= a.m) break;  // warp-uniform
@@ -365,7 +404,7 @@ __global__ void __launch_bounds__(256) dense_split_kernel(const float* __restric
 constexpr int kUnpackI = 16, kUnpackC = 32;
 
 __global__ void __launch_bounds__(256) dense_unpack_kernel(const uint16_t* __restrict__ buckets, int in_dim, int cols,
-                                                           uint16_t* __restrict__ w, int ldw) {
+                                                           uint16_t* __restrict__ w, int ldw, int rpb, int pitch) {
     __shared__ __align__(16) uint16_t s_out[kUnpackC * 16][kUnpackI];  // [dense row in tile][input]
     const int i0 = blockIdx.x * kUnpackI, c0 = blockIdx.y * kUnpackC;
     for (int e = threadIdx.x; e < kUnpackC * 16 * kUnpackI; e += blockDim.x) (&s_out[0][0])[e] = 0;
@@ -384,7 +423,8 @@ __global__ void __launch_bounds__(256) dense_unpack_kernel(const uint16_t* __res
         const int o = c0 * 16 + orow;
         if (c0 + (orow >> 4) >= cols) continue;
         const int ib = i0 + half * 8;
-        uint16_t* dst = w + (size_t)o * ldw + ib;
+        const size_t drow = rpb > 0 ? (size_t)(o / rpb) * pitch + o % rpb : (size_t)o;
+        uint16_t* dst = w + drow * ldw + ib;
         if (ib + 8 <= in_dim) {
             *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&s_out[orow][half * 8]);
         } else {
@@ -448,6 +488,9 @@ int launch_gemm(const DenseProblem& p, int split, int kb_total, int kb_per, cuda
     a.ldr = p.ldr;
     a.partial = split > 1 ? p.partial : nullptr;
     a.err = p.err;
+    a.silu_hi = p.silu_out_hi;
+    a.silu_lo = p.silu_out_lo;
+    a.ld_silu = p.ld_silu;
     const dim3 grid((p.n + kDenseBT - 1) / kDenseBT, (p.m + kDenseBW - 1) / kDenseBW, split);
     IAM_CUDA_TRY(launch_ex(dense_gemm_kernel, grid, dim3(128), Tile::kSmem, s, pdl, tw, thi, tlo, a));
     return IAM_OK;
@@ -491,6 +534,11 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl) {
     int kb_per = (kb_total + split - 1) / split;
     split = (kb_total + kb_per - 1) / kb_per;  // every slice non-empty
     if (split > 1 && p.partial == nullptr) return fail(IAM_ERR_ARG, "dense_gemm: split-K needs a partial buffer");
+    if (p.silu_out_hi != nullptr) {
+        if (split != 1 || p.m % kDenseBW != 0 || p.silu_out_lo == nullptr || p.ld_silu % 16 != 0 ||
+            p.ld_silu < p.m / 2 || !aligned16(p.silu_out_hi) || !aligned16(p.silu_out_lo))
+            return fail(IAM_ERR_ARG, "dense_gemm: the SiLU epilogue needs m % 256 == 0, no K split, ld % 16 == 0");
+    }
     const int rc = launch_gemm(p, split, kb_total, kb_per, s, pdl);
     if (rc != IAM_OK || split == 1) return rc;
     const int vec = p.m % 4 == 0 && p.ldy % 4 == 0 && aligned16(p.y) && (!p.residual || (p.ldr % 4 == 0 && aligned16(p.residual)));
@@ -499,12 +547,15 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl) {
     return IAM_OK;
 }
 
-int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s) {
+int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s,
+                 int rows_per_block, int block_pitch) {
     if (buckets == nullptr || w == nullptr || in_dim <= 0 || cols <= 0 || ldw < in_dim)
         return fail(IAM_ERR_ARG, "dense_unpack: bad arguments");
     if (ldw % 8 != 0 || !aligned16(w)) return fail(IAM_ERR_ARG, "dense_unpack: ldw % 8 and 16-byte alignment");
+    if (rows_per_block < 0 || (rows_per_block > 0 && block_pitch < rows_per_block))
+        return fail(IAM_ERR_ARG, "dense_unpack: row blocks");
     const dim3 grid((in_dim + kUnpackI - 1) / kUnpackI, (cols + kUnpackC - 1) / kUnpackC);
-    dense_unpack_kernel<<<grid, 256, 0, s>>>(buckets, in_dim, cols, w, ldw);
+    dense_unpack_kernel<<<grid, 256, 0, s>>>(buckets, in_dim, cols, w, ldw, rows_per_block, block_pitch);
     IAM_CUDA_TRY(cudaGetLastError());
     return IAM_OK;
 }

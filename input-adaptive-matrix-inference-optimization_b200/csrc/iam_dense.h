@@ -35,6 +35,13 @@ struct DenseProblem {
     float* partial;         // split-K scratch: split * n * m floats (needed when split > 1)
     int split;              // K slices (1 = none); clamped to the K blocks
     unsigned* err;          // device word set when a pipeline wait gave up (may be null)
+    // SiLU epilogue (silu_out_hi != null): W's rows come in blocks of 256 = 128 gate rows then
+    // the 128 up rows of the same FFN columns; instead of y the tile writes
+    // a = up * gate / (1 + exp(-gate)) of its 128 FFN columns as fp16 hi / lo [n][ld_silu].
+    // Needs m % 256 == 0 and no K split.
+    uint16_t* silu_out_hi;
+    uint16_t* silu_out_lo;
+    int ld_silu;
 };
 
 // Splits fp32 X [n][k] (row stride ldx) into fp16 hi / lo [n][k].
@@ -46,6 +53,9 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl = false);
 // Dense fp16 matrix W'[16*c + slot][i] from the bucket layout buckets[16*in][cols]: the
 // packed word (value with its slot in the low 4 bits) lands at its original position, which
 // is the multiplicand bucketMul uses when every bucket row is selected.
-int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s);
+// rows_per_block > 0 places dense row o at (o / rows_per_block) * block_pitch + o % rows_per_block
+// (used to interleave the gate and up matrices for the SiLU epilogue).
+int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s,
+                 int rows_per_block = 0, int block_pitch = 0);
 
 }  // namespace iam

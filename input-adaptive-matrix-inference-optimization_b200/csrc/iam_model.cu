@@ -197,6 +197,8 @@ struct iam_model_s {
     int* pf_tok = nullptr;
     float *pf_h = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_gu = nullptr, *pf_part = nullptr;
     uint16_t *pf_hi = nullptr, *pf_lo = nullptr;
+    uint16_t *pf_hi2 = nullptr, *pf_lo2 = nullptr;  // SiLU(gate) * up as the down product's input
+    bool pf_silu_fused = false;  // gate|up rows interleaved in 128-row blocks, SiLU in its epilogue
     unsigned* pf_err = nullptr;
 };
 
@@ -799,18 +801,23 @@ int build_prefill(iam_model_s* m, cudaStream_t s) {
         if ((rc = dalloc(m, &D.qkv, (size_t)(qn + 2 * kvn) * d)) || (rc = dalloc(m, &D.o, (size_t)d * qn)) ||
             (rc = dalloc(m, &D.gu, (size_t)2 * f * d)) || (rc = dalloc(m, &D.down, (size_t)d * f)))
             return rc;
-        struct Part { int which; uint16_t* dst; };
-        const Part parts[NMAT] = {{MQ, D.qkv},
-                                  {MK, D.qkv + (size_t)qn * d},
-                                  {MV, D.qkv + (size_t)(qn + kvn) * d},
-                                  {MO, D.o},
-                                  {MG, D.gu},
-                                  {MU, D.gu + (size_t)f * d},
-                                  {MD, D.down}};
+        // gate|up: with ffn a multiple of 128, blocks of 128 gate rows then the 128 up rows of
+        // the same FFN columns (one 256-row product tile each: SiLU in the product's epilogue)
+        const bool fused = f % (kDenseBW / 2) == 0;
+        const int blk = fused ? kDenseBW / 2 : 0, pitch = fused ? kDenseBW : 0;
+        struct Part { int which; uint16_t* dst; int rpb, pitch; };
+        const Part parts[NMAT] = {{MQ, D.qkv, 0, 0},
+                                  {MK, D.qkv + (size_t)qn * d, 0, 0},
+                                  {MV, D.qkv + (size_t)(qn + kvn) * d, 0, 0},
+                                  {MO, D.o, 0, 0},
+                                  {MG, D.gu, blk, pitch},
+                                  {MU, D.gu + (size_t)(fused ? blk : f) * d, blk, pitch},
+                                  {MD, D.down, 0, 0}};
         for (const Part& p : parts) {
             const Matrix& mat = L.m[p.which];
-            if ((rc = dense_unpack(mat.buckets, mat.in_dim, mat.cols, p.dst, mat.in_dim, s))) return rc;
+            if ((rc = dense_unpack(mat.buckets, mat.in_dim, mat.cols, p.dst, mat.in_dim, s, p.rpb, p.pitch))) return rc;
         }
+        m->pf_silu_fused = fused;
     }
     int cap = 256;
     if (const char* v = getenv("IAM_PREFILL_CHUNK")) cap = std::max(1, atoi(v));
@@ -819,7 +826,8 @@ int build_prefill(iam_model_s* m, cudaStream_t s) {
     if ((rc = dalloc(m, &m->pf_tok, (size_t)cap)) || (rc = dalloc(m, &m->pf_h, (size_t)cap * d)) ||
         (rc = dalloc(m, &m->pf_qkv, (size_t)cap * (qn + 2 * kvn))) || (rc = dalloc(m, &m->pf_att, (size_t)cap * qn)) ||
         (rc = dalloc(m, &m->pf_gu, (size_t)cap * 2 * f)) || (rc = dalloc(m, &m->pf_hi, (size_t)cap * wide)) ||
-        (rc = dalloc(m, &m->pf_lo, (size_t)cap * wide)) ||
+        (rc = dalloc(m, &m->pf_lo, (size_t)cap * wide)) || (rc = dalloc(m, &m->pf_hi2, (size_t)cap * f)) ||
+        (rc = dalloc(m, &m->pf_lo2, (size_t)cap * f)) ||
         (rc = dalloc(m, &m->pf_part, dense_partial_floats(m->sm_count))) || (rc = dalloc(m, &m->pf_err, 1)))
         return rc;
     IAM_CUDA_TRY(cudaMemsetAsync(m->pf_err, 0, sizeof(unsigned), s));
@@ -828,16 +836,16 @@ int build_prefill(iam_model_s* m, cudaStream_t s) {
     return IAM_OK;
 }
 
-// y[t][:] (+)= W x[t] with x given as the hi / lo halves in m->pf_hi / m->pf_lo [n][k].
+// y[t][:] (+)= W x[t] with x given as the hi / lo halves [n][k] (default m->pf_hi / m->pf_lo).
 int prefill_gemm(iam_model_s* m, const uint16_t* w, int out, int k, int n, float* y, const float* residual,
-                 cudaStream_t s) {
+                 cudaStream_t s, const uint16_t* x_hi = nullptr, const uint16_t* x_lo = nullptr) {
     DenseProblem p{};
     p.w = w;
     p.m = out;
     p.k = k;
     p.ldw = k;
-    p.x_hi = m->pf_hi;
-    p.x_lo = m->pf_lo;
+    p.x_hi = x_hi ? x_hi : m->pf_hi;
+    p.x_lo = x_lo ? x_lo : m->pf_lo;
     p.n = n;
     p.y = y;
     p.ldy = out;
@@ -872,11 +880,30 @@ int prefill_chunk(iam_model_s* m, const int* tokens_host, int n, int pos0, cudaS
                                     m->pf_att, qn, s)) ||
             (rc = dense_split(m->pf_att, n, qn, qn, m->pf_hi, m->pf_lo, s)) ||
             (rc = prefill_gemm(m, D.o, d, qn, n, m->pf_h, m->pf_h, s)) ||
-            (rc = prefill_rms_split(m->pf_h, n, d, L.ffn_norm, c.norm_eps, m->pf_hi, m->pf_lo, s)) ||
-            (rc = prefill_gemm(m, D.gu, 2 * f, d, n, m->pf_gu, nullptr, s)) ||
-            (rc = prefill_silu_split(m->pf_gu, n, f, m->pf_hi, m->pf_lo, s)) ||
-            (rc = prefill_gemm(m, D.down, d, f, n, m->pf_h, m->pf_h, s)))
+            (rc = prefill_rms_split(m->pf_h, n, d, L.ffn_norm, c.norm_eps, m->pf_hi, m->pf_lo, s)))
             return rc;
+        if (m->pf_silu_fused) {  // SiLU(gate) * up straight from the gate|up product's epilogue
+            DenseProblem p{};
+            p.w = D.gu;
+            p.m = 2 * f;
+            p.k = d;
+            p.ldw = d;
+            p.x_hi = m->pf_hi;
+            p.x_lo = m->pf_lo;
+            p.n = n;
+            p.y = m->pf_gu;  // unused by this epilogue
+            p.ldy = 2 * f;
+            p.split = 1;
+            p.err = m->pf_err;
+            p.silu_out_hi = m->pf_hi2;
+            p.silu_out_lo = m->pf_lo2;
+            p.ld_silu = f;
+            if ((rc = dense_gemm(p, s))) return rc;
+        } else if ((rc = prefill_gemm(m, D.gu, 2 * f, d, n, m->pf_gu, nullptr, s)) ||
+                   (rc = prefill_silu_split(m->pf_gu, n, f, m->pf_hi2, m->pf_lo2, s))) {
+            return rc;
+        }
+        if ((rc = prefill_gemm(m, D.down, d, f, n, m->pf_h, m->pf_h, s, m->pf_hi2, m->pf_lo2))) return rc;
     }
     return IAM_OK;
 }

@@ -139,87 +139,137 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
     }
 }
 
-template <int VD>
-IAM_DEV void load_halves(const uint16_t* p, float (&f)[VD]) {
-    if constexpr (VD == 8) {
-        const uint4 u = *reinterpret_cast<const uint4*>(p);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            f[2 * i] = h2f(w[i] & 0xffffu);
-            f[2 * i + 1] = h2f(w[i] >> 16);
-        }
-    } else if constexpr (VD == 4) {
-        const uint2 u = *reinterpret_cast<const uint2*>(p);
-        f[0] = h2f(u.x & 0xffffu);
-        f[1] = h2f(u.x >> 16);
-        f[2] = h2f(u.y & 0xffffu);
-        f[3] = h2f(u.y >> 16);
-    } else if constexpr (VD == 2) {
-        const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
-        f[0] = h2f(u & 0xffffu);
-        f[1] = h2f(u >> 16);
-    } else {
-        f[0] = h2f(*p);
-    }
-}
+constexpr int kAttnQ = 4;      // query tokens per CTA
+constexpr int kAttnKT = 32;    // keys per shared-memory tile (one per lane in the score pass)
 
-constexpr int kKeysPerStep = 4;  // keys whose dot products reduce together (shuffle latency overlap)
-
-// One CTA per (kv head, token), one warp per query head of the group; lane owns VD dims.
-template <int VD>
-__global__ void prefill_attention_kernel(const float* __restrict__ qkv, int ldq, int n_heads, int n_kv,
-                                         const uint16_t* __restrict__ k_cache, const uint16_t* __restrict__ v_cache,
-                                         int max_ctx, int pos0, float* __restrict__ out, int ldo) {
+// One CTA per (kv head, block of kAttnQ query tokens): rows r = (token, query head of the
+// group), RW rows per warp.  Per tile of 32 keys: the CTA stages K (rows padded to HD/2 + 1
+// words: lane-per-key reads hit distinct banks) and V in shared memory; lane j scores key j
+// against the warp's rows (no reductions inside the dot products); one max and one sum per
+// row and tile update the running softmax; then each lane accumulates its VD dims of P V.
+template <int VD, int RW>
+__global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __restrict__ qkv, int ldq, int n,
+                                                                int n_heads, int n_kv,
+                                                                const uint16_t* __restrict__ k_cache,
+                                                                const uint16_t* __restrict__ v_cache, int max_ctx,
+                                                                int pos0, float* __restrict__ out, int ldo) {
     constexpr int HD = 32 * VD;
-    const int kvh = blockIdx.x, t = blockIdx.y;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = kvh * (n_heads / n_kv) + w;
-    const int last = pos0 + t;
-    float q[VD];
-    const float* qp = qkv + (size_t)t * ldq + (size_t)h * HD + lane * VD;
+    constexpr int KW = HD / 2 + 1;  // padded K row in 32-bit words
+    extern __shared__ float sm[];
+    const int gq = n_heads / n_kv;
+    const int rows = kAttnQ * gq;
+    const int nwarps = blockDim.x >> 5;
+    float* s_q = sm;                                       // [rows][HD]
+    uint32_t* s_k = reinterpret_cast<uint32_t*>(s_q + rows * HD);  // [KT][KW] half2 words
+    uint32_t* s_v = s_k + kAttnKT * KW;                    // [KT][HD / 2] half2 words
+    float* s_p = reinterpret_cast<float*>(s_v + kAttnKT * HD / 2);  // [warps][RW][KT]
+
+    const int kvh = blockIdx.x, tb = blockIdx.y * kAttnQ;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nq = min(kAttnQ, n - tb);
+    const int last_key = pos0 + tb + nq - 1;  // the block's last query sees keys [0, last_key]
+
+    for (int e = threadIdx.x; e < rows * HD; e += blockDim.x) {
+        const int r = e / HD, d = e % HD, ti = r / gq, g = r % gq;
+        s_q[e] = ti < nq ? qkv[(size_t)(tb + ti) * ldq + (size_t)(kvh * gq + g) * HD + d] : 0.0f;
+    }
+    float mx[RW], l[RW], acc[RW][VD];
+    int lastr[RW];
 #pragma unroll
-    for (int i = 0; i < VD; ++i) q[i] = qp[i];
-    const uint16_t* kb = k_cache + (size_t)kvh * max_ctx * HD + lane * VD;
-    const uint16_t* vb = v_cache + (size_t)kvh * max_ctx * HD + lane * VD;
+    for (int a = 0; a < RW; ++a) {
+        const int r = warp * RW + a;
+        mx[a] = -INFINITY;
+        l[a] = 0.0f;
+        lastr[a] = pos0 + tb + min(r / gq, nq - 1);
+#pragma unroll
+        for (int i = 0; i < VD; ++i) acc[a][i] = 0.0f;
+    }
     const float inv_scale = sqrtf((float)HD);  // score = dot / sqrt(head_dim), aux.cl:537
-    float mx = -INFINITY, l = 0.0f, acc[VD];
-#pragma unroll
-    for (int i = 0; i < VD; ++i) acc[i] = 0.0f;
-    for (int j0 = 0; j0 <= last; j0 += kKeysPerStep) {
-        float kf[kKeysPerStep][VD], vf[kKeysPerStep][VD], s[kKeysPerStep];
-#pragma unroll
-        for (int u = 0; u < kKeysPerStep; ++u) {
-            const int j = min(j0 + u, last);  // keys past the last are loaded clamped and skipped
-            load_halves<VD>(kb + (size_t)j * HD, kf[u]);
-            load_halves<VD>(vb + (size_t)j * HD, vf[u]);
+    const uint16_t* kb = k_cache + (size_t)kvh * max_ctx * HD;
+    const uint16_t* vb = v_cache + (size_t)kvh * max_ctx * HD;
+    float* pw = s_p + warp * RW * kAttnKT;
+
+    for (int k0 = 0; k0 <= last_key; k0 += kAttnKT) {
+        __syncthreads();  // the previous tile is consumed (and s_q written, on the first pass)
+        // stage K and V of keys [k0, k0 + 32) (rows past last_key read as zeros)
+        for (int e = threadIdx.x; e < kAttnKT * HD / 8; e += blockDim.x) {
+            const int j = e / (HD / 8), c = e % (HD / 8);
+            uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
+            if (k0 + j <= last_key) {
+                kv4 = *reinterpret_cast<const uint4*>(kb + (size_t)(k0 + j) * HD + c * 8);
+                vv4 = *reinterpret_cast<const uint4*>(vb + (size_t)(k0 + j) * HD + c * 8);
+            }
+            uint32_t* kr = s_k + j * KW + c * 4;
+            kr[0] = kv4.x;
+            kr[1] = kv4.y;
+            kr[2] = kv4.z;
+            kr[3] = kv4.w;
+            *reinterpret_cast<uint4*>(s_v + j * (HD / 2) + c * 4) = vv4;
         }
+        __syncthreads();
+        if (warp * RW >= rows) continue;  // warps past the rows only help staging
+        // scores: lane = key
+        float sc[RW];
 #pragma unroll
-        for (int u = 0; u < kKeysPerStep; ++u) {
-            s[u] = 0.0f;
+        for (int a = 0; a < RW; ++a) sc[a] = 0.0f;
+        const uint32_t* kr = s_k + lane * KW;
+        for (int w2 = 0; w2 < HD / 2; ++w2) {
+            const uint32_t kw = kr[w2];
+            const float k0f = h2f(kw & 0xffffu), k1f = h2f(kw >> 16);
 #pragma unroll
-            for (int i = 0; i < VD; ++i) s[u] = fmaf(q[i], kf[u][i], s[u]);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int u = 0; u < kKeysPerStep; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], off);
-#pragma unroll
-        for (int u = 0; u < kKeysPerStep; ++u) {
-            if (j0 + u <= last) {  // uniform over the warp
-                const float sc = s[u] / inv_scale;
-                const float mn = fmaxf(mx, sc);
-                const float c = expf(mx - mn), pe = expf(sc - mn);
-                l = l * c + pe;
-#pragma unroll
-                for (int i = 0; i < VD; ++i) acc[i] = acc[i] * c + pe * vf[u][i];
-                mx = mn;
+            for (int a = 0; a < RW; ++a) {
+                const float2 qv = *reinterpret_cast<const float2*>(s_q + (warp * RW + a) * HD + 2 * w2);
+                sc[a] = fmaf(qv.x, k0f, sc[a]);
+                sc[a] = fmaf(qv.y, k1f, sc[a]);
             }
         }
-    }
-    float* op = out + (size_t)t * ldo + (size_t)h * HD + lane * VD;
+        const int key = k0 + lane;
 #pragma unroll
-    for (int i = 0; i < VD; ++i) op[i] = acc[i] / l;
+        for (int a = 0; a < RW; ++a) {
+            const float sv = key <= lastr[a] ? sc[a] / inv_scale : -INFINITY;
+            float tm = sv;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+            const float mn = fmaxf(mx[a], tm);  // finite: key 0 is in the first tile of every row
+            const float c = expf(mx[a] - mn);
+            const float pj = expf(sv - mn);
+            float ps = pj;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l[a] = l[a] * c + ps;
+            mx[a] = mn;
+#pragma unroll
+            for (int i = 0; i < VD; ++i) acc[a][i] *= c;
+            pw[a * kAttnKT + lane] = pj;
+        }
+        __syncwarp();
+        const int nk = min(kAttnKT, last_key - k0 + 1);
+        for (int j = 0; j < nk; ++j) {
+            float vf[VD];
+            const uint32_t* vr = s_v + j * (HD / 2) + lane * (VD / 2);
+#pragma unroll
+            for (int i = 0; i < VD / 2; ++i) {
+                vf[2 * i] = h2f(vr[i] & 0xffffu);
+                vf[2 * i + 1] = h2f(vr[i] >> 16);
+            }
+#pragma unroll
+            for (int a = 0; a < RW; ++a) {
+                const float pj = pw[a * kAttnKT + j];
+#pragma unroll
+                for (int i = 0; i < VD; ++i) acc[a][i] = fmaf(pj, vf[i], acc[a][i]);
+            }
+        }
+        __syncwarp();
+    }
+    if (warp * RW >= rows) return;
+#pragma unroll
+    for (int a = 0; a < RW; ++a) {
+        const int r = warp * RW + a, ti = r / gq, g = r % gq;
+        if (ti >= nq) continue;
+        float* op = out + (size_t)(tb + ti) * ldo + (size_t)(kvh * gq + g) * HD + lane * VD;
+#pragma unroll
+        for (int i = 0; i < VD; ++i) op[i] = acc[a][i] / l[a];
+    }
 }
 
 // Grid (column blocks of 4 x 256, tokens); ffn % 4 == 0.
@@ -235,6 +285,23 @@ __global__ void __launch_bounds__(256) silu_split_kernel(const float* __restrict
                                  __fdiv_rn(__fmul_rn(u.z, g.z), __fadd_rn(1.0f, expf(-g.z))),
                                  __fdiv_rn(__fmul_rn(u.w, g.w), __fadd_rn(1.0f, expf(-g.w))));
     split_store4(a, hi, lo, (size_t)t * ffn + i);
+}
+
+template <int VD, int RW>
+int launch_attention_t(const float* qkv, int ldq, int n, int n_heads, int n_kv, const uint16_t* k_cache,
+                       const uint16_t* v_cache, int max_ctx, int pos0, float* out, int ldo, cudaStream_t s) {
+    constexpr int HD = 32 * VD;
+    const int rows = kAttnQ * (n_heads / n_kv);
+    const int warps = std::max(1, (rows + RW - 1) / RW);
+    const size_t smem = (size_t)rows * HD * 4 + (size_t)kAttnKT * (HD / 2 + 1) * 4 + (size_t)kAttnKT * HD * 2 +
+                        (size_t)warps * RW * kAttnKT * 4;
+    if (warps > 8 || smem > 200 * 1024) return fail(IAM_ERR_UNSUPPORTED, "prefill attention: query group too large");
+    auto kern = prefill_attention_kernel<VD, RW>;
+    IAM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<dim3(n_kv, (n + kAttnQ - 1) / kAttnQ), 32 * warps, smem, s>>>(qkv, ldq, n, n_heads, n_kv, k_cache, v_cache,
+                                                                         max_ctx, pos0, out, ldo);
+    IAM_CUDA_TRY(cudaGetLastError());
+    return IAM_OK;
 }
 
 }  // namespace
@@ -264,21 +331,25 @@ int prefill_rope_kv(float* qkv, int n, int ld, int n_heads, int n_kv, int hd, co
     return IAM_OK;
 }
 
+
 int prefill_attention(const float* qkv, int ldq, int n, int n_heads, int n_kv, int hd, const uint16_t* k_cache,
                       const uint16_t* v_cache, int max_ctx, int pos0, float* out, int ldo, cudaStream_t s) {
     if (n <= 0) return IAM_OK;
-    const int gq = n_heads / n_kv;
-    if (n_heads % n_kv != 0 || gq > 32) return fail(IAM_ERR_UNSUPPORTED, "prefill attention: query group size");
-    const dim3 grid(n_kv, n), block(32 * gq);
+    if (n_heads % n_kv != 0) return fail(IAM_ERR_UNSUPPORTED, "prefill attention: n_heads % n_kv_heads");
+    if ((n + kAttnQ - 1) / kAttnQ > 65535) return fail(IAM_ERR_UNSUPPORTED, "prefill attention: tokens");
+    // rows per warp: 8 warps when the block's rows fill them, else one row per warp
+    const int rows = kAttnQ * (n_heads / n_kv);
+    const bool two = rows % 16 == 0 && rows / 2 <= 8 * 2;
     switch (hd) {
-        case 32: prefill_attention_kernel<1><<<grid, block, 0, s>>>(qkv, ldq, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo); break;
-        case 64: prefill_attention_kernel<2><<<grid, block, 0, s>>>(qkv, ldq, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo); break;
-        case 128: prefill_attention_kernel<4><<<grid, block, 0, s>>>(qkv, ldq, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo); break;
-        case 256: prefill_attention_kernel<8><<<grid, block, 0, s>>>(qkv, ldq, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo); break;
-        default: return fail(IAM_ERR_UNSUPPORTED, "prefill attention: head_dim must be 32, 64, 128 or 256");
+        case 64:
+            return two ? launch_attention_t<2, 2>(qkv, ldq, n, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo, s)
+                       : launch_attention_t<2, 1>(qkv, ldq, n, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo, s);
+        case 128:
+            return two ? launch_attention_t<4, 2>(qkv, ldq, n, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo, s)
+                       : launch_attention_t<4, 1>(qkv, ldq, n, n_heads, n_kv, k_cache, v_cache, max_ctx, pos0, out, ldo, s);
+        default:
+            return fail(IAM_ERR_UNSUPPORTED, "prefill attention: head_dim must be 64 or 128");
     }
-    IAM_CUDA_TRY(cudaGetLastError());
-    return IAM_OK;
 }
 
 int prefill_silu_split(const float* gu, int n, int ffn, uint16_t* hi, uint16_t* lo, cudaStream_t s) {

@@ -137,3 +137,20 @@ def test_prefill_mistral_layer(iam, ora, torch_mod):
     assert nxt == best
     kv_close(iam, m, om, 1, cfg.n_kv_heads, cfg.max_ctx, cfg.head_dim, len(prompt))
     m.close()
+
+
+def test_prefill_without_the_silu_epilogue(iam, ora, torch_mod):
+    """ffn_dim 320 is not a multiple of 128: gate and up stay separate matrices and SiLU runs as
+    its own pass (the other configs take the fused gate|up epilogue)."""
+    torch = torch_mod
+    cfg = iam.ModelConfig.make(**dict(SMALL, ffn_dim=320))
+    m = iam.Model.random(cfg, seed=11)
+    om = ora.OracleModel(cfg.as_dict(), m.export_weights())
+    prompt = np.random.default_rng(5).integers(3, cfg.vocab, 18).tolist()
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+    nxt = m.prefill(prompt, 0, logits)
+    for pos, tok in enumerate(prompt):
+        best, ref = om.forward_dense(tok, pos)
+    assert rel_err(logits.cpu().numpy(), ref) < LOGIT_TOL
+    assert nxt == best
+    m.close()
