@@ -436,14 +436,13 @@ int env_int(const char* name, int dflt) {
 
 template <int VEC, int XM>
 cudaError_t set_attrs() {
-    static std::once_flag once;
-    static cudaError_t err = cudaSuccess;
-    std::call_once(once, [] {
+    static std::atomic<unsigned long long> done{0};
+    return once_per_device(done, [] {
         auto kern = bm_fused_kernel<VEC, XM>;
-        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (err == cudaSuccess) err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        return err;
     });
-    return err;
 }
 
 template <int VEC, int XM>

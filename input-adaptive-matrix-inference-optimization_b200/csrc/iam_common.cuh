@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/iam_b200.h"
@@ -38,6 +39,21 @@ IAM_DEV float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigne
 // 1e5 * |x * s| with both multiplies rounded separately (bucketMul.cl:110, :378).
 IAM_DEV float importance(float x, float s) {
     return __fmul_rn(kCutoffScale, fabsf(__fmul_rn(x, s)));
+}
+
+// Host-side: runs `set` (e.g. cudaFuncSetAttribute calls) once for the current device; CUDA
+// function attributes belong to a device's context, so a process that drives several devices
+// sets them on each.  Concurrent first calls may both run `set` (idempotent).
+template <class F>
+cudaError_t once_per_device(std::atomic<unsigned long long>& done, F&& set) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
 }
 
 // Host-side: per-thread last error message.

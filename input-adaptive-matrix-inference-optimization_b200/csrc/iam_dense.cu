@@ -464,13 +464,10 @@ int make_map(CUtensorMap* map, const void* base, int inner, int rows, int ld, in
 }
 
 int launch_gemm(const DenseProblem& p, int split, int kb_total, int kb_per, cudaStream_t s, bool pdl) {
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(dense_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)Tile::kSmem);
-    });
-    IAM_CUDA_TRY(attr_err);
+    static std::atomic<unsigned long long> attrs_set{0};
+    IAM_CUDA_TRY(once_per_device(attrs_set, [] {
+        return cudaFuncSetAttribute(dense_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::kSmem);
+    }));
     CUtensorMap tw, thi, tlo;
     int rc = make_map(&tw, p.w, p.k, p.m, p.ldw, kDenseBW);
     if (rc == IAM_OK) rc = make_map(&thi, p.x_hi, p.k, p.n, p.k, kDenseBT);
