@@ -158,7 +158,6 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __r
     extern __shared__ float sm[];
     const int gq = n_heads / n_kv;
     const int rows = kAttnQ * gq;
-    const int nwarps = blockDim.x >> 5;
     float* s_q = sm;                                       // [rows][HD]
     uint32_t* s_k = reinterpret_cast<uint32_t*>(s_q + rows * HD);  // [KT][KW] half2 words
     uint32_t* s_v = s_k + kAttnKT * KW;                    // [KT][HD / 2] half2 words
