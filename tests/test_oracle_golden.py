@@ -98,6 +98,20 @@ def test_oracle_all_rows_close_to_dense(ora):
     assert rel_err(out, dense) < 2e-2
 
 
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_oracle_all_rows_equal_the_packed_dense_matrix(ora, weights_mod, case):
+    """The dense path's matrix: bucketMul over every bucket row (bucketMul.cl:392-497) is the
+    fp64 product with W' = (bits(W) & 0xFFF0) | (row & 15) up to fp32 summation, on the
+    reference's own bucket fixtures and every fixture input."""
+    g = golden(case)
+    R = g["buckets"].shape[0]
+    wp = weights_mod.dense_packed(g["W"].view(np.float16))
+    for x in g["x"]:
+        out = ora.bucket_mul(g["buckets"], x, np.arange(R, dtype=np.int32))
+        ref = ora.dense_gemv(wp, x)
+        assert rel_err(out, ref) < 1e-5, case
+
+
 def test_oracle_fp16_roundtrip(ora):
     L = ora.lib()
     for v in [0.0, -0.0, 1.0, -2.5, 65504.0, 1e-7, 6.1e-5, 3.14159, 70000.0]:
