@@ -693,6 +693,25 @@ def run_reference(args, rank, world):
                              "sample": cb["sample"]},
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
+    if args.workload == "prefill":  # the reference's way: the prompt through the dense step, token by token
+        import torch
+        iam = load_pkg()
+        cfg = mistral_cfg(iam, PROMPT_LEN + 8, args.layers)
+        model = iam.Model.random(cfg, seed=0)
+        cb = cpu_baseline_prefill(model, cfg, budget_s=args.cpu_seconds, tokens=max(1, min(args.steps, 4)))
+        model.close()
+        return {
+            "metric": METRIC, "value": cb["value"], "unit": "prompt tokens/s", "n_gpus": world,
+            "steps": max(1, min(args.steps, 4)), "warmup": args.warmup, "ms_per_step": round(1e3 / cb["value"], 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "prefill: the config-4 prompt through the CPU restatement (oracle) of the "
+                                   "reference's step with every bucket row selected, one token at a time",
+                       "model": "Mistral-7B (random init)", "prompt_tokens": PROMPT_LEN, "global_batch": 1},
+            "cpu_baseline": {"value": cb["value"], "unit": cb["unit"], "cores": cb["cores"], "kind": "port",
+                             "sample": cb["sample"]},
+            "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
     import torch
     iam = load_pkg()
     dev = torch.device("cuda:0") if torch.cuda.is_available() else None
