@@ -141,10 +141,10 @@ def test_prefill_mistral_layers(iam, ora, torch_mod):
 
 
 def test_prefill_without_the_silu_epilogue(iam, ora, torch_mod):
-    """ffn_dim 320 is not a multiple of 128: gate and up stay separate matrices and SiLU runs as
+    """ffn_dim 144 is not a multiple of 128: gate and up stay separate matrices and SiLU runs as
     its own pass (the other configs take the fused gate|up epilogue)."""
     torch = torch_mod
-    cfg = iam.ModelConfig.make(**dict(SMALL, ffn_dim=320))
+    cfg = iam.ModelConfig.make(**dict(SMALL, ffn_dim=144))
     m = iam.Model.random(cfg, seed=11)
     om = ora.OracleModel(cfg.as_dict(), m.export_weights())
     prompt = np.random.default_rng(5).integers(3, cfg.vocab, 18).tolist()
