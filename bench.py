@@ -6,7 +6,7 @@
 
 Prints ONE JSON line (rank 0).
 
-`decode` (default): the 32-layer Mistral-7B shape (d 4096, 32/8 heads,
+`decode` (default; the 32-layer decode workload): the 32-layer Mistral-7B shape (d 4096, 32/8 heads,
 head_dim 128, ffn 14336, vocab 32000, tied embeddings) with random-init N(0, 0.02) fp16
 weights bucketized on the GPU, RMSNorm gains 1.0, a 128-token prompt drawn uniformly from
 [3, 32000) with seed 1, then greedy decoding at `--effort`.  One step = one generated token
@@ -18,7 +18,7 @@ fused bucketMul kernel's effective HBM bandwidth: its algorithmic bytes (2|S|C +
 2*4096 + 4M per bucketMul, |S| reported by the kernel) over its CUDA-event time inside the
 captured step.  Weights (13.9 GB) exceed the 126 MB L2 by two orders of magnitude.
 
-`bucketmul`: one step = the 7 bucketMuls of one Mistral layer on
+`bucketmul` (the Mistral FFN and attention shapes): one step = the 7 bucketMuls of one Mistral layer on
 alternating weight sets; value = effective GB/s.
 
 `prefill`: one step = the config-4 prompt (128 tokens) ingested in one batched pass on the dense

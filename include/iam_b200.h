@@ -125,8 +125,11 @@ int iam_bucketmul_trace(iam_bucketmul_t h, long long* trace_dev, int capacity);
  * iam_bucketmul_full minus the handle; its scratch is a ~1 MiB __device__ array built into
  * the library, held by every GPU that loads it until exit.
  * Limits: bucket_cols <= 1024 (out_dim <= 16384), else IAM_ERR_ARG.
- * The first call on a device looks up that array's device address (cudaGetSymbolAddress),
- * so make the first call on each device before any stream capture.
+ * Every call made outside a stream capture looks up that array's device address on the
+ * current device (cudaGetSymbolAddress, which allocates nothing) and remembers it; a call made
+ * while its stream is being captured uses the remembered address, so make the first call on
+ * each device before any capture (a captured first call returns IAM_ERR_ARG).  After a
+ * cudaDeviceReset the next call outside capture picks up the re-created array's address.
  * All calls share the one array: calls that overlap on the GPU (different streams, or
  * threads without ordering) race and corrupt each other's results; serialise them. */
 int iam_bucketmul_full_noalloc(const float* x_dev, const uint16_t* stats_dev, int stats_stride,
@@ -234,9 +237,21 @@ int iam_model_destroy(iam_model_t m);
  * Single-GPU models only (IAM_ERR_UNSUPPORTED for a tensor-parallel rank). */
 int iam_model_save(iam_model_t m, const char* weights_dir);
 /* Synchronises the device and reports IAM_ERR_TIMEOUT when a tensor-parallel exchange of an
- * earlier step gave up waiting for a peer (its outputs are then invalid); IAM_OK otherwise.
+ * earlier step gave up waiting for a peer (its outputs are then invalid), IAM_ERR_ARG when a
+ * decode step found its device position at or past max_ctx (the entry points refuse such
+ * calls before launching; the kernels clamp to the last slot and flag it); IAM_OK otherwise.
  * (No counterpart in the reference: failure detection of the multi-GPU path.) */
 int iam_model_status(iam_model_t m);
+/* Self-test of the bounded device-side wait of the one-shot tensor-parallel exchanges, on ONE
+ * GPU and with no peer process (no counterpart in the reference): builds a two-rank exchange
+ * window on `device` whose second rank is a plain local buffer that never sends anything,
+ * then runs the all-reduce of n floats twice with at most spin_limit polls per element.  The
+ * first call's waits run out (the error word is set); the second returns without waiting.
+ * *err_out (may be NULL) receives the error word, *first_ms / *second_ms (may be NULL) each
+ * call's device time.  Returns IAM_ERR_TIMEOUT when the wait gave up as designed (what
+ * iam_model_status reports for a model whose exchange timed out), IAM_OK if it did not. */
+int iam_tp_wait_selftest(int device, int n, long long spin_limit, unsigned* err_out, float* first_ms,
+                         float* second_ms);
 /* MistralModel::reset_caches (model.hpp:233-237): zero the KV cache and the position. */
 int iam_model_reset(iam_model_t m, void* stream);
 /* MistralModel::forward (model.hpp:152-231): one decode step of `token` at `pos`; logits_dev
@@ -249,7 +264,9 @@ int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* lo
  * (test_generation.cpp:202-213); iam_model_forward does the same, at the chosen effort.
  * logits_dev (vocab floats, may be NULL) receives the last token's logits; *next_token (may be
  * NULL; the call then synchronises the stream) its greedy argmax.  The first call builds dense
- * fp16 copies of the weights (as large as the bucket weights) and prefill scratch.
+ * fp16 copies of the weights (as large as the bucket weights) and prefill scratch.  The device
+ * position becomes start_pos + n_tokens, so iam_model_generate with first_token < 0 continues
+ * after the prompt from its greedy token.
  * Single-GPU models only (IAM_ERR_UNSUPPORTED for a tensor-parallel rank). */
 int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int start_pos, float* logits_dev,
                       int* next_token, void* stream);
@@ -257,7 +274,9 @@ int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int s
  * host round trips): step 0 decodes first_token at start_pos, every later step decodes the
  * previous step's argmax; the n_tokens generated ids land in tokens_dev.  Steps after the
  * first replay one captured CUDA graph.  first_token < 0 continues from the device position
- * and the last argmax (start_pos is then ignored), replaying the graph for every step. */
+ * and the last argmax (start_pos is then ignored), replaying the graph for every step.
+ * IAM_ERR_ARG, before anything is launched, when a step would decode at max_ctx or beyond
+ * (the library tracks the position every entry point leaves on the device). */
 int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_tokens, float effort,
                        int* tokens_dev, void* stream);
 /* Diagnostics: decodes `steps` greedy tokens (continuing from the device position and the

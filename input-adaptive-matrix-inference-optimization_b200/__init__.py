@@ -263,6 +263,7 @@ _SIGNATURES.update({
     "iam_model_save": [_vp, ctypes.c_char_p],
     "iam_model_selected_rows_by_matrix": [_vp, _vp, _i32],
     "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
+    "iam_tp_wait_selftest": [_i32, _i32, _i64, _vp, _vp, _vp],
     "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
     "iam_model_load_tp": [_vp, ctypes.c_char_p, _vp, _i32, _i32, _i32, _vp],
 })
@@ -285,6 +286,14 @@ def tp_shard_info(cfg, rank, world):
     res = {name: tuple(out[4 * i:4 * i + 4]) for i, name in enumerate(MATRIX_NAMES)}
     res["vocab"] = (out[4 * len(MATRIX_NAMES)], out[4 * len(MATRIX_NAMES) + 1])
     return res
+
+
+def tp_wait_selftest(n=256, spin_limit=4096, device=0):
+    """iam_tp_wait_selftest: -> (status code, error word, first call ms, second call ms)."""
+    err, t1, t2 = ctypes.c_uint(), ctypes.c_float(), ctypes.c_float()
+    rc = load_library().iam_tp_wait_selftest(device, n, spin_limit, ctypes.byref(err), ctypes.byref(t1),
+                                             ctypes.byref(t2))
+    return rc, err.value, t1.value, t2.value
 
 
 def _tp_args(tp):

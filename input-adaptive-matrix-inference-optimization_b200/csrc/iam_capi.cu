@@ -363,20 +363,29 @@ constexpr size_t kNoAllocFloats = kNoAllocPartials + kNoAllocCtrSlots + kNoAlloc
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
 
-// Device address of g_noalloc_scratch on the current device (set up once per device; the
-// host-side name is only a stand-in for the symbol and must never reach a kernel).
-int noalloc_scratch(float** out) {
+// Device address of g_noalloc_scratch on the current device (the host-side name is only a
+// stand-in for the symbol and must never reach a kernel).  Every call made outside a stream
+// capture looks the address up again (cudaGetSymbolAddress, no allocation) and remembers it
+// for the device, so a context torn down and re-created (cudaDeviceReset) gets the new
+// module's address; a call made while `stream` is being captured uses the remembered one,
+// which an earlier call outside capture on the same device must have set.
+int noalloc_scratch(cudaStream_t stream, float** out) {
     static std::mutex mu;
     static float* addr[256] = {};
     int dev = 0;
     IAM_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 256) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full_noalloc: device index >= 256");
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    IAM_CUDA_TRY(cudaStreamIsCapturing(stream, &cap));
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    if (cap == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return cuda_fail(e, "iam_bucketmul_full_noalloc: cudaGetSymbolAddress");
         addr[dev] = static_cast<float*>(p);
+    } else if (!addr[dev]) {
+        return fail(IAM_ERR_ARG,
+                    "iam_bucketmul_full_noalloc: the first call on a device must come before any stream capture");
     }
     *out = addr[dev];
     return IAM_OK;
@@ -400,7 +409,7 @@ extern "C" int iam_bucketmul_full_noalloc(const float* x_dev, const uint16_t* st
         return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: stats_stride must be 1 or 4");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_bucketmul_full_noalloc: effort must be in (0, 1]");
     float* scratch = nullptr;
-    int rc = noalloc_scratch(&scratch);
+    int rc = noalloc_scratch((cudaStream_t)stream, &scratch);
     if (rc) return rc;
     const int G = bm_default_cluster();
     BMBatch b;

@@ -220,6 +220,7 @@ __global__ void __launch_bounds__(128, 1)
 
     if (warp == 0 && lane == 0) {
         // producer: stage i of this slice into ring slot i % kStages once its MMAs are done
+        int issued = 0;
         for (int i = 0; i < nkb; ++i) {
             const int s = i % Tile::kStages;
             const uint32_t ph = (uint32_t)(i / Tile::kStages) & 1u;
@@ -230,6 +231,15 @@ __global__ void __launch_bounds__(128, 1)
             tma_load_2d(st, &thi, kx, t0, &full_bar[s]);
             if (a.has_lo) tma_load_2d(st + Tile::kA, &tlo, kx, t0, &full_bar[s]);
             tma_load_2d(st + 2 * Tile::kA, &tw, kx, o0, &full_bar[s]);
+            issued = i + 1;
+        }
+        // drain: no bulk copy of this CTA may still be writing shared memory when it exits.
+        // The last stage issued into each ring slot completes its full barrier when its bytes
+        // have landed (at once on the normal path, where the MMA warp consumed every stage;
+        // after a failed wait of the MMA warp this is what keeps the exit safe).  Bounded.
+        for (int s = 0; s < Tile::kStages && s < issued; ++s) {
+            const int last = s + Tile::kStages * ((issued - 1 - s) / Tile::kStages);
+            mbar_wait(&full_bar[s], (uint32_t)(last / Tile::kStages) & 1u, a.err);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: 4 K-steps of 16 per stage; hi products into columns [0, 256), lo into [256, 512)

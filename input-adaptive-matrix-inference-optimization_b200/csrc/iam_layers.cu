@@ -111,7 +111,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
     pdl_wait();
     const int kvh = blockIdx.x / p.n_split, s = blockIdx.x % p.n_split;
     const int tid = threadIdx.x, hw = tid >> 4, hl = tid & 15;
-    const int pos = *p.pos_dev;
+    int pos = *p.pos_dev;
+    if (pos >= p.max_ctx) {  // a step past the cache (the host refuses these): flagged, clamped
+        if (p.pos_err && blockIdx.x == 0 && tid == 0) *p.pos_err = 1;
+        pos = p.max_ctx - 1;
+    }
     const int n_tok = pos + 1;
     int chunk = (n_tok + p.n_split - 1) / p.n_split;
     if (chunk < p.min_chunk) chunk = p.min_chunk;
@@ -402,13 +406,14 @@ __global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(LMHeadParams p) {
     }
 }
 
-// pos += 1 after a generated step, and the chosen token appended to tokens_out[*count].
-__global__ void advance_kernel(int* pos, const unsigned long long* key, int* tokens_out, int* count) {
+// pos += 1 after a generated step (saturating at max_ctx: "no room left"), and the chosen
+// token appended to tokens_out[*count].
+__global__ void advance_kernel(int* pos, const unsigned long long* key, int* tokens_out, int* count, int max_ctx) {
     pdl_trigger();
     pdl_wait();
     if (tokens_out) tokens_out[*count] = (int)(0xffffffffu - (unsigned)(*key & 0xffffffffull));
     if (count) *count += 1;
-    *pos += 1;
+    *pos = min(*pos + 1, max_ctx);
 }
 
 // ------------------------------------------------------------------ host launchers
@@ -465,8 +470,9 @@ int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s, bool pdl) {
     return IAM_OK;
 }
 
-int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s, bool pdl) {
-    IAM_CUDA_TRY(launch_ex(advance_kernel, dim3(1), dim3(1), 0, s, pdl, pos, key, tokens_out, count));
+int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, int max_ctx, cudaStream_t s,
+                   bool pdl) {
+    IAM_CUDA_TRY(launch_ex(advance_kernel, dim3(1), dim3(1), 0, s, pdl, pos, key, tokens_out, count, max_ctx));
     return IAM_OK;
 }
 

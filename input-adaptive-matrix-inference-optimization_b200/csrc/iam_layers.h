@@ -19,6 +19,7 @@ struct AttnParams {
     uint16_t* v_cache;     // this layer: [n_kv_heads][max_ctx][head_dim] fp16
     const float* rope;     // [max_ctx][head_dim/2][2] cos, sin
     const int* pos_dev;    // position of the token being decoded (context = pos + 1)
+    int* pos_err;          // set when pos_dev holds max_ctx or more (the step is clamped), may be null
     float* out;            // [n_heads][head_dim]
     float* part;           // scratch [n_kv_heads][n_split][gq][head_dim + 2]
     int* ctr;              // [n_kv_heads] zero-initialised, self-resetting
@@ -44,7 +45,7 @@ size_t attention_smem(const AttnParams& p, int gq);
 // pdl: launch with programmatic stream serialization (see launch_ex)
 int launch_attention(const AttnParams& p, int gq, cudaStream_t s, bool pdl = false);
 int launch_lm_head(const LMHeadParams& p, int grid, cudaStream_t s, bool pdl = false);
-int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, cudaStream_t s,
+int launch_advance(int* pos, const unsigned long long* key, int* tokens_out, int* count, int max_ctx, cudaStream_t s,
                    bool pdl = false);
 
 }  // namespace iam

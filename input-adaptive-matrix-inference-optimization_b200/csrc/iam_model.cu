@@ -161,6 +161,8 @@ struct iam_model_s {
     float *x = nullptr, *x1 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
     float *g = nullptr, *u = nullptr, *logits = nullptr;
     int* pos = nullptr;
+    int* pos_err = nullptr;  // set by a decode step whose device position was past the cache
+    int host_pos = 0;        // the device position once the work enqueued so far has run
     int* token_used = nullptr;
     int* gen_count = nullptr;
     unsigned long long* key = nullptr;
@@ -274,6 +276,8 @@ int alloc_runtime(iam_model_s* m) {
         TpWindow& w = m->win;
         w.rank = m->tp_rank;
         w.world = m->tp_world;
+        w.spin_limit = kTpSpinLimit;
+        if (const char* v = getenv("IAM_TP_SPIN_LIMIT")) w.spin_limit = std::max(1LL, atoll(v));
         // the largest exchange: the o/down all-reduce (dim), the head all-gather, the gate+up
         // all-gather (2 x ffn_local) or the logits all-gather (vocab_local)
         w.mbox_floats = std::max(std::max(c.dim, qn / m->tp_world), std::max(2 * m->ffn_local, m->vocab_local));
@@ -295,10 +299,11 @@ int alloc_runtime(iam_model_s* m) {
         return rc;
     }
     if ((rc = dalloc(m, &m->q, qn)) || (rc = dalloc(m, &m->k, kvn)) || (rc = dalloc(m, &m->v, kvn)) ||
-        (rc = dalloc(m, &m->pos, 4)) || (rc = dalloc(m, &m->token_used, 4)) || (rc = dalloc(m, &m->gen_count, 4)) ||
+        (rc = dalloc(m, &m->pos, 4)) || (rc = dalloc(m, &m->pos_err, 1)) || (rc = dalloc(m, &m->token_used, 4)) || (rc = dalloc(m, &m->gen_count, 4)) ||
         (rc = dalloc(m, &m->key, 2)) || (rc = dalloc(m, &m->sel, (size_t)c.n_layers * NMAT)))
         return rc;
     IAM_CUDA_TRY(cudaMemset(m->pos, 0, 16));
+    IAM_CUDA_TRY(cudaMemset(m->pos_err, 0, sizeof(int)));
     IAM_CUDA_TRY(cudaMemset(m->key, 0, 16));
     const int cols_max = std::max(std::max(qn, c.dim), c.ffn_dim) / 16;
     for (int s = 0; s < 3; ++s) {
@@ -715,6 +720,7 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
         ap.v_cache = m->v_cache + (size_t)l * layer_kv;
         ap.rope = m->rope;
         ap.pos_dev = m->pos;
+        ap.pos_err = m->pos_err;
         ap.out = m->att + (size_t)m->tp_rank * m->n_heads_local * c.head_dim;
         ap.part = m->att_part;
         ap.ctr = m->att_ctr;
@@ -973,7 +979,7 @@ int create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long l
     cudaError_t e = cudaMalloc(&wtmp, wmax * 2);
     if (e == cudaSuccess && world > 1) e = cudaMalloc(&btmp, wmax * 2);
     if (e != cudaSuccess) rc = cuda_fail(e, "model build scratch");
-    const uint16_t one = 0x3c00;  // fp16 1.0: RMSNorm gains
+    const uint16_t one = 0x3c00;  // fp16 1.0: RMSNorm gains of the random-init benchmark model
     unsigned long long tensor = 1;
     for (int l = 0; l < c.n_layers && !rc; ++l) {
         Layer& L = m->layers[l];
@@ -986,7 +992,7 @@ int create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long l
     if (!rc && !(rc = dalloc(m, &m->embed, (size_t)c.vocab * c.dim)) && !(rc = dalloc(m, &m->final_norm, c.dim))) {
         init_normal_fp16<<<4 * m->sm_count, 256>>>(m->embed, (size_t)c.vocab * c.dim, seed, 0, 0.02f);
         fill_u16<<<8, 256>>>(m->final_norm, c.dim, one);
-        m->lm_head = m->embed + (size_t)m->vocab0 * c.dim;  // tied embeddings
+        m->lm_head = m->embed + (size_t)m->vocab0 * c.dim;  // tied embeddings (the random-init 32000-token model)
         if (!c.tied_embeddings && !(rc = dalloc(m, &m->lm_head, (size_t)m->vocab_local * c.dim)))
             init_normal_fp16<<<4 * m->sm_count, 256>>>(m->lm_head, (size_t)m->vocab_local * c.dim, seed, tensor++,
                                                        0.02f, (size_t)m->vocab0 * c.dim);
@@ -1109,6 +1115,7 @@ int iam_model_reset(iam_model_t m, void* stream) {
     IAM_CUDA_TRY(cudaMemsetAsync(m->k_cache, 0, kv, (cudaStream_t)stream));
     IAM_CUDA_TRY(cudaMemsetAsync(m->v_cache, 0, kv, (cudaStream_t)stream));
     IAM_CUDA_TRY(cudaMemsetAsync(m->pos, 0, sizeof(int), (cudaStream_t)stream));
+    m->host_pos = 0;
     return IAM_OK;
 }
 
@@ -1117,7 +1124,9 @@ int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* lo
     if (token < 0 || token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_forward: token out of range");
     if (pos < 0 || pos >= m->cfg.max_ctx) return fail(IAM_ERR_ARG, "iam_model_forward: pos out of range");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_forward: effort must be in (0, 1]");
-    return enqueue_step(m, token, pos, effort, logits_dev ? logits_dev : m->logits, (cudaStream_t)stream);
+    const int rc = enqueue_step(m, token, pos, effort, logits_dev ? logits_dev : m->logits, (cudaStream_t)stream);
+    if (!rc) m->host_pos = pos;
+    return rc;
 }
 
 int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int start_pos, float* logits_dev,
@@ -1150,6 +1159,10 @@ int iam_model_prefill(iam_model_t m, const int* tokens_host, int n_tokens, int s
     hp.logits = logits_dev;
     hp.argmax_key = m->key;
     if ((rc = launch_lm_head(hp, 2 * m->sm_count, s, false))) return rc;
+    // decoding continues after the prompt (iam_model_generate with first_token < 0 takes the
+    // prefill's greedy token from the argmax slot and this position)
+    IAM_CUDA_TRY(launch_ex(set_int_kernel, dim3(1), dim3(1), 0, s, false, m->pos, start_pos + n_tokens));
+    m->host_pos = start_pos + n_tokens;
     if (next_token) {
         IAM_CUDA_TRY(cudaStreamSynchronize(s));
         unsigned err = 0;
@@ -1167,9 +1180,13 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
     if (!m || !tokens_dev) return fail(IAM_ERR_ARG, "iam_model_generate: null argument");
     const bool cont = first_token < 0;  // continue from the device position and last argmax
     if (first_token >= m->cfg.vocab) return fail(IAM_ERR_ARG, "iam_model_generate: bad token");
-    if (!cont && (start_pos < 0 || start_pos + n_tokens > m->cfg.max_ctx))
-        return fail(IAM_ERR_ARG, "iam_model_generate: positions exceed max_ctx");
     if (n_tokens < 0) return fail(IAM_ERR_ARG, "iam_model_generate: negative n_tokens");
+    if (!cont && (start_pos < 0 || (long long)start_pos + n_tokens > m->cfg.max_ctx))
+        return fail(IAM_ERR_ARG, "iam_model_generate: positions exceed max_ctx");
+    // continuing decodes at the device position, which the host tracks: refused before any
+    // launch when the steps would run past the KV cache
+    if (cont && (long long)m->host_pos + n_tokens > m->cfg.max_ctx)
+        return fail(IAM_ERR_ARG, "iam_model_generate: continuing would decode past max_ctx");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_generate: effort must be in (0, 1]");
     cudaStream_t s = (cudaStream_t)stream;
     if (n_tokens == 0) return IAM_OK;
@@ -1182,7 +1199,7 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
     if (!cont) {
         if ((rc = enqueue_step(m, first_token, start_pos, effort, m->tp_world > 1 ? nullptr : m->logits, s)))
             return rc;
-        if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, s, m->pdl))) return rc;
+        if ((rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, m->cfg.max_ctx, s, m->pdl))) return rc;
         done = 1;
         if (n_tokens == 1) return IAM_OK;
     }
@@ -1199,7 +1216,7 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
             // greedy generation needs only the argmax key: under tensor parallelism the
             // logits all-gather is left out
             rc = enqueue_step(m, -1, -1, effort, m->tp_world > 1 ? nullptr : m->logits, cap);
-            if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, cap, m->pdl);
+            if (!rc) rc = launch_advance(m->pos, m->key, tokens_dev, m->gen_count, m->cfg.max_ctx, cap, m->pdl);
             e = cudaStreamEndCapture(cap, &graph);
         }
         if (e == cudaSuccess && !rc) e = cudaGraphInstantiate(&m->gen_graph, graph, 0);
@@ -1211,6 +1228,7 @@ int iam_model_generate(iam_model_t m, int first_token, int start_pos, int n_toke
         m->gen_tokens = tokens_dev;
     }
     for (int i = done; i < n_tokens; ++i) IAM_CUDA_TRY(cudaGraphLaunch(m->gen_graph, s));
+    m->host_pos = (cont ? m->host_pos : start_pos) + n_tokens;
     return IAM_OK;
 }
 
@@ -1218,6 +1236,8 @@ int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kerne
                             int* n_kernels, void* stream) {
     if (!m || steps <= 0 || !n_kernels) return fail(IAM_ERR_ARG, "iam_model_profile_steps: bad arguments");
     if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "iam_model_profile_steps: effort must be in (0, 1]");
+    if ((long long)m->host_pos + steps > m->cfg.max_ctx)
+        return fail(IAM_ERR_ARG, "iam_model_profile_steps: the steps would decode past max_ctx");
     cudaStream_t s = (cudaStream_t)stream;
     int rc = build_plans(m, effort);
     if (rc) return rc;
@@ -1230,7 +1250,7 @@ int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kerne
     if (e == cudaSuccess) {
         rc = enqueue_step(m, -1, -1, effort, m->logits, cap, &hk);
         if (!rc) rc = hook(&hk, IAM_KERNEL_OTHER, cap);
-        if (!rc) rc = launch_advance(m->pos, m->key, nullptr, nullptr, cap);
+        if (!rc) rc = launch_advance(m->pos, m->key, nullptr, nullptr, m->cfg.max_ctx, cap);
         if (!rc) rc = hook(&hk, IAM_KERNEL_OTHER, cap);
         e = cudaStreamEndCapture(cap, &graph);
     }
@@ -1252,6 +1272,7 @@ int iam_model_profile_steps(iam_model_t m, float effort, int steps, float* kerne
     for (cudaEvent_t ev : hk.ev) cudaEventDestroy(ev);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(e, "iam_model_profile_steps");
+    m->host_pos += steps;
     *n_kernels = nk;
     for (int k = 0; k < nk && k < capacity; ++k) {
         if (kernel_ms) kernel_ms[k] = (float)(acc[k] / steps);
@@ -1439,6 +1460,9 @@ int iam_model_status(iam_model_t m) {
         IAM_CUDA_TRY(cudaMemcpy(&err, m->xwin + m->win.err_off, sizeof(err), cudaMemcpyDeviceToHost));
         if (err) return fail(IAM_ERR_TIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
     }
+    int perr = 0;
+    IAM_CUDA_TRY(cudaMemcpy(&perr, m->pos_err, sizeof(perr), cudaMemcpyDeviceToHost));
+    if (perr) return fail(IAM_ERR_ARG, "a decode step found its position at or past max_ctx (clamped to the last slot)");
     return IAM_OK;
 }
 

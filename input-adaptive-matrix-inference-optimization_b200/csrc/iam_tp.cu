@@ -14,8 +14,6 @@ namespace iam {
 
 namespace {
 
-constexpr long long kSpinLimit = 1LL << 21;  // polls of one element before the wait gives up (~1 s)
-
 IAM_DEV void st_ll(uint2* p, uint32_t bits, uint32_t epoch) {
     asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(bits), "r"(epoch) : "memory");
 }
@@ -59,7 +57,7 @@ IAM_DEV float recv(const TpWindow& w, uint32_t epoch, int r, int i) {
     for (;;) {
         const uint2 v = ld_ll(q);
         if (v.y == epoch) return __uint_as_float(v.x);
-        if (++n > kSpinLimit || *err != 0u) {
+        if (++n > w.spin_limit || *err != 0u) {
             *err = 1u;
             return 0.0f;
         }
@@ -155,3 +153,68 @@ int tp_keymax(const TpWindow& w, unsigned long long* key, cudaStream_t s, bool p
 }
 
 }  // namespace iam
+
+// ------------------------------------------------------------------ bounded-wait self-test
+
+using namespace iam;
+
+extern "C" int iam_tp_wait_selftest(int device, int n, long long spin_limit, unsigned* err_out, float* first_ms,
+                                    float* second_ms) {
+    if (n <= 0 || n > (1 << 20) || spin_limit <= 0) return fail(IAM_ERR_ARG, "iam_tp_wait_selftest: bad n or spin_limit");
+    IAM_CUDA_TRY(cudaSetDevice(device));
+    // two windows on this GPU: rank 0's own and a stand-in for rank 1 that no kernel ever
+    // writes into rank 0's mailbox, so every wait of rank 0 runs to its poll bound
+    TpWindow w{};
+    w.rank = 0;
+    w.world = 2;
+    w.mbox_floats = n;
+    w.spin_limit = spin_limit;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 255) / 256 * 256;
+        return o;
+    };
+    const size_t o_buf = take((size_t)n * 4);
+    w.epoch_off = take(4 * kTpCtas);
+    w.err_off = take(4);
+    w.mbox_off = take((size_t)2 * w.world * w.mbox_floats * 8);
+    char* mem[2] = {nullptr, nullptr};
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    cudaStream_t s = nullptr;
+    int rc = IAM_OK;
+    cudaError_t e = cudaMalloc(&mem[0], off);
+    if (e == cudaSuccess) e = cudaMalloc(&mem[1], off);
+    if (e == cudaSuccess) e = cudaMemset(mem[0], 0, off);
+    if (e == cudaSuccess) e = cudaMemset(mem[1], 0, off);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventCreate(&ev[i]);
+    if (e != cudaSuccess) rc = cuda_fail(e, "iam_tp_wait_selftest: setup");
+    w.base[0] = mem[0];
+    w.base[1] = mem[1];
+    if (!rc && (e = cudaEventRecord(ev[0], s)) != cudaSuccess) rc = cuda_fail(e, "iam_tp_wait_selftest: event");
+    if (!rc) rc = tp_allreduce_sum(w, o_buf, n, s, false);
+    if (!rc && (e = cudaEventRecord(ev[1], s)) != cudaSuccess) rc = cuda_fail(e, "iam_tp_wait_selftest: event");
+    if (!rc) rc = tp_allreduce_sum(w, o_buf, n, s, false);  // the error word is set: no waiting
+    if (!rc && (e = cudaEventRecord(ev[2], s)) != cudaSuccess) rc = cuda_fail(e, "iam_tp_wait_selftest: event");
+    if (!rc && (e = cudaStreamSynchronize(s)) != cudaSuccess) rc = cuda_fail(e, "iam_tp_wait_selftest: run");
+    unsigned err = 0;
+    if (!rc && (e = cudaMemcpy(&err, mem[0] + w.err_off, sizeof(err), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        rc = cuda_fail(e, "iam_tp_wait_selftest: read error word");
+    float t1 = 0.0f, t2 = 0.0f;
+    if (!rc) {
+        cudaEventElapsedTime(&t1, ev[0], ev[1]);
+        cudaEventElapsedTime(&t2, ev[1], ev[2]);
+    }
+    for (cudaEvent_t x : ev)
+        if (x) cudaEventDestroy(x);
+    if (s) cudaStreamDestroy(s);
+    cudaFree(mem[0]);
+    cudaFree(mem[1]);
+    if (rc) return rc;
+    if (err_out) *err_out = err;
+    if (first_ms) *first_ms = t1;
+    if (second_ms) *second_ms = t2;
+    if (err) return fail(IAM_ERR_TIMEOUT, "iam_tp_wait_selftest: the exchange gave up waiting for the missing peer");
+    return IAM_OK;
+}

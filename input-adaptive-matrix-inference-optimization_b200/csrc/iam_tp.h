@@ -24,7 +24,11 @@ struct TpWindow {
     size_t err_off;           // u32: set when a wait gave up
     size_t mbox_off;          // uint2 [2][world][mbox_floats]: {value bits, epoch} from rank r
     int mbox_floats;          // elements per mailbox slot
+    long long spin_limit;     // polls of one element before a wait gives up (kTpSpinLimit by default)
 };
+
+// Default poll bound of a wait (~1 s on a B200 with the back-off of the poll loop).
+constexpr long long kTpSpinLimit = 1LL << 21;
 
 // Rank r's chunk [r*chunk, (r+1)*chunk) of the float buffer(s) at window offset off_a (and
 // off_b unless it is SIZE_MAX) is copied to the same place in every peer.

@@ -97,7 +97,7 @@ def make_x(kind, n, rng):
         return np.zeros(n, np.float32)
     if kind == "ones":
         return np.ones(n, np.float32)
-    if kind == "outliers":  # 1% of channels scaled x20
+    if kind == "outliers":  # the outlier inputs: 1% of channels scaled x20
         x = rng.standard_normal(n).astype(np.float32)
         idx = rng.choice(n, max(1, n // 100), replace=False)
         x[idx] *= np.float32(20.0)

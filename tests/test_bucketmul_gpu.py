@@ -1,6 +1,6 @@
 """GPU parity of the bucketMul operator (C ABI via ctypes) against the CPU oracle.
 
-Bar (BASELINE north_star): cutoff bit-exact, selected bucket-row SET identical, outputs
+Bar: cutoff bit-exact, selected bucket-row SET identical, outputs
 within max-abs 1e-3 x output RMS for fp16 weights with fp32 accumulation.
 """
 import numpy as np
@@ -244,7 +244,7 @@ def big_weights(iam, torch_mod, weights_mod):
 @pytest.mark.parametrize("name", list(SHAPES))
 @pytest.mark.parametrize("xkind", ["gaussian", "outliers"])
 def test_config2_shapes(bm, torch_mod, ora, big_weights, name, xkind):
-    """Mistral attention/FFN shapes at every effort."""
+    """Mistral attention/FFN shapes (x with 1% outliers x20) at every effort."""
     torch = torch_mod
     W, buckets, s1, pr = big_weights[name]
     o, i = SHAPES[name]

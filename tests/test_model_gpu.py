@@ -1,7 +1,7 @@
 """Decode-model parity on the GPU against the CPU oracle's decode step (ora_model_forward,
 which follows model.hpp:152-231 / transformer_layer.hpp:75-122 / attention.hpp:135-404).
 
-Bar (BASELINE north_star): greedy token ids equal for at least the first 32 tokens at each
+Bar: greedy token ids equal for at least the first 32 tokens at each
 effort; logits within LOGIT_TOL x RMS (fp32 summation order, GPU expf and the occasional
 bucket row whose importance sits within an ulp of the cutoff differ from the oracle).
 """
@@ -169,8 +169,36 @@ def test_model_rejects_bad_arguments(small, iam):
         iam.Model.random(bad)
 
 
+def test_positions_past_max_ctx_are_refused(iam, torch_mod):
+    """Every entry point that moves the device position checks it on the host first: a
+    continuing generate or a profile run that would decode at max_ctx or beyond is refused
+    with IAM_ERR_ARG before anything is launched, and the model stays usable."""
+    torch = torch_mod
+    cfg = iam.ModelConfig.make(**dict(SMALL, max_ctx=24))
+    m = iam.Model.random(cfg, seed=11)
+    toks = torch.empty(32, dtype=torch.int32, device="cuda")
+    m.generate(5, 0, 20, 0.5, toks)  # positions 0..19: fits
+    for call in (lambda: m.generate(-1, 0, 5, 0.5, toks),       # 20..24: past the cache
+                 lambda: m.generate(3, 20, 5, 0.5, toks),        # explicit start past it
+                 lambda: m.profile_steps(0.5, 5)):               # 20..24 again
+        with pytest.raises(iam.IamError) as e:
+            call()
+        assert e.value.code == iam.IAM_ERR_ARG
+    m.generate(-1, 0, 4, 0.5, toks)  # 20..23: exactly fills the cache
+    torch.cuda.synchronize()
+    m.status()  # no step ran at or past max_ctx
+    with pytest.raises(iam.IamError):
+        m.generate(-1, 0, 1, 0.5, toks)
+    m.forward(7, cfg.max_ctx - 1, 0.5)  # an explicit position inside the cache is fine
+    m.reset()
+    m.generate(-1, 0, 3, 0.5, toks)  # after a reset the position is 0 again
+    torch.cuda.synchronize()
+    m.status()
+    m.close()
+
+
 def test_config3_mistral_layer(iam, ora, torch_mod):
-    """one Mistral-7B decoder layer (d 4096, 32/8 heads, ffn 14336), KV cache
+    """One Mistral-7B decoder layer (d 4096, 32/8 heads, ffn 14336), KV cache
     of 1024 random N(0,1) fp16 tokens, gains 1.0, effort 0.25; plus the tied 32000-row head."""
     torch = torch_mod
     cfg = iam.ModelConfig.make(**dict(iam.MISTRAL_7B, n_layers=1, max_ctx=1040))

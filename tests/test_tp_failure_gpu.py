@@ -45,3 +45,20 @@ def test_missing_peer_ends_in_timeout(iam, cuda):
     code = int(line[-1].split()[1])
     assert code == iam.IAM_ERR_TIMEOUT, (line, r.stderr[-1000:])
     assert took < 90, took
+
+
+def test_exchange_wait_runs_out_on_one_gpu(iam, cuda):
+    """The bounded device-side wait of the one-shot exchanges, driven to its limit on one GPU:
+    a two-rank exchange window whose second rank is a local buffer that never sends.  The
+    first all-reduce gives up after spin_limit polls per element and sets the error word; the
+    next one returns without waiting; the status is IAM_ERR_TIMEOUT, as iam_model_status
+    reports it for a model.  No fault and no hang: every wait has its poll bound."""
+    rc, err, first_ms, second_ms = iam.tp_wait_selftest(n=256, spin_limit=4096)
+    assert rc == iam.IAM_ERR_TIMEOUT, (rc, err)
+    assert err == 1
+    assert 0.0 < first_ms < 2000.0, first_ms
+    assert second_ms < first_ms, (first_ms, second_ms)
+    # a longer bound waits longer before it gives up
+    rc2, err2, first2, _ = iam.tp_wait_selftest(n=256, spin_limit=4 * 4096)
+    assert rc2 == iam.IAM_ERR_TIMEOUT and err2 == 1
+    assert first2 > first_ms, (first_ms, first2)
