@@ -97,25 +97,31 @@ int iam_bucketmul_read_dispatch(iam_bucketmul_t h, int32_t* rows_dev, int* count
 int iam_bucketmul_mul(iam_bucketmul_t h, const uint16_t* buckets_dev, int bucket_rows,
                       int bucket_cols, float* out_dev, void* stream);
 
-/* BucketMul::fullMul (bucket_mul.hpp:254-267) as ONE fused launch: cutoff, selection and
- * accumulation in the same kernel.  count_dev (may be NULL) receives the number of
- * selected bucket rows, cutoff_dev (may be NULL) the cutoff. */
+/* BucketMul::fullMul (bucket_mul.hpp:254-267) as ONE fused launch: cutoff, selection,
+ * accumulation and integrate in the same kernel (one wave of at most one CTA per SM that
+ * meets at a grid-wide barrier; nothing else may keep every SM of the device busy while it
+ * runs).  count_dev (may be NULL) receives the number of selected bucket rows, cutoff_dev
+ * (may be NULL) the cutoff. */
 int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* stats_dev,
                        int stats_stride, const uint16_t* probes_dev, const uint16_t* buckets_dev,
                        int expert_no, int in_dim, int bucket_cols, int expert_size, float effort,
                        float* out_dev, int* count_dev, float* cutoff_dev, void* stream);
+/* Synchronises the device; IAM_ERR_TIMEOUT when an iam_bucketmul_full launch of `h` gave up
+ * waiting at its grid barrier (its outputs are then invalid), IAM_OK otherwise.  (No
+ * counterpart in the reference.) */
+int iam_bucketmul_status(iam_bucketmul_t h);
 
-/* Diagnostics: every later launch of `h` writes globaltimer stamps (ns) of its first CTA
- * to times_dev[0..9] (16 slots): [0] start, [1] cutoff done, [2] row lists done, [3] cluster
- * numbering done, [4] accumulation done, [5] partial tile done, [6] end, [8] cutoff loads
- * and min/max done, [9] bisection done.  NULL turns it off. */
+/* Diagnostics: every later iam_bucketmul_full of `h` writes the 16 trace slots (below) of
+ * its first CTA to times_dev[0..15].  NULL turns it off. */
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev);
 
-/* Diagnostics: every CTA c < capacity of later fused launches of `h` writes 8 int64 to
- * trace_dev[8c .. 8c+7]: globaltimer stamps (ns) [0] start, [1] cutoff done, [2] row lists
- * done, [3] cluster numbering done, [4] accumulation done, [5] partial tile done, [6] end,
- * and [7] the number of bucket rows the CTA accumulated.  NULL turns it off.  (No
- * counterpart in the reference: load-balance evidence for the fused kernel.) */
+/* Diagnostics: every CTA c < capacity of later iam_bucketmul_full launches of `h` writes 16
+ * int64 to trace_dev[16c .. 16c+15]: globaltimer stamps (ns) [0] start, [1] cutoff inputs
+ * loaded, [8] bisection mids computed, [9] values binned, [10] suffix counts, [11] binned
+ * steps replayed, [2] cutoff done, [3] row selection done, [4] accumulation done, [5] group
+ * sums pushed to the cluster, [6] end; and counts [7] bucket rows of the CTA's input group,
+ * [12] values of the last bisection bracket, [13] bisection steps.  NULL turns it off.
+ * (No counterpart in the reference: phase and load-balance evidence for the kernel.) */
 int iam_bucketmul_trace(iam_bucketmul_t h, long long* trace_dev, int capacity);
 
 /* iam_bucketmul_full without any device allocation, for callers that cannot allocate device
@@ -314,6 +320,18 @@ int iam_model_selected_rows(iam_model_t m, long long* total);
  * o, gate, up, down (this rank's rows under tensor parallelism: the whole selection for the
  * column-parallel matrices, its inputs' share for o and down).  capacity >= 7*n_layers. */
 int iam_model_selected_rows_by_matrix(iam_model_t m, int* counts, int capacity);
+/* Diagnostics (no counterpart in the reference): while a capture buffer is set, every decode
+ * step records, for each layer, the input x of its bucketMuls exactly as the kernels computed
+ * it (after the fused RMSNorm * gain or SiLU * up), their cutoffs and their outputs, so that
+ * every bucketMul of a real step can be checked against a reference implementation on
+ * identical inputs.  One record per layer, floats, with d = dim, a = n_heads * head_dim,
+ * kv = n_kv_heads * head_dim, f = ffn_dim:
+ *   x_qkv[d] q[a] k[kv] v[kv] x_o[a] res_o[d] out_o[d] x_gu[d] gate[f] up[f]
+ *   x_down[f] res_down[d] out_down[d] cutoff[8] (q, k, v, o, gate, up, down, unused)
+ * where out_o = res_o + o(x_o) and out_down = res_down + down(x_down).  buf_dev holds
+ * iam_model_capture_floats floats; NULL turns capturing off.  Single-GPU models only. */
+int iam_model_capture_floats(const iam_model_config* cfg, long long* floats);
+int iam_model_capture(iam_model_t m, float* buf_dev, size_t capacity_floats);
 /* Algorithmic bytes of the last step at KV length `context`: per bucketMul
  * 2|S|C + 2R + 4N + 2*min(N,4096) + 4M, plus K/V reads and the dense LM head (this rank's
  * share under tensor parallelism). */

@@ -40,6 +40,7 @@ _SIGNATURES = {
     "iam_bucketmul_mul": [_vp, _vp, _i32, _i32, _vp, _vp],
     "iam_bucketmul_full": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_bucketmul_phase_times": [_vp, _vp],
+    "iam_bucketmul_status": [_vp],
     "iam_bucketmul_trace": [_vp, _vp, ctypes.c_int],
     "iam_bucketmul_full_noalloc": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "iam_stats_pack": [_vp, _i64, _vp, _vp],
@@ -120,13 +121,17 @@ class BucketMul:
         except Exception:
             pass
 
+    def status(self):
+        """Raises IamError(IAM_ERR_TIMEOUT) if a full_mul launch gave up at its grid barrier."""
+        check(self.lib.iam_bucketmul_status(self.h))
+
     def phase_times(self, times):
-        """Diagnostics: later launches write 7 int64 globaltimer stamps into `times`."""
+        """Diagnostics: later full_mul launches write CTA 0's 16 int64 trace slots into `times`."""
         check(self.lib.iam_bucketmul_phase_times(self.h, _ptr(times)))
 
     def trace(self, stamps):
-        """Diagnostics: later fused launches write 8 int64 per CTA into `stamps` (None: off)."""
-        cap = 0 if stamps is None else int(stamps.numel()) // 8
+        """Diagnostics: later full_mul launches write 16 int64 per CTA into `stamps` (None: off)."""
+        cap = 0 if stamps is None else int(stamps.numel()) // 16
         check(self.lib.iam_bucketmul_trace(self.h, _ptr(stamps), cap))
 
     def cutoff(self, x, probes, in_dim, effort, out, iters=None, expert_no=0, stream=None):
@@ -264,6 +269,8 @@ _SIGNATURES.update({
     "iam_model_selected_rows_by_matrix": [_vp, _vp, _i32],
     "iam_tp_shard_info": [_vp, _i32, _i32, _vp],
     "iam_tp_wait_selftest": [_i32, _i32, _i64, _vp, _vp, _vp],
+    "iam_model_capture_floats": [_vp, _vp],
+    "iam_model_capture": [_vp, _vp, ctypes.c_size_t],
     "iam_model_create_random_tp": [_vp, _vp, ctypes.c_ulonglong, _i32, _i32, _i32, _vp],
     "iam_model_load_tp": [_vp, ctypes.c_char_p, _vp, _i32, _i32, _i32, _vp],
 })
@@ -400,6 +407,35 @@ class Model:
         out = np.zeros(n, np.int32)
         check(self.lib.iam_model_selected_rows_by_matrix(self.h, out.ctypes.data_as(ctypes.c_void_p), n))
         return out.reshape(self.cfg.n_layers, len(MATRIX_NAMES))
+
+    def capture(self, buf):
+        """iam_model_capture: later steps record every layer's bucketMul inputs, cutoffs and
+        outputs into `buf` (fp32 device tensor of capture_floats() elements; None: off)."""
+        check(self.lib.iam_model_capture(self.h, _ptr(buf), 0 if buf is None else buf.numel()))
+
+    def capture_floats(self):
+        n = ctypes.c_longlong()
+        check(self.lib.iam_model_capture_floats(ctypes.byref(self.cfg), ctypes.byref(n)))
+        return n.value
+
+    def capture_records(self, buf):
+        """Splits a capture buffer (copied to the host) into per-layer dicts of numpy arrays."""
+        import numpy as np
+        c = self.cfg
+        d, a, kv, f = c.dim, c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim, c.ffn_dim
+        parts = [("x_qkv", d), ("q", a), ("k", kv), ("v", kv), ("x_o", a), ("res_o", d), ("out_o", d),
+                 ("x_gu", d), ("gate", f), ("up", f), ("x_down", f), ("res_down", d), ("out_down", d),
+                 ("cutoff", 8)]
+        per = sum(n for _, n in parts)
+        host = buf.detach().cpu().numpy().reshape(c.n_layers, per)
+        recs = []
+        for l in range(c.n_layers):
+            off, rec = 0, {}
+            for name, n in parts:
+                rec[name] = host[l, off:off + n].copy()
+                off += n
+            recs.append(rec)
+        return recs
 
     def step_bytes(self, context):
         t = ctypes.c_longlong()

@@ -423,6 +423,14 @@ struct VecLoad<4> {
     }
 };
 template <>
+struct VecLoad<2> {
+    using T = uint32_t;
+    static IAM_DEV T load(const uint16_t* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+    static IAM_DEV T zero() { return 0u; }
+    static IAM_DEV uint32_t word(const T& v, int) { return v; }
+    static IAM_DEV uint32_t bits(const T& v, int k) { return (k & 1) ? (v >> 16) : (v & 0xffffu); }
+};
+template <>
 struct VecLoad<1> {
     using T = uint32_t;
     static IAM_DEV T load(const uint16_t* p) { return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p)); }
@@ -438,7 +446,7 @@ struct VecLoad<1> {
 // ((word << SS) & (15 << SS)) | acc_lane (low half) or ((word >> (16 - SS)) & ...) (high half).
 template <int VEC>
 struct SlotShift {
-    static constexpr int value = VEC == 8 ? 10 : VEC == 4 ? 9 : 7;  // log2(VEC * 128)
+    static constexpr int value = VEC == 8 ? 10 : VEC == 4 ? 9 : VEC == 2 ? 8 : 7;  // log2(VEC * 128)
 };
 
 // Volatile asm keeps these in program order among themselves (a later row may hit the same

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <string>
 
+#include "iam_bucketmul_group.h"
 #include "iam_bucketmul_launch.h"
 #include "iam_common.cuh"
 
@@ -38,6 +39,9 @@ struct iam_bucketmul_s {
     int* ctr = nullptr;         // slice arrival counters (zeroed once, self-resetting)
     float* cutoff = nullptr;    // device scalar
     int* ints = nullptr;        // device scalars: [0] count, [1] iters, [2] selected total, [8..] split counts
+    float* gpartials = nullptr;  // range-kernel partials (iam_bucketmul_full)
+    size_t gpartials_cap = 0;    // capacity in floats
+    unsigned* bar = nullptr;     // range-kernel grid barrier words (zeroed once)
     // dispatch recorded by iam_bucketmul_calc_dispatch (consumed by iam_bucketmul_mul)
     bool have_dispatch = false;
     BMProblem disp{};
@@ -182,6 +186,8 @@ int iam_bucketmul_create(iam_bucketmul_t* out, int device) {
     if (e == cudaSuccess) e = cudaMalloc(&h->ints, sizeof(int) * (8 + kMaxSplits));
     if (e == cudaSuccess) e = cudaMalloc(&h->ctr, sizeof(int) * kCtrSlots);
     if (e == cudaSuccess) e = cudaMemset(h->ctr, 0, sizeof(int) * kCtrSlots);
+    if (e == cudaSuccess) e = cudaMalloc(&h->bar, 4 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(h->bar, 0, 4 * sizeof(unsigned));
     if (e != cudaSuccess) {
         iam_bucketmul_destroy(h);
         return cuda_fail(e, "iam_bucketmul_create: cudaMalloc");
@@ -197,6 +203,8 @@ int iam_bucketmul_destroy(iam_bucketmul_t h) {
     cudaFree(h->ctr);
     cudaFree(h->cutoff);
     cudaFree(h->ints);
+    cudaFree(h->gpartials);
+    cudaFree(h->bar);
     delete h;
     return IAM_OK;
 }
@@ -280,36 +288,61 @@ int iam_bucketmul_full(iam_bucketmul_t h, const float* x_dev, const uint16_t* st
                        float* cutoff_dev, void* stream) {
     if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_full: null handle");
     if (!buckets_dev || !out_dev) return fail(IAM_ERR_ARG, "iam_bucketmul_full: null buckets/out");
-    const int G = bm_default_cluster();
-    BMBatch b;
-    memset(&b, 0, sizeof(b));
-    int rc = fill_problem(h, b.p[0], G, x_dev, stats_dev, stats_stride, probes_dev, expert_no, in_dim,
-                          bucket_cols, expert_size, effort);
-    if (rc) return rc;
-    b.p[0].buckets = buckets_dev;
-    b.p[0].out = out_dev;
-    b.p[0].count_out = count_dev;
-    b.p[0].cutoff_out = cutoff_dev;
-    b.nprob = 1;
-    b.mode = kModeFused;
-    const int vec = pick_vec(b);
-    const BMBatch spec = b;
-    bm_plan(b, vec, G, bm_max_active_clusters(vec, G));
-    int g_used = G;
-    // as the decode step's plans: clusters of 2 when clusters of G leave a fifth of the SMs idle
-    int dev = 0, sms = 0;
-    if (!getenv("IAM_BM_CLUSTER") && G != 2 && cudaGetDevice(&dev) == cudaSuccess &&
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-        bm_total_clusters(b) * G < 0.8 * sms) {
-        BMBatch alt = spec;
-        bm_plan(alt, vec, 2, bm_max_active_clusters(vec, 2));
-        if (bm_total_clusters(alt) * 2 > bm_total_clusters(b) * G) {
-            b = alt;
-            g_used = 2;
-        }
+    if (!x_dev || !stats_dev || !probes_dev) return fail(IAM_ERR_ARG, "bucketmul: null input/stats/probes pointer");
+    if (in_dim <= 0 || bucket_cols <= 0 || expert_size <= 0 || expert_no < 0)
+        return fail(IAM_ERR_ARG, "bucketmul: in_dim, bucket_cols, expert_size must be > 0, expert_no >= 0");
+    if (stats_stride != 1 && stats_stride != 4)
+        return fail(IAM_ERR_ARG, "bucketmul: stats_stride must be 1 (packed) or 4 (file layout)");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "bucketmul: effort must be in (0, 1]");
+    // one launch of the range kernel (iam_bucketmul_group.cu); its partials and barrier words
+    // live in the handle
+    const size_t need = bg_scratch_floats(kMaxRanges, bucket_cols);
+    if (need > h->gpartials_cap) {
+        if (h->gpartials) IAM_CUDA_TRY(cudaFree(h->gpartials));
+        h->gpartials = nullptr;
+        h->gpartials_cap = 0;
+        IAM_CUDA_TRY(cudaMalloc(&h->gpartials, need * sizeof(float)));
+        h->gpartials_cap = need;
     }
-    if (!plan_fits(b, g_used)) return fail(IAM_ERR_UNSUPPORTED, "iam_bucketmul_full: plan exceeds scratch");
-    return bm_launch(b, vec, g_used, (cudaStream_t)stream);
+    BGBatch b;
+    memset(&b, 0, sizeof(b));
+    BGProblem& p = b.p[0];
+    p.x = x_dev;
+    p.stats = stats_dev;
+    p.stats_stride = stats_stride;
+    p.probes = probes_dev + (size_t)expert_no * IAM_PROBES_COUNT;  // bucketMul.cl:103
+    p.buckets = buckets_dev;
+    p.row0 = (long long)expert_size * expert_no;                    // bucketMul.cl:363
+    p.bucket_row0 = 0;
+    p.n_rows_valid = expert_size < 16 * in_dim ? expert_size : 16 * in_dim;
+    p.in_begin = 0;
+    p.n_in = (p.n_rows_valid + 15) / 16;
+    p.cols = bucket_cols;
+    p.P = in_dim < IAM_PROBES_COUNT ? in_dim : IAM_PROBES_COUNT;
+    p.target = bm_target(effort, p.P);
+    p.out = out_dev;
+    p.count_out = count_dev;
+    p.cutoff_out = cutoff_dev;
+    p.partials = h->gpartials;
+    if ((p.row0 + p.n_rows_valid) * (long long)bucket_cols >= (1LL << 31))
+        return fail(IAM_ERR_UNSUPPORTED, "bucketmul: rows * bucket_cols must stay below 2^31 elements");
+    b.nprob = 1;
+    b.xmode = kXPlain;
+    b.barrier = h->bar;
+    b.trace = h->trace ? h->trace : h->dbg;
+    b.trace_cap = h->trace ? h->trace_cap : (h->dbg ? 1 : 0);
+    bg_choose_shape(b);
+    return bg_launch(b, (cudaStream_t)stream);
+}
+
+int iam_bucketmul_status(iam_bucketmul_t h) {
+    if (!h) return fail(IAM_ERR_ARG, "iam_bucketmul_status: null handle");
+    IAM_CUDA_TRY(cudaSetDevice(h->device));
+    IAM_CUDA_TRY(cudaDeviceSynchronize());
+    unsigned bar[4] = {0, 0, 0, 0};
+    IAM_CUDA_TRY(cudaMemcpy(bar, h->bar, sizeof(bar), cudaMemcpyDeviceToHost));
+    if (bar[2]) return fail(IAM_ERR_TIMEOUT, "iam_bucketmul_full: a launch gave up waiting at its grid barrier");
+    return IAM_OK;
 }
 
 int iam_bucketmul_phase_times(iam_bucketmul_t h, long long* times_dev) {

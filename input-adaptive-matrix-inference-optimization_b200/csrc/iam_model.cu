@@ -21,6 +21,7 @@
 
 #include <nccl.h>
 
+#include "iam_bucketmul_group.h"
 #include "iam_bucketmul_launch.h"
 #include "iam_common.cuh"
 #include "iam_dense.h"
@@ -32,6 +33,32 @@ namespace iam {
 
 enum { MQ = 0, MK, MV, MO, MG, MU, MD, NMAT };
 static const char* kMatNames[NMAT] = {"q", "k", "v", "o", "gate", "up", "down"};
+
+// Float offsets of one layer's record in a capture buffer (iam_model_capture).
+struct CaptureLayout {
+    size_t xqkv, q, k, v, xo, reso, outo, xgu, g, u, xd, resd, outd, cut, total;
+};
+inline CaptureLayout capture_layout(const iam_model_config& c) {
+    const size_t d = c.dim, a = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * c.head_dim, f = c.ffn_dim;
+    CaptureLayout L{};
+    size_t o = 0;
+    L.xqkv = o; o += d;
+    L.q = o;    o += a;
+    L.k = o;    o += kv;
+    L.v = o;    o += kv;
+    L.xo = o;   o += a;
+    L.reso = o; o += d;
+    L.outo = o; o += d;
+    L.xgu = o;  o += d;
+    L.g = o;    o += f;
+    L.u = o;    o += f;
+    L.xd = o;   o += f;
+    L.resd = o; o += d;
+    L.outd = o; o += d;
+    L.cut = o;  o += 8;
+    L.total = o;
+    return L;
+}
 
 struct Matrix {
     uint16_t* buckets = nullptr;  // [16*in][out/16] (column shard for column-parallel TP)
@@ -176,7 +203,12 @@ struct iam_model_s {
     int* att_ctr = nullptr;
     int att_split = 32, att_min_chunk = kAttnMinChunk;
     // launch plans for the current effort
-    std::vector<BMBatch> plans;  // 4 per layer
+    std::vector<BMBatch> plans;   // 4 per layer (cluster-split kernel, IAM_BM_KERNEL=split)
+    std::vector<BGBatch> gplans;  // 4 per layer (range kernel, the default)
+    bool use_group = true;
+    float* gpartials[3] = {nullptr, nullptr, nullptr};  // range-kernel partials, one slot per problem
+    unsigned* bm_bar = nullptr;                          // range-kernel grid barrier words
+    float* capture = nullptr;                            // diagnostics: per-layer bucketMul records
     float plan_effort = -1.0f;
     int vec = 4, G = 4;
     bool pdl = true;  // step kernels launched with programmatic stream serialization (IAM_PDL=0: off)
@@ -308,10 +340,13 @@ int alloc_runtime(iam_model_s* m) {
     const int cols_max = std::max(std::max(qn, c.dim), c.ffn_dim) / 16;
     for (int s = 0; s < 3; ++s) {
         if ((rc = dalloc(m, &m->partials[s], (size_t)kMaxSplits * 16 * cols_max)) ||
-            (rc = dalloc(m, &m->ctr[s], 4096)) || (rc = dalloc(m, &m->split_sel[s], kMaxSplits)))
+            (rc = dalloc(m, &m->ctr[s], 4096)) || (rc = dalloc(m, &m->split_sel[s], kMaxSplits)) ||
+            (rc = dalloc(m, &m->gpartials[s], bg_scratch_floats(kMaxRanges, cols_max))))
             return rc;
         IAM_CUDA_TRY(cudaMemset(m->ctr[s], 0, 4096 * sizeof(int)));
     }
+    if ((rc = dalloc(m, &m->bm_bar, 4))) return rc;
+    IAM_CUDA_TRY(cudaMemset(m->bm_bar, 0, 4 * sizeof(unsigned)));
     const int gq = c.n_heads / c.n_kv_heads;
     // chunks per KV head: about 2 CTAs per SM at long context (short contexts use fewer: a
     // chunk holds at least att_min_chunk tokens; 4 per SM and 4 tokens per half-warp in flight
@@ -668,8 +703,65 @@ int build_plans(iam_model_s* m, float effort) {
         d.p[0].count_out = sel + MD;
         plan_batch(m, d);
     }
+    // the same launches for the range kernel (the default): one wave of CTAs over column
+    // tiles x input ranges of the inputs this rank holds
+    m->gplans.assign(m->plans.size(), BGBatch{});
+    static const int kMats[4][3] = {{MQ, MK, MV}, {MO, -1, -1}, {MG, MU, -1}, {MD, -1, -1}};
+    for (int l = 0; l < c.n_layers; ++l)
+        for (int bi = 0; bi < 4; ++bi) {
+            const BMBatch& a = m->plans[l * 4 + bi];
+            BGBatch& b = m->gplans[l * 4 + bi];
+            memset(&b, 0, sizeof(b));
+            b.nprob = a.nprob;
+            b.xmode = a.xmode;
+            b.barrier = m->bm_bar;
+            for (int i = 0; i < a.nprob; ++i) {
+                const Matrix& mat = m->layers[l].m[kMats[bi][i]];
+                const BMProblem& sp = a.p[i];
+                BGProblem& p = b.p[i];
+                p.buckets = sp.buckets;
+                p.stats = sp.stats;
+                p.stats_stride = sp.stats_stride;
+                p.probes = sp.probes;
+                p.x = sp.x;
+                p.x2 = sp.x2;
+                p.gain = sp.gain;
+                p.norm_eps = sp.norm_eps;
+                p.norm_n = sp.norm_n;
+                p.out = sp.out;
+                p.residual = sp.residual;
+                p.count_out = sp.count_out;
+                p.partials = m->gpartials[i];
+                p.row0 = 0;
+                p.bucket_row0 = 16LL * mat.in_begin;
+                p.n_rows_valid = 16 * mat.in_dim;
+                p.in_begin = mat.in_begin;
+                p.n_in = mat.in_end - mat.in_begin;
+                p.cols = mat.cols;
+                p.P = sp.P;
+                p.target = sp.target;
+                if (m->capture) {  // diagnostics: the x each launch used and every cutoff
+                    const CaptureLayout CL = capture_layout(c);
+                    float* rec = m->capture + (size_t)l * CL.total;
+                    const size_t xoff[4] = {CL.xqkv, CL.xo, CL.xgu, CL.xd};
+                    if (i == 0) p.x_capture = rec + xoff[bi];
+                    p.cutoff_out = rec + CL.cut + kMats[bi][i];
+                }
+            }
+            bg_choose_shape(b);
+        }
     m->plan_effort = effort;
     return IAM_OK;
+}
+
+// One bucketMul launch of the step: the group kernel, or the cluster-split kernel.
+int launch_plan(iam_model_s* m, int idx, bool pdl, cudaStream_t s) {
+    if (m->use_group) {
+        m->gplans[idx].pdl = pdl;
+        return bg_launch(m->gplans[idx], s);
+    }
+    m->plans[idx].pdl = pdl;
+    return bm_launch(m->plans[idx], m->vec, m->plans[idx].cluster, s);
 }
 
 // Optional per-launch CUDA events (diagnostics): an event is recorded before every launch
@@ -709,8 +801,15 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     const int gq = c.n_heads / c.n_kv_heads;
     for (int l = 0; l < c.n_layers; ++l) {
         if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
-        m->plans[l * 4 + 0].pdl = pdl;
-        if ((rc = bm_launch(m->plans[l * 4 + 0], m->vec, m->plans[l * 4 + 0].cluster, s))) return rc;
+        if ((rc = launch_plan(m, l * 4 + 0, pdl, s))) return rc;
+        if (m->capture) {  // q, k, v of this layer (before attention rotates them)
+            const CaptureLayout CL = capture_layout(c);
+            float* rec = m->capture + (size_t)l * CL.total;
+            const size_t qn = (size_t)c.n_heads * c.head_dim, kvn = (size_t)c.n_kv_heads * c.head_dim;
+            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.q, m->q, qn * 4, cudaMemcpyDeviceToDevice, s));
+            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.k, m->k, kvn * 4, cudaMemcpyDeviceToDevice, s));
+            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.v, m->v, kvn * 4, cudaMemcpyDeviceToDevice, s));
+        }
         AttnParams ap{};
         ap.q = m->q;
         ap.k = m->k;
@@ -751,8 +850,21 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
                 if (rc) return rc;
             }
             if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
-            m->plans[l * 4 + b].pdl = pdl;
-            if ((rc = bm_launch(m->plans[l * 4 + b], m->vec, m->plans[l * 4 + b].cluster, s))) return rc;
+            if (m->capture && b != 2)  // the residual this launch adds (o: x, down: x1)
+                IAM_CUDA_TRY(cudaMemcpyAsync(m->capture + (size_t)l * capture_layout(c).total +
+                                                 (b == 1 ? capture_layout(c).reso : capture_layout(c).resd),
+                                             b == 1 ? m->x : m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+            if ((rc = launch_plan(m, l * 4 + b, pdl, s))) return rc;
+            if (m->capture) {  // this launch's outputs
+                const CaptureLayout CL = capture_layout(c);
+                float* rec = m->capture + (size_t)l * CL.total;
+                if (b == 1) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outo, m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+                if (b == 2) {
+                    IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.g, m->g, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
+                    IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.u, m->u, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
+                }
+                if (b == 3) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outd, m->x, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+            }
         }
         if (m->tp_world > 1) {
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
@@ -937,6 +1049,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int ran
     m->tp_rank = rank;
     m->tp_world = world;
     if (const char* v = getenv("IAM_PDL")) m->pdl = atoi(v) != 0;
+    if (const char* v = getenv("IAM_BM_KERNEL")) m->use_group = std::string(v) != "split";
     if (const char* v = getenv("IAM_TP_TIMEOUT_S")) m->tp_timeout_s = atof(v);
     if (const char* v = getenv("IAM_TP_COLL")) m->tp_p2p = std::string(v) != "nccl";
     m->n_heads_local = cfg->n_heads / world;
@@ -1444,6 +1557,31 @@ int iam_model_save(iam_model_t m, const char* weights_dir) {
     return rc;
 }
 
+int iam_model_capture_floats(const iam_model_config* cfg, long long* floats) {
+    if (!cfg || !floats) return fail(IAM_ERR_ARG, "iam_model_capture_floats: null argument");
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    *floats = (long long)capture_layout(*cfg).total * cfg->n_layers;
+    return IAM_OK;
+}
+
+int iam_model_capture(iam_model_t m, float* buf_dev, size_t capacity_floats) {
+    if (!m) return fail(IAM_ERR_ARG, "iam_model_capture: null model");
+    if (buf_dev) {
+        if (m->tp_world > 1) return fail(IAM_ERR_UNSUPPORTED, "iam_model_capture: single-GPU models only");
+        if (!m->use_group) return fail(IAM_ERR_UNSUPPORTED, "iam_model_capture: needs the range bucketMul kernel");
+        if (capacity_floats < capture_layout(m->cfg).total * (size_t)m->cfg.n_layers)
+            return fail(IAM_ERR_ARG, "iam_model_capture: buffer smaller than iam_model_capture_floats");
+    }
+    m->capture = buf_dev;
+    m->plan_effort = -1.0f;  // plans carry the capture pointers: rebuilt at the next step
+    if (m->gen_graph) {
+        cudaGraphExecDestroy(m->gen_graph);
+        m->gen_graph = nullptr;
+    }
+    return IAM_OK;
+}
+
 int iam_model_selected_rows_by_matrix(iam_model_t m, int* counts, int capacity) {
     if (!m || !counts) return fail(IAM_ERR_ARG, "iam_model_selected_rows_by_matrix: null argument");
     const int n = m->cfg.n_layers * NMAT;
@@ -1460,6 +1598,9 @@ int iam_model_status(iam_model_t m) {
         IAM_CUDA_TRY(cudaMemcpy(&err, m->xwin + m->win.err_off, sizeof(err), cudaMemcpyDeviceToHost));
         if (err) return fail(IAM_ERR_TIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
     }
+    unsigned bar[4] = {0, 0, 0, 0};
+    IAM_CUDA_TRY(cudaMemcpy(bar, m->bm_bar, sizeof(bar), cudaMemcpyDeviceToHost));
+    if (bar[2]) return fail(IAM_ERR_TIMEOUT, "a bucketMul launch gave up waiting at its grid barrier");
     int perr = 0;
     IAM_CUDA_TRY(cudaMemcpy(&perr, m->pos_err, sizeof(perr), cudaMemcpyDeviceToHost));
     if (perr) return fail(IAM_ERR_ARG, "a decode step found its position at or past max_ctx (clamped to the last slot)");

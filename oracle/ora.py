@@ -60,6 +60,8 @@ def lib():
         L.ora_model_forward.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, ctypes.c_int]
         L.ora_model_forward_dense.restype = ctypes.c_int
         L.ora_model_forward_dense.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
+        L.ora_attention.restype = None
+        L.ora_attention.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int, _vp]
         _lib = L
     return _lib
 
@@ -161,6 +163,17 @@ def lm_head(W_u16, x, nthreads=1):
     rows, cols = W_u16.shape
     out = np.empty(rows, np.float32)
     lib().ora_lm_head(_p(W_u16), rows, cols, _p(x), _p(out), nthreads)
+    return out
+
+
+def attention(cfg, q_roped, k_layer, v_layer, n_tokens):
+    """ora_attention (aux.cl:497-540, :204-225, :370-384): every query head over the first
+    n_tokens of one layer's fp16 caches k/v [n_kv_heads][max_ctx][head_dim]; q post-RoPE."""
+    c = _Config(cfg["dim"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ffn_dim"],
+                cfg["vocab"], cfg["max_ctx"], cfg.get("norm_eps", 1e-5), cfg.get("rope_theta", 1e6))
+    q = _f32(q_roped)
+    out = np.empty(cfg["n_heads"] * cfg["head_dim"], np.float32)
+    lib().ora_attention(ctypes.byref(c), _p(q), _p(_u16(k_layer)), _p(_u16(v_layer)), n_tokens, _p(out))
     return out
 
 
