@@ -316,11 +316,9 @@ def prompt_tokens(vocab):
     return np.random.default_rng(1).integers(3, vocab, PROMPT_LEN).tolist()
 
 
-def run_decode(args, rank, world):
-    import torch
-    iam = load_pkg()
-    dev = torch.device(f"cuda:{int(os.environ.get('LOCAL_RANK', 0))}")
-    torch.cuda.set_device(dev)
+def decode_plan(args):
+    """(start position, max_ctx, effort sweep, sweep tokens, profiled steps, e2e tokens) of the
+    decode workload; the reference arm builds its model from the same numbers."""
     sweep = [e for e in (0.5, 1.0) if e != args.effort] if not args.no_sweep else []
     n_sweep = max(8, args.steps // 4)
     n_prof = 4
@@ -329,6 +327,31 @@ def run_decode(args, rank, world):
     # random fp16 KV prefix, decoding starts after it
     start = args.kv_prefix if args.kv_prefix > 0 else PROMPT_LEN
     max_ctx = start + args.warmup + args.steps + n_sweep * len(sweep) + n_prof + n_e2e + 8
+    return start, max_ctx, sweep, n_sweep, n_prof, n_e2e
+
+
+def decode_config(args, cfg, world):
+    """The workload description both arms print (the timed tokens are positions
+    start + W .. start + W + K - 1 of the same model and prompt)."""
+    start = args.kv_prefix if args.kv_prefix > 0 else PROMPT_LEN
+    return {"workload": ("decode: config 5 context, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
+                         f"tied embeddings, greedy batch-1 decode after a random fp16 KV prefix of "
+                         f"{args.kv_prefix} tokens") if args.kv_prefix > 0 else
+                        ("decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
+                         "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)"),
+            "model": "Mistral-7B (random init)" + (f", {cfg.n_layers} layers" if args.layers else ""),
+            "effort": args.effort, "global_batch": 1, "seq_len": start + args.warmup + args.steps,
+            "timed_positions": [start + args.warmup, start + args.warmup + args.steps - 1],
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token"}
+
+
+def run_decode(args, rank, world):
+    import torch
+    iam = load_pkg()
+    dev = torch.device(f"cuda:{int(os.environ.get('LOCAL_RANK', 0))}")
+    torch.cuda.set_device(dev)
+    start, max_ctx, sweep, n_sweep, n_prof, n_e2e = decode_plan(args)
     cfg = mistral_cfg(iam, max_ctx, args.layers)
     tp = None
     if world > 1:  # one decode stream, tensor-parallel over the ranks (NCCL inside the library)
@@ -336,20 +359,13 @@ def run_decode(args, rank, world):
         torch.distributed.broadcast_object_list(uid, src=0)
         tp = (rank, world, uid[0])
     t_build = time.perf_counter()
-    model = iam.Model.random(cfg, seed=0, device=dev.index, tp=tp)
+    model, logits, first = prepared_decode_model(args, iam, torch, cfg, dev, tp)
     build_s = time.perf_counter() - t_build
     stream = torch.cuda.current_stream()
-    logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
-    if args.kv_prefix > 0:
-        model.fill_kv_random(args.kv_prefix, seed=1)
-        model.forward(int(prompt_tokens(cfg.vocab)[0]), start - 1, args.effort, logits)
-    else:
-        for pos, tok in enumerate(prompt_tokens(cfg.vocab)):  # token by token (test_generation.cpp:202-210)
-            model.forward(tok, pos, args.effort, logits)
-    first = int(torch.argmax(logits).item())
     toks = torch.empty(max_ctx, dtype=torch.int32, device=dev)
     model.generate(first, start, args.warmup, args.effort, toks)  # includes the graph capture
     torch.cuda.synchronize()
+    timed_first = int(toks[args.warmup - 1].item())  # the token the first timed step takes in
 
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -388,7 +404,12 @@ def run_decode(args, rank, world):
     kv_bytes = 2 * cfg.n_layers * (cfg.n_kv_heads // world) * (ctx_end + n_prof) * cfg.head_dim * 2
     bm_bytes = total_bytes - lm_bytes - kv_bytes
     peak, peak_kind = measured_peaks()
-    achieved = bm_bytes / (bm_ms * 1e-3) / 1e9
+    # Events between the kernels of an eager profiled step add their own gaps, so their sum is
+    # longer than a graph-replayed step: each kernel kind is given its share of the events'
+    # total, applied to the graph-timed step.
+    share = bm_ms / all_ms if all_ms > 0 else 1.0
+    bm_graph_ms = (ms / args.steps) * share
+    achieved = bm_bytes / (bm_graph_ms * 1e-3) / 1e9
 
     # effort sweep (same graph machinery, fewer tokens)
     sweep_res = {}
@@ -425,6 +446,13 @@ def run_decode(args, rank, world):
         e2e_s = float(t[0])
     e2e_tok_s = n_e2e / e2e_s
 
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU port runs on rank 0 at N=1 only
+        # a bounded sample from the GPU's cache at the first timed position (the later
+        # positions are rewritten as the oracle goes), before the prefill below rewrites the prompt's
+        cpu_base = cpu_baseline_decode(model, cfg, args.effort, start + args.warmup, timed_first,
+                                       budget_s=args.cpu_seconds)
+
     prefill = None
     if world == 1:  # the prompt again, in one batched pass on the dense tensor-core path
         prompt = prompt_tokens(cfg.vocab)
@@ -439,27 +467,24 @@ def run_decode(args, rank, world):
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": ("decode: config 5 context, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
-                                f"tied embeddings, greedy batch-1 decode after a random fp16 KV prefix of "
-                                f"{args.kv_prefix} tokens") if args.kv_prefix > 0 else
-                               ("decode: config 4, Mistral-7B shape, 32 layers, random N(0,0.02) weights, "
-                                "tied embeddings, greedy batch-1 decode after a 128-token prompt (seed 1)"),
-                   "model": "Mistral-7B (random init)" + (f", {cfg.n_layers} layers" if args.layers else ""),
-                   "effort": args.effort, "global_batch": 1,
-                   "seq_len": ctx_end, "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token",
-                   "tokens_per_s_by_effort": sweep_res, "selected_rows_per_step": sel_rows,
+        "config": decode_config(args, cfg, world),
+        "detail": {"tokens_per_s_by_effort": sweep_res, "selected_rows_per_step": sel_rows,
                    "algorithmic_bytes_per_step": step_bytes,
                    "step_effective_GBps": round(step_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
                    "model_build_s": round(build_s, 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.effort),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one "
-                                       "decode step's 128 launches (profiles/decode_step_launch_list.md)",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per bg_kernel launch, "
+                                       "mean over the 8 launches of a 2-layer decode step (profiles/"
+                                       "decode_step_launch_list.md); the per-launch bytes do not depend on depth",
                      "peak_source": peak_kind,
-                     "kernel": "bm_fused_kernel", "bytes_per_launch": int(bm_bytes / (4 * cfg.n_layers)),
-                     "kernel_ms_per_step": round(bm_ms, 4), "step_ms_events": round(all_ms, 4),
-                     "ms_per_step_by_kernel": {k: round(v, 4) for k, v in by_kind.items()}},
+                     "kernel": "bg_kernel", "bytes_per_launch": int(bm_bytes / (4 * cfg.n_layers)),
+                     "kernel_ms_per_step": round(bm_graph_ms, 4),
+                     "kernel_share_of_step": round(share, 4),
+                     "timing": "the kernel's share of the CUDA-event times of profiled steps, applied to the "
+                               "graph-timed ms_per_step",
+                     "kernel_ms_per_step_events": round(bm_ms, 4), "step_ms_events": round(all_ms, 4),
+                     "ms_per_step_by_kernel_events": {k: round(v, 4) for k, v in by_kind.items()}},
         "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab},
         # ours per step and rank: embed, key clear, 32 x (4 bucketMul + attention), LM head,
@@ -471,8 +496,8 @@ def run_decode(args, rank, world):
     }
     if prefill:
         res["prefill"] = prefill
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU port runs on rank 0 at N=1 only
-        res["cpu_baseline"] = cpu_baseline_decode(model, cfg, args.effort, budget_s=args.cpu_seconds)
+    if cpu_base:
+        res["cpu_baseline"] = cpu_base
     model.close()  # its captured graph holds NCCL work: released before the process group
     return res
 
@@ -643,22 +668,24 @@ def cpu_baseline_prefill(model, cfg, budget_s=10.0, tokens=2):
             "sample": f"{n} prompt tokens of config 4 through the oracle's dense decode step ({cfg.n_layers} layers)"}
 
 
-def cpu_baseline_decode(model, cfg, effort, budget_s=10.0, steps=None):
-    """The oracle decode step (CPU restatement of the reference's kernels) on the same
-    weights, every host thread, continuing the same prompt."""
+def cpu_baseline_decode(model, cfg, effort, start_pos, first_tok, budget_s=10.0, steps=None, warmup=0):
+    """The oracle decode step (CPU restatement of the reference's kernels), every host thread,
+    on the same weights, continuing from the GPU model's KV cache: `warmup` untimed steps at
+    start_pos.., then timed steps (all `steps`, or as many as fit in budget_s)."""
     sys.path.insert(0, ROOT)
     from oracle import ora
+    iam = sys.modules["iam_b200"]
     threads = os.cpu_count() or 1
-    om = ora.OracleModel(cfg.as_dict(), model.export_weights())
-    prompt = prompt_tokens(cfg.vocab)
     t_pre = time.perf_counter()
-    tok = prompt[0]
-    ingest = 4  # a short prefix of the prompt keeps the sample bounded
-    for pos in range(ingest):
-        tok, _, _ = om.forward(prompt[pos], pos, effort, nthreads=threads)
+    om = ora.OracleModel(cfg.as_dict(), model.export_weights())
+    om.set_kv(np.stack([model.read_weight(iam.W_K_CACHE, l) for l in range(cfg.n_layers)]),
+              np.stack([model.read_weight(iam.W_V_CACHE, l) for l in range(cfg.n_layers)]))
+    tok, pos = first_tok, start_pos
+    for _ in range(warmup):
+        tok, _, _ = om.forward(tok, pos, effort, nthreads=threads)
+        pos += 1
     t0 = time.perf_counter()
-    done = 0
-    pos = ingest
+    done, p0 = 0, pos
     while True:
         tok, _, _ = om.forward(tok, pos, effort, nthreads=threads)
         pos += 1
@@ -667,8 +694,24 @@ def cpu_baseline_decode(model, cfg, effort, budget_s=10.0, steps=None):
         if (steps is not None and done >= steps) or (steps is None and el >= budget_s):
             break
     return {"value": round(done / el, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{done} greedy decode steps of the same 32-layer model after a {ingest}-token prefix, "
-                      f"{el:.1f} s", "seconds": round(el, 2), "setup_s": round(t0 - t_pre, 1)}
+            "sample": f"{done} greedy decode steps at positions {p0}..{pos - 1} of the same 32-layer model, "
+                      f"continuing from the GPU-built KV cache, {el:.1f} s", "seconds": round(el, 2),
+            "steps": done, "setup_s": round(t0 - t_pre, 1)}
+
+
+def prepared_decode_model(args, iam, torch, cfg, dev, tp=None):
+    """The decode model after its context: the 128-token prompt ingested token by token
+    (test_generation.cpp:202-210) or, for --kv-prefix, a random fp16 KV prefix.  Returns
+    (model, logits, first greedy token)."""
+    model = iam.Model.random(cfg, seed=0, device=dev.index, tp=tp)
+    logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+    if args.kv_prefix > 0:
+        model.fill_kv_random(args.kv_prefix, seed=1)
+        model.forward(int(prompt_tokens(cfg.vocab)[0]), args.kv_prefix - 1, args.effort, logits)
+    else:
+        for pos, tok in enumerate(prompt_tokens(cfg.vocab)):
+            model.forward(tok, pos, args.effort, logits)
+    return model, logits, int(torch.argmax(logits).item())
 
 
 def run_reference(args, rank, world):
@@ -676,19 +719,26 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     if args.workload == "decode":
+        # the GPU arm's workload: the same model, context and timed positions (the context is
+        # built on the GPU, as the GPU arm builds it; the oracle then runs W untimed and K
+        # timed steps from there)
         import torch
         iam = load_pkg()
-        cfg = mistral_cfg(iam, PROMPT_LEN + 64)
-        model = iam.Model.random(cfg, seed=0)
-        steps = max(1, min(args.steps, 12))
-        cb = cpu_baseline_decode(model, cfg, args.effort, steps=steps)
+        dev = torch.device("cuda:0")
+        torch.cuda.set_device(dev)
+        start, max_ctx, _, _, _, _ = decode_plan(args)
+        cfg = mistral_cfg(iam, max_ctx, args.layers)
+        model, _, first = prepared_decode_model(args, iam, torch, cfg, dev)
+        torch.cuda.synchronize()
+        cb = cpu_baseline_decode(model, cfg, args.effort, start, first, steps=args.steps, warmup=args.warmup)
         model.close()
         return {
-            "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": round(1e3 * cb["seconds"] / steps, 2), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "decode: config 4 on the CPU restatement (oracle) of the reference kernels",
-                       "model": "Mistral-7B (random init)", "effort": args.effort, "global_batch": 1},
+            "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": cb["steps"],
+            "warmup": args.warmup, "ms_per_step": round(1e3 * cb["seconds"] / cb["steps"], 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": decode_config(args, cfg, world),
+            "reference_path": "the CPU restatement (oracle) of the reference's decode step: bucketMul.cl, aux.cl, "
+                              "matrix.cl, transformer_layer.hpp, every host thread",
             "cpu_baseline": {"value": cb["value"], "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
                              "sample": cb["sample"]},
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

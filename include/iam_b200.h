@@ -263,6 +263,26 @@ int iam_model_reset(iam_model_t m, void* stream);
 /* MistralModel::forward (model.hpp:152-231): one decode step of `token` at `pos`; logits_dev
  * (vocab floats, may be NULL) receives the logits. */
 int iam_model_forward(iam_model_t m, int token, int pos, float effort, float* logits_dev, void* stream);
+/* Block-level entry points over one layer of a model (single-GPU models; IAM_ERR_UNSUPPORTED
+ * for a tensor-parallel rank).  Vectors are device float arrays; the KV cache is the model's
+ * own cache of that layer (iam_model_set_kv / iam_model_read_weight W_K_CACHE, W_V_CACHE), in
+ * place of the caller-owned k_cache / v_cache buffers of the reference; the reference's
+ * temporaries have no counterpart.  pos in [0, max_ctx), effort in (0, 1], else IAM_ERR_ARG.
+ *
+ * TransformerLayer::forward (transformer_layer.hpp:75-122): out = x + Attention(RMSNorm(x)),
+ * then out += FeedForward(RMSNorm(out)), with the layer's gains; writes the layer's K/V at pos
+ * and attends over [0, pos].  x_dev and out_dev hold dim floats (they may be the same array). */
+int iam_layer_forward(iam_model_t m, int layer, const float* x_dev, int pos, float effort, float* out_dev,
+                      void* stream);
+/* Attention::forward (attention.hpp:135-202): h_dev (dim floats, already normalised) through
+ * the q/k/v bucketMuls, RoPE, the fp16 K/V append at pos, attention over [0, pos] and the o
+ * bucketMul into out_dev (dim floats); no residual. */
+int iam_attention_forward(iam_model_t m, int layer, const float* h_dev, int pos, float effort, float* out_dev,
+                          void* stream);
+/* FeedForward::forward (feedforward.hpp:180): out = down(SiLU(gate(h)) * up(h)) for h_dev
+ * (dim floats, already normalised) into out_dev (dim floats); no residual. */
+int iam_feedforward_forward(iam_model_t m, int layer, const float* h_dev, float effort, float* out_dev,
+                            void* stream);
 /* Batched prefill on the dense tensor-core path: the n_tokens prompt tokens (host array) at
  * positions [start_pos, start_pos + n_tokens) go through every layer at once, with every bucket
  * row selected (the dense matmul of matrix.cl, basicMul :80-93, in place of bucketMul), and fill

@@ -1,7 +1,9 @@
 // iam_b200.hpp -- header-only C++ shim over libiamb200.so that keeps the reference's host
-// API: the class and method names of bucket_mul.hpp (BufferWrapper, ScalarFloat, BucketMul)
-// and model.hpp (MistralModel), so the reference's callers (attention.hpp, feedforward.hpp,
-// test_generation.cpp) compile against it with their OpenCL Gpu* replaced by a device id.
+// API: the class and method names of bucket_mul.hpp (BufferWrapper, ScalarFloat, BucketMul),
+// model.hpp (MistralModel) and the layer classes (TransformerLayer, Attention, FeedForward of
+// transformer_layer.hpp, attention.hpp, feedforward.hpp), so the reference's callers
+// (test_generation.cpp, per-layer drivers) compile against it with their OpenCL Gpu* replaced
+// by a device id.
 //
 // Differences from the reference, all deliberate:
 //   - buffers are CUDA device allocations (cudaMalloc) instead of cl_mem;
@@ -157,6 +159,12 @@ class MistralModel {
     MistralModel(Gpu* g, const std::string& weights_dir, const iam_model_config& c = mistral7b()) : gpu(g), cfg(c) {
         check(iam_model_load(&handle, weights_dir.c_str(), &cfg, g->device), "MistralModel");
     }
+    // A model of random N(0, 0.02) weights (no counterpart in the reference: tests, benchmarks).
+    MistralModel(Gpu* g, const iam_model_config& c, unsigned long long seed) : gpu(g), cfg(c) {
+        check(iam_model_create_random(&handle, &cfg, seed, g->device), "MistralModel (random)");
+    }
+    MistralModel(const MistralModel&) = delete;
+    MistralModel& operator=(const MistralModel&) = delete;
     ~MistralModel() { iam_model_destroy(handle); }
     // model.hpp:152-231 (no eval inside; call gpu->eval() or read the logits)
     void forward(int token_id, int pos, float effort, BufferWrapper<float>* logits_out) {
@@ -175,6 +183,68 @@ class MistralModel {
                                 &next, gpu->stream),
               "MistralModel::prefill");
         return next;
+    }
+};
+
+// transformer_layer.hpp:15-122: a decoder layer of a MistralModel (its weights, gains and KV
+// cache).  The reference's caller-owned caches and temporaries are accepted and not used: the
+// layer reads and writes the model's own KV cache of layer_idx.
+class TransformerLayer {
+   public:
+    Gpu* gpu;
+    MistralModel* model;
+    int layer;
+    TransformerLayer(Gpu* g, MistralModel* m, int layer_idx) : gpu(g), model(m), layer(layer_idx) {}
+    void forward(BufferWrapper<float>* input, int layer_idx, int pos, float effort, BufferWrapper<float>* output) {
+        check(iam_layer_forward(model->handle, layer_idx, input->buffer, pos, effort, output->buffer, gpu->stream),
+              "TransformerLayer::forward");
+    }
+    // the reference's argument list (transformer_layer.hpp:75-93)
+    void forward(BufferWrapper<float>* input, int layer_idx, int pos, float effort, BufferWrapper<float>* /*k_cache*/,
+                 BufferWrapper<float>* /*v_cache*/, BufferWrapper<float>* /*h_norm*/,
+                 BufferWrapper<float>* /*temp_xq*/, BufferWrapper<float>* /*temp_xk*/,
+                 BufferWrapper<float>* /*temp_xv*/, BufferWrapper<float>* /*temp_xk_repeated*/,
+                 BufferWrapper<float>* /*temp_xq_heads*/, BufferWrapper<float>* /*temp_xk_heads*/,
+                 BufferWrapper<float>* /*temp_scores*/, BufferWrapper<float>* /*temp_attn_output*/,
+                 BufferWrapper<float>* /*attn_out*/, BufferWrapper<float>* /*fxn*/, BufferWrapper<float>* /*ffn_out*/,
+                 BufferWrapper<float>* output) {
+        forward(input, layer_idx, pos, effort, output);
+    }
+};
+
+// attention.hpp:19-202: q/k/v bucketMuls, RoPE, the fp16 K/V append at pos, attention over
+// [0, pos] and the o bucketMul of an already normalised input; no residual.
+class Attention {
+   public:
+    Gpu* gpu;
+    MistralModel* model;
+    int layer;
+    Attention(Gpu* g, MistralModel* m, int layer_idx) : gpu(g), model(m), layer(layer_idx) {}
+    void forward(BufferWrapper<float>* input, int layer_idx, int pos, float effort, BufferWrapper<float>* output) {
+        check(iam_attention_forward(model->handle, layer_idx, input->buffer, pos, effort, output->buffer, gpu->stream),
+              "Attention::forward");
+    }
+    // the reference's argument list (attention.hpp:135-149)
+    void forward(BufferWrapper<float>* input, int layer_idx, int pos, float effort, BufferWrapper<float>* /*k_cache*/,
+                 BufferWrapper<float>* /*v_cache*/, BufferWrapper<float>* /*temp_xq*/,
+                 BufferWrapper<float>* /*temp_xk*/, BufferWrapper<float>* /*temp_xv*/,
+                 BufferWrapper<float>* /*temp_xk_repeated*/, BufferWrapper<float>* /*temp_xq_heads*/,
+                 BufferWrapper<float>* /*temp_xk_heads*/, BufferWrapper<float>* /*temp_scores*/,
+                 BufferWrapper<float>* /*temp_attn_output*/, BufferWrapper<float>* output) {
+        forward(input, layer_idx, pos, effort, output);
+    }
+};
+
+// feedforward.hpp:14-183: down(SiLU(gate(x)) * up(x)) of an already normalised input.
+class FeedForward {
+   public:
+    Gpu* gpu;
+    MistralModel* model;
+    int layer;
+    FeedForward(Gpu* g, MistralModel* m, int layer_idx) : gpu(g), model(m), layer(layer_idx) {}
+    void forward(BufferWrapper<float>* input, BufferWrapper<float>* output, float effort = 1.0f) {
+        check(iam_feedforward_forward(model->handle, layer, input->buffer, effort, output->buffer, gpu->stream),
+              "FeedForward::forward");
     }
 };
 

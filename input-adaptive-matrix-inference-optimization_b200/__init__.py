@@ -255,6 +255,9 @@ _SIGNATURES.update({
     "iam_model_destroy": [_vp],
     "iam_model_reset": [_vp, _vp],
     "iam_model_forward": [_vp, _i32, _i32, _f32, _vp, _vp],
+    "iam_layer_forward": [_vp, _i32, _vp, _i32, _f32, _vp, _vp],
+    "iam_attention_forward": [_vp, _i32, _vp, _i32, _f32, _vp, _vp],
+    "iam_feedforward_forward": [_vp, _i32, _vp, _f32, _vp, _vp],
     "iam_model_prefill": [_vp, _vp, _i32, _i32, _vp, _vp, _vp],
     "iam_model_generate": [_vp, _i32, _i32, _i32, _f32, _vp, _vp],
     "iam_model_set_kv": [_vp, _i32, _vp, _vp, _i32, _vp],
@@ -365,6 +368,21 @@ class Model:
 
     def forward(self, token, pos, effort, logits=None, stream=None):
         check(self.lib.iam_model_forward(self.h, token, pos, effort, _ptr(logits), _stream(stream)))
+
+    def layer_forward(self, layer, x, pos, effort, out, stream=None):
+        """iam_layer_forward (TransformerLayer::forward): out = the decoder layer applied to x
+        (device float tensors of dim) at pos, over the model's KV cache of that layer."""
+        check(self.lib.iam_layer_forward(self.h, layer, _ptr(x), pos, effort, _ptr(out), _stream(stream)))
+
+    def attention_forward(self, layer, h, pos, effort, out, stream=None):
+        """iam_attention_forward (Attention::forward): q/k/v, attention at pos and o of a
+        normalised input, no residual."""
+        check(self.lib.iam_attention_forward(self.h, layer, _ptr(h), pos, effort, _ptr(out), _stream(stream)))
+
+    def feedforward_forward(self, layer, h, effort, out, stream=None):
+        """iam_feedforward_forward (FeedForward::forward): down(SiLU(gate(h)) * up(h)), no
+        residual."""
+        check(self.lib.iam_feedforward_forward(self.h, layer, _ptr(h), effort, _ptr(out), _stream(stream)))
 
     def prefill(self, tokens, start_pos=0, logits=None, stream=None):
         """iam_model_prefill: the prompt through the dense tensor-core path in one pass; returns

@@ -92,15 +92,252 @@ IAM_DEV void load_halves(const uint16_t* p, float* o) {
     }
 }
 
+// 16-byte global -> shared copy that does not wait (cp.async; completed by cp_async_wait_all).
+IAM_DEV void cp_async16(void* dst_smem, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst_smem)),
+                 "l"(__cvta_generic_to_global(src))
+                 : "memory");
+}
+IAM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// mma.sync m16n8k16, f16 x f16 -> f32 (fragments as the PTX ISA lays them out: A rows
+// g = lane / 4 and g + 8, columns 2 * (lane % 4) + {0, 1} and + 8; B rows 2 * (lane % 4) + {0, 1}
+// and + 8, column g; C rows g and g + 8, columns 2 * (lane % 4) + {0, 1}).
+IAM_DEV void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+IAM_DEV void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+IAM_DEV void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+IAM_DEV uint32_t pack_h2(float a, float b) {  // a in the low half, both rounded to fp16
+    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+// x = hi + lo with hi = fp16(x): the low part of a two-term fp16 split (exact in fp32)
+IAM_DEV float split_lo(float x) { return __fsub_rn(x, __half2float(__float2half_rn(x))); }
+
+// Long-context layout of one chunk [t0, t1) on the tensor cores (GQ <= 4 query heads per KV
+// head, head_dim 64 or 128): warp w takes the 32-token groups t0 + 32w, t0 + 32(w + 8), ...
+// For a group, the K rows go to the warp's shared tile (cp.async, 16-byte pieces XOR-swizzled
+// by the row's low 3 bits so that ldmatrix reads are conflict-free) and the scores are
+// S[32 tokens][8] = K . Q^T with the queries split in two fp16 terms (columns 0..3 the high
+// parts, 4..7 the low parts of the GQ heads, summed after the product): the fp16 K values times
+// the two-term queries, accumulated in fp32, equal the fp32 dot product to about 2^-22.  The
+// group's max and sum per head are warp reductions, the probabilities are split the same way
+// (A rows 0..3 high, 4..7 low), the V rows replace the K rows in the tile, and O += P . V on
+// the tensor cores, the two halves summed at the end.  The running max, sum and p.V per head
+// land in cm/cl/co slot `warp` (slots 0..7).  The new token pos is patched into the tile from
+// knew/vnew (its fp16-rounded K/V), never read from the cache row this launch writes.
+template <int GQ, int VD>
+IAM_DEV void attn_mma_chunk(const float* __restrict__ qr, const float* __restrict__ knew,
+                            const float* __restrict__ vnew, const uint16_t* __restrict__ kc,
+                            const uint16_t* __restrict__ vc, uint16_t* tiles, int t0, int t1, int pos, float* cm,
+                            float* cl, float* co) {
+    constexpr int HD = 16 * VD;
+    constexpr int KS = HD / 16;  // k-steps of the scores
+    constexpr int NT = HD / 8;   // n-tiles of p.V
+    constexpr int CPR = HD / 8;  // 16-byte pieces per row
+    constexpr int NW = kAttnThreads / 32;
+    static_assert(GQ <= 4 && (HD == 64 || HD == 128), "tensor-core attention: GQ <= 4, head_dim 64 or 128");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+    char* tile = reinterpret_cast<char*>(tiles + (size_t)warp * 32 * HD);  // 32 rows of HD fp16
+    const uint32_t tile_s = (uint32_t)__cvta_generic_to_shared(tile);
+    __shared__ __align__(16) float ps_all[kAttnThreads / 32][32 * 4];
+    float* ps = ps_all[warp];  // the group's probabilities [token][4 heads]
+    auto off = [](int r, int c) { return r * (HD * 2) + ((c ^ (r & 7)) << 4); };
+    auto load_rows = [&](const uint16_t* src, int base, int nv) {
+#pragma unroll
+        for (int i = 0; i < CPR; ++i) {
+            const int f = i * 32 + lane, r = f / CPR, c = f % CPR;
+            if (r < nv) cp_async16(tile + off(r, c), src + (size_t)(base + r) * HD + c * 8);
+            else *reinterpret_cast<uint4*>(tile + off(r, c)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        cp_async_wait_all();
+        __syncwarp();
+    };
+    auto patch_row = [&](const float* vals, int r) {  // the new token's row, fp16 pairs
+        for (int d = 2 * lane; d < HD; d += 64)
+            *reinterpret_cast<uint32_t*>(tile + off(r, d >> 3) + (d & 7) * 2) = pack_h2(vals[d], vals[d + 1]);
+        __syncwarp();
+    };
+
+    // Q^T fragments: column g is head g & 3, its high part (g < 4) or its low part
+    uint32_t bq[KS][2];
+    {
+        const int j = g & 3;
+        const bool lo = g >= 4;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int d0 = 16 * ks + 2 * tig;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (j < GQ) {
+                v[0] = qr[j * HD + d0];
+                v[1] = qr[j * HD + d0 + 1];
+                v[2] = qr[j * HD + d0 + 8];
+                v[3] = qr[j * HD + d0 + 9];
+            }
+            if (lo)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[e] = split_lo(v[e]);
+            bq[ks][0] = pack_h2(v[0], v[1]);
+            bq[ks][1] = pack_h2(v[2], v[3]);
+        }
+    }
+    const float scale_div = sqrtf((float)HD);
+    // this lane's two heads in the softmax: hp and hp + 1
+    const int hp = 2 * (tig & 1);
+    float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.0f, 0.0f};
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[nt][e] = 0.0f;
+
+    for (int base = t0 + warp * 32; base < t1; base += NW * 32) {
+        const int nv = min(32, t1 - base);
+        const bool has_pos = pos >= base && pos < base + nv;
+        __syncwarp();  // the previous group's tile and probabilities are consumed
+        load_rows(kc, base, nv);
+        if (has_pos) patch_row(knew, pos - base);
+        float sc[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[mt][e] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t a[4];
+                ldsm_x4(a, tile_s + off(mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * ks + (lane >> 4)));
+                mma_16816(sc[mt], a, bq[ks][0], bq[ks][1]);
+            }
+        }
+        // high + low columns (lanes tig and tig ^ 2), scale, mask: token of sc[mt][e] is
+        // 16 mt + g + 8 (e >> 1), head hp + (e & 1)
+        float pr[2][4];  // [head][k]: tokens g, g + 8, 16 + g, 24 + g
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float full = sc[mt][e] + __shfl_xor_sync(0xffffffffu, sc[mt][e], 2);
+                const int k = 2 * mt + (e >> 1), tok = 16 * mt + g + 8 * (e >> 1);
+                pr[e & 1][k] = tok < nv ? __fdiv_rn(full, scale_div) : -INFINITY;
+            }
+        float rsc[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(fmaxf(pr[h][0], pr[h][1]), fmaxf(pr[h][2], pr[h][3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float nm = fmaxf(mrun[h], mx);  // token 0 of the group is in range
+            rsc[h] = expf(mrun[h] - nm);
+            float sum = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                pr[h][k] = pr[h][k] == -INFINITY ? 0.0f : expf(pr[h][k] - nm);
+                sum += pr[h][k];
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            lrun[h] = fmaf(lrun[h], rsc[h], sum);
+            mrun[h] = nm;
+        }
+        if (tig < 2)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int tok = 16 * (k >> 1) + g + 8 * (k & 1);
+                *reinterpret_cast<float2*>(ps + tok * 4 + hp) = make_float2(pr[0][k], pr[1][k]);
+            }
+        {   // rescale the O rows: row g holds head g & 3 (its high or low part)
+            const int src = (g & 3) >> 1;  // a lane that owns head g & 3 in the softmax
+            const float r0 = __shfl_sync(0xffffffffu, rsc[0], src), r1 = __shfl_sync(0xffffffffu, rsc[1], src);
+            const float rr = (g & 1) ? r1 : r0;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                o[nt][0] *= rr;
+                o[nt][1] *= rr;
+            }
+        }
+        load_rows(vc, base, nv);  // the K fragments are consumed: V rows into the same tile
+        if (has_pos) patch_row(vnew, pos - base);
+        // A = P: row g is head g & 3, high part (g < 4) or low part; rows 8..15 zero
+        uint32_t ap[2][4];
+        {
+            const int j = g & 3;
+            const bool lo = g >= 4;
+#pragma unroll
+            for (int kt = 0; kt < 2; ++kt) {
+                const int ta = 16 * kt + 2 * tig, tb = ta + 8;
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (j < GQ) {
+                    v[0] = ps[ta * 4 + j];
+                    v[1] = ps[(ta + 1) * 4 + j];
+                    v[2] = ps[tb * 4 + j];
+                    v[3] = ps[(tb + 1) * 4 + j];
+                }
+                if (lo)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[e] = split_lo(v[e]);
+                ap[kt][0] = pack_h2(v[0], v[1]);
+                ap[kt][1] = 0u;
+                ap[kt][2] = pack_h2(v[2], v[3]);
+                ap[kt][3] = 0u;
+            }
+        }
+#pragma unroll
+        for (int kt = 0; kt < 2; ++kt)
+#pragma unroll
+            for (int n2 = 0; n2 < NT / 2; ++n2) {
+                uint32_t bv[4];
+                ldsm_x4_t(bv, tile_s + off(16 * kt + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * n2 + (lane >> 4)));
+                mma_16816(o[2 * n2], ap[kt], bv[0], bv[1]);
+                mma_16816(o[2 * n2 + 1], ap[kt], bv[2], bv[3]);
+            }
+    }
+    // high + low rows (lanes g and g + 4 = lane ^ 16); lanes g < GQ hold head g
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const float v = o[nt][e] + __shfl_xor_sync(0xffffffffu, o[nt][e], 16);
+            if (g < GQ) co[(warp * GQ + g) * HD + 8 * nt + 2 * tig + e] = v;
+        }
+    if (g == 0 && tig < 2)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (hp + h < GQ) {
+                cm[warp * GQ + hp + h] = mrun[h];
+                cl[warp * GQ + hp + h] = lrun[h];
+            }
+}
+
 // grid = n_kv_heads * n_split, block = kAttnThreads (16 half-warps).  Single pass over the
 // context (flash-decoding): the tokens [0, pos] are cut into `active` chunks of at least
-// p.min_chunk tokens; CTA (kvh, s < active) runs chunk s for the GQ query heads of KV head kvh.
-// Each half-warp takes kAttnTU tokens at a time (K and V loads issued together, 16 lanes x
-// VD dimensions), reduces the GQ dot products over its 16 lanes, and keeps an online softmax
-// (running max, sum and p.V per head) in registers.  The half-warps are combined in shared
-// memory; with more than one chunk the last CTA of the KV head combines the chunks in chunk
-// order.  The new token's K/V (RoPE'd, rounded through fp16) are appended by the CTA whose
-// chunk holds pos and used from shared memory for that token.
+// p.min_chunk tokens (n_split follows from the model's KV heads, so the chunks of a context do
+// not depend on the tensor-parallel degree); CTA (kvh, s < active) runs chunk s for the GQ
+// query heads of KV head kvh.  Two layouts, chosen from the context length on the device (one
+// captured step serves every position):
+//   * the tensor-core layout (attn_mma_chunk) for contexts of at most lane_short_max tokens,
+//     in one chunk per KV head, and of at least lane_min_ctx tokens;
+//   * the half-warp layout in between: each half-warp takes kAttnTU tokens at a time (K and V
+//     loads issued together, 16 lanes x VD dimensions), reduces the GQ dot products over its
+//     16 lanes, and keeps an online softmax (running max, sum and p.V per head) in registers.
+// The warps' or half-warps' states are combined in shared memory in slot order; with more than
+// one chunk the last CTA of the KV head combines the chunks in chunk order.  The new token's
+// K/V (RoPE'd, rounded through fp16) are appended by the CTA whose chunk holds pos and used
+// from shared memory for that token.
 template <int GQ, int VD>
 __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
@@ -117,8 +354,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
         pos = p.max_ctx - 1;
     }
     const int n_tok = pos + 1;
+    // the layout by context length: the tensor-core one for a short context (in one chunk per
+    // KV head: no combine across CTAs) and for a long one, the half-warp one in between
+    const bool tc_layout = n_tok <= p.lane_short_max || n_tok >= p.lane_min_ctx;
     int chunk = (n_tok + p.n_split - 1) / p.n_split;
     if (chunk < p.min_chunk) chunk = p.min_chunk;
+    if (tc_layout && n_tok <= p.lane_short_max) chunk = n_tok;
     const int active = (n_tok + chunk - 1) / chunk;
     if (s >= active) return;  // takes no part in the combine
     const int t0 = s * chunk, t1 = min(t0 + chunk, n_tok);
@@ -128,8 +369,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
     float* vnew = knew + HD;        // [HD] v at pos, rounded through fp16
     float* cm = vnew + HD;          // [NH][GQ] half-warp running max
     float* cl = cm + NH * GQ;       // [NH][GQ] half-warp running sum
-    float* co = cl + NH * GQ;       // [NH][GQ][HD] half-warp p.V
-    float* wgt = co + NH * GQ * HD; // [GQ][n_split] chunk weights (combine)
+    float* wgt = cl + NH * GQ;      // [GQ][n_split] chunk weights (combine)
+    float* co = wgt + ((GQ * p.n_split + 3) & ~3);  // [NH][GQ][HD] half-warp p.V, 16-byte aligned
+    // [8 warps][32][HD] fp16 K, then V, rows of the long-context layout; co and vt together
+    // are the staging area of the chunk combine
+    uint16_t* vt = reinterpret_cast<uint16_t*>(co + NH * GQ * HD);
+    const int nslots = tc_layout ? kAttnThreads / 32 : NH;  // filled cm/cl/co slots
     const float* cs = p.rope + (size_t)pos * HD;
 
     for (int e = tid; e < GQ * HD; e += kAttnThreads) {
@@ -149,6 +394,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
             vc[(size_t)pos * HD + d] = __half_as_ushort(__float2half_rn(vnew[d]));
         }
     }
+    if (tc_layout) {  // (the host enables the layout only for the shapes it takes)
+        if constexpr (GQ <= 4 && (VD == 4 || VD == 8))
+            attn_mma_chunk<GQ, VD>(qr, knew, vnew, kc, vc, vt, t0, t1, pos, cm, cl, co);
+    } else {
     float qv[GQ][VD];
 #pragma unroll
     for (int j = 0; j < GQ; ++j)
@@ -167,7 +416,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
     // warp-uniform trip count (the dot-product shuffles use the full warp); each half-warp
     // takes TU tokens of its warp's group of 2*TU, masking those past the chunk.  The K/V of
     // the next group are loaded before the current group is scored (software pipeline).
-    const int warp = tid >> 5, hwin = (tid >> 4) & 1;
+    const int warp = tid >> 5, hwin = (tid >> 4) & 1;  // (in the half-warp path)
     constexpr int NWT = kAttnThreads / 32;
     // K/V travel as raw fp16 words (VD/2 per token) and are widened at use
     constexpr int VW = VD / 2;
@@ -264,22 +513,32 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
 #pragma unroll
         for (int e = 0; e < VD; ++e) co[(hw * GQ + j) * HD + hl * VD + e] = o[j][e];
     }
+    }
     __syncthreads();
-    // this chunk: M = max over half-warps, L and O rescaled to M (fixed half-warp order)
+    // this chunk: M = max over the slots, L and O rescaled to M (fixed slot order); the slot
+    // weights exp(m_h - M) are computed once per query head and kept in cm
+    __shared__ float sM[8], sL[8];
+    if (tid < GQ) {
+        const int j = tid;
+        float M = -INFINITY;
+        for (int h = 0; h < nslots; ++h) M = fmaxf(M, cm[h * GQ + j]);
+        float L = 0.0f;
+        for (int h = 0; h < nslots; ++h) {
+            const float mh = cm[h * GQ + j];
+            const float w = mh == -INFINITY ? 0.0f : expf(mh - M);
+            cm[h * GQ + j] = w;
+            L = fmaf(w, cl[h * GQ + j], L);
+        }
+        sM[j] = M;
+        sL[j] = L;
+    }
+    __syncthreads();
     float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (HD + 2);
     for (int idx = tid; idx < GQ * HD; idx += kAttnThreads) {
         const int j = idx / HD, d = idx % HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < NH; ++h) M = fmaxf(M, cm[h * GQ + j]);
-        float L = 0.0f, O = 0.0f;
-#pragma unroll
-        for (int h = 0; h < NH; ++h) {
-            const float mh = cm[h * GQ + j];
-            const float w = mh == -INFINITY ? 0.0f : expf(mh - M);
-            L = fmaf(w, cl[h * GQ + j], L);
-            O = fmaf(w, co[(h * GQ + j) * HD + d], O);
-        }
+        const float M = sM[j], L = sL[j];
+        float O = 0.0f;
+        for (int h = 0; h < nslots; ++h) O = fmaf(cm[h * GQ + j], co[(h * GQ + j) * HD + d], O);
         if (active == 1) {
             p.out[(size_t)(kvh * GQ + j) * HD + d] = __fdiv_rn(O, L);
         } else {
@@ -302,32 +561,46 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
     if (!last) return;
     __threadfence();
     const float* base = p.part + (size_t)kvh * p.n_split * GQ * (HD + 2);
-    const int lane = tid & 31;
+    const int lane = tid & 31, warp = tid >> 5;
     constexpr int NWA = kAttnThreads / 32;
-    for (int j = warp; j < GQ; j += NWA) {
-        float M = -INFINITY;
-        for (int r = lane; r < active; r += 32) M = fmaxf(M, __ldcg(base + ((size_t)r * GQ + j) * (HD + 2)));
+    // every chunk's (M, L, O) into shared memory at once (co and vt are free now), when they fit
+    constexpr int PER = GQ * (HD + 2);  // floats per chunk
+    const bool staged = (PER % 4 == 0) && ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) &&
+                        (size_t)active * PER <= (size_t)NH * GQ * HD + (size_t)(kAttnThreads / 32) * 32 * HD / 2;
+    if (staged) {
+        for (int f = tid; f < active * PER / 4; f += kAttnThreads) cp_async16(co + 4 * f, base + 4 * f);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        cp_async_wait_all();
+        __syncthreads();
+    }
+    // (two copies of the loops, so that the staged one never touches global memory)
+    auto combine = [&](auto part_at) {
+        for (int j = warp; j < GQ; j += NWA) {
+            float M = -INFINITY;
+            for (int r = lane; r < active; r += 32) M = fmaxf(M, part_at(r * PER + j * (HD + 2)));
 #pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-        float L = 0.0f;
-        for (int r = lane; r < active; r += 32) {
-            const float* st = base + ((size_t)r * GQ + j) * (HD + 2);
-            const float w = expf(__ldcg(st) - M);
-            wgt[j * p.n_split + r] = w;
-            L = fmaf(w, __ldcg(st + 1), L);
+            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+            float L = 0.0f;
+            for (int r = lane; r < active; r += 32) {
+                const float w = expf(part_at(r * PER + j * (HD + 2)) - M);
+                wgt[j * p.n_split + r] = w;
+                L = fmaf(w, part_at(r * PER + j * (HD + 2) + 1), L);
+            }
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+            for (int r = lane; r < active; r += 32) wgt[j * p.n_split + r] = __fdiv_rn(wgt[j * p.n_split + r], L);
         }
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
-        for (int r = lane; r < active; r += 32) wgt[j * p.n_split + r] = __fdiv_rn(wgt[j * p.n_split + r], L);
-    }
-    __syncthreads();
-    for (int e = tid; e < GQ * HD; e += kAttnThreads) {
-        const int j = e / HD, d = e % HD;
-        float O = 0.0f;
+        __syncthreads();
+        for (int e = tid; e < GQ * HD; e += kAttnThreads) {
+            const int j = e / HD, d = e % HD;
+            float O = 0.0f;
 #pragma unroll 8
-        for (int r = 0; r < active; ++r) O = fmaf(wgt[j * p.n_split + r], __ldcg(base + ((size_t)r * GQ + j) * (HD + 2) + 2 + d), O);
-        p.out[(size_t)(kvh * GQ + j) * HD + d] = O;
-    }
+            for (int r = 0; r < active; ++r) O = fmaf(wgt[j * p.n_split + r], part_at(r * PER + j * (HD + 2) + 2 + d), O);
+            p.out[(size_t)(kvh * GQ + j) * HD + d] = O;
+        }
+    };
+    if (staged) combine([&](int i) { return co[i]; });
+    else combine([&](int i) { return __ldcg(base + i); });
     if (tid == 0) p.ctr[kvh] = 0;  // ready for the next launch
 }
 
@@ -430,7 +703,8 @@ int launch_embed(const uint16_t* embed, int dim, int token, const unsigned long 
 
 size_t attention_smem(const AttnParams& p, int gq) {
     const size_t hd = p.head_dim, nh = kAttnThreads / 16;
-    return sizeof(float) * ((size_t)gq * hd + 2 * hd + 2 * nh * gq + nh * gq * hd + (size_t)gq * p.n_split);
+    return sizeof(float) * ((size_t)gq * hd + 2 * hd + 2 * nh * gq + nh * gq * hd + (((size_t)gq * p.n_split + 3) & ~3)) +
+           sizeof(uint16_t) * (kAttnThreads / 32) * 32 * hd;
 }
 
 template <int GQ, int VD>

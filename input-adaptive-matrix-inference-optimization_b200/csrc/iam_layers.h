@@ -9,6 +9,8 @@ namespace iam {
 constexpr int kAttnThreads = 256;   // 16 half-warps
 constexpr int kAttnTU = 2;          // tokens per half-warp in flight
 constexpr int kAttnMinChunk = 32;   // context tokens per CTA at least (default of AttnParams::min_chunk)
+constexpr int kAttnLaneMinCtx = 2048;   // default of AttnParams::lane_min_ctx
+constexpr int kAttnLaneShortMax = 256;  // default of AttnParams::lane_short_max (8 warps x 32 tokens)
 constexpr int kHeadThreads = 256;
 
 struct AttnParams {
@@ -25,6 +27,8 @@ struct AttnParams {
     int* ctr;              // [n_kv_heads] zero-initialised, self-resetting
     int n_kv_heads, head_dim, max_ctx, n_split;
     int min_chunk;         // context tokens per CTA at least
+    int lane_min_ctx;      // contexts of this many tokens or more take the tensor-core layout,
+    int lane_short_max;    // and so do contexts of at most this many (in one chunk per KV head)
 };
 
 struct LMHeadParams {

@@ -8,6 +8,7 @@
 //   down bucketMul (SiLU*up fused, +residual)] -> LM head (final RMSNorm*gain, argmax).
 // Position and token live in device memory, so a step can be captured once as a CUDA graph
 // and replayed for every generated token without host round trips.
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -201,7 +202,8 @@ struct iam_model_s {
     // attention scratch
     float* att_part = nullptr;
     int* att_ctr = nullptr;
-    int att_split = 32, att_min_chunk = kAttnMinChunk;
+    int att_split = 32, att_min_chunk = kAttnMinChunk, att_lane_min = kAttnLaneMinCtx,
+        att_lane_short = kAttnLaneShortMax;
     // launch plans for the current effort
     std::vector<BMBatch> plans;   // 4 per layer (cluster-split kernel, IAM_BM_KERNEL=split)
     std::vector<BGBatch> gplans;  // 4 per layer (range kernel, the default)
@@ -348,16 +350,24 @@ int alloc_runtime(iam_model_s* m) {
     if ((rc = dalloc(m, &m->bm_bar, 4))) return rc;
     IAM_CUDA_TRY(cudaMemset(m->bm_bar, 0, 4 * sizeof(unsigned)));
     const int gq = c.n_heads / c.n_kv_heads;
-    // chunks per KV head: about 2 CTAs per SM at long context (short contexts use fewer: a
-    // chunk holds at least att_min_chunk tokens; 4 per SM and 4 tokens per half-warp in flight
-    // measured slower at 8192 tokens)
-    m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, m->n_kv_local)));
+    // chunks per KV head: about 2 CTAs per SM at long context with every KV head on one GPU
+    // (short contexts use fewer: a chunk holds at least att_min_chunk tokens; 4 per SM and 4
+    // tokens per half-warp in flight measured slower at 8192 tokens).  The count follows from
+    // the model's KV heads, not this rank's, so a context is cut into the same chunks, and
+    // summed in the same order, at every tensor-parallel degree.
+    m->att_split = std::max(1, std::min(64, 2 * m->sm_count / std::max(1, c.n_kv_heads)));
     if (const char* v = getenv("IAM_ATTN_MIN_CHUNK")) m->att_min_chunk = std::max(1, atoi(v));
+    if (const char* v = getenv("IAM_ATTN_LANE_MIN_CTX")) m->att_lane_min = std::max(1, atoi(v));
+    if (const char* v = getenv("IAM_ATTN_LANE_SHORT_MAX")) m->att_lane_short = std::max(0, atoi(v));
+    if (gq > 4 || (hd != 64 && hd != 128)) {  // outside the tensor-core layout's shapes
+        m->att_lane_min = INT_MAX;
+        m->att_lane_short = 0;
+    }
     {
         AttnParams probe{};
         probe.head_dim = hd;
         probe.n_split = m->att_split;
-        if (attention_smem(probe, gq) > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "model: max_ctx too large for attention");
+        if (attention_smem(probe, gq) > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "model: head_dim too large for attention");
     }
     if ((rc = dalloc(m, &m->att_part, (size_t)m->n_kv_local * m->att_split * gq * (hd + 2))) ||
         (rc = dalloc(m, &m->att_ctr, m->n_kv_local)))
@@ -783,6 +793,121 @@ int hook(StepHooks* h, int kind, cudaStream_t s) {
     return IAM_OK;
 }
 
+// Decode attention of layer l over the layer's KV cache at the model's device position:
+// q, k, v from the q/k/v bucketMuls, output into this rank's heads of m->att.
+AttnParams attn_params(iam_model_s* m, int l) {
+    const iam_model_config& c = m->cfg;
+    AttnParams ap{};
+    ap.q = m->q;
+    ap.k = m->k;
+    ap.v = m->v;
+    const size_t layer_kv = (size_t)m->n_kv_local * c.max_ctx * c.head_dim;
+    ap.k_cache = m->k_cache + (size_t)l * layer_kv;
+    ap.v_cache = m->v_cache + (size_t)l * layer_kv;
+    ap.rope = m->rope;
+    ap.pos_dev = m->pos;
+    ap.pos_err = m->pos_err;
+    ap.out = m->att + (size_t)m->tp_rank * m->n_heads_local * c.head_dim;
+    ap.part = m->att_part;
+    ap.ctr = m->att_ctr;
+    ap.n_kv_heads = m->n_kv_local;
+    ap.head_dim = c.head_dim;
+    ap.max_ctx = c.max_ctx;
+    ap.n_split = m->att_split;
+    ap.min_chunk = m->att_min_chunk;
+    ap.lane_min_ctx = m->att_lane_min;
+    ap.lane_short_max = m->att_lane_short;
+    return ap;
+}
+
+// Launch bi (0 q/k/v, 1 o, 2 gate/up, 3 down) of layer l for the block-level entry points:
+// x read as given (no fused RMSNorm), no residual added, o and down written to `out`.
+int launch_plain_plan(iam_model_s* m, int l, int bi, const float* x, float* out, cudaStream_t s) {
+    BGBatch b = m->gplans[(size_t)l * 4 + bi];
+    for (int i = 0; i < b.nprob; ++i) {
+        BGProblem& p = b.p[i];
+        if (bi == 0 || bi == 2) {
+            p.x = x;
+            p.gain = nullptr;
+        }
+        if (bi == 1 || bi == 3) {
+            p.residual = nullptr;
+            p.out = out;
+        }
+        p.x_capture = nullptr;
+        p.cutoff_out = nullptr;
+    }
+    if (bi == 0 || bi == 2) b.xmode = kXPlain;
+    b.pdl = 0;
+    bg_choose_shape(b);
+    return bg_launch(b, s);
+}
+
+// The launches of decoder layer l (transformer_layer.hpp:75-122): RMSNorm-fused q/k/v
+// bucketMuls, attention with the RoPE'd fp16 KV append, o (+ the residual), RMSNorm-fused
+// gate/up, SiLU-fused down (+ the residual), with the tensor-parallel exchanges between them.
+// Reads m->x at the model's device position; leaves the layer's output in m->x.
+int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk) {
+    const iam_model_config& c = m->cfg;
+    const int gq = c.n_heads / c.n_kv_heads;
+    int rc = IAM_OK;
+    if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
+    if ((rc = launch_plan(m, l * 4 + 0, pdl, s))) return rc;
+    if (m->capture) {  // q, k, v of this layer (before attention rotates them)
+        const CaptureLayout CL = capture_layout(c);
+        float* rec = m->capture + (size_t)l * CL.total;
+        const size_t qn = (size_t)c.n_heads * c.head_dim, kvn = (size_t)c.n_kv_heads * c.head_dim;
+        IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.q, m->q, qn * 4, cudaMemcpyDeviceToDevice, s));
+        IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.k, m->k, kvn * 4, cudaMemcpyDeviceToDevice, s));
+        IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.v, m->v, kvn * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    const AttnParams ap = attn_params(m, l);
+    if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
+    if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
+    for (int b = 1; b < 4; ++b) {
+        if (m->tp_world > 1 && m->tp_p2p) {  // the exchange in front of launch b (NVLink one-shot)
+            if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+            if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
+            else if (b == 2) rc = tp_allreduce_sum(m->win, woff(m, m->x1), c.dim, s, pdl);
+            else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
+            if (rc) return rc;
+        } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
+            if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+            if (b == 1) rc = nccl_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
+            else if (b == 2) rc = nccl_allreduce_sum(m, m->x1, c.dim, s);
+            else {
+                if ((rc = nccl_done(m, ncclGroupStart(), "ncclGroupStart"))) return rc;
+                ncclAllGather(m->g + (size_t)m->tp_rank * m->ffn_local, m->g, m->ffn_local, ncclFloat, m->comm, s);
+                ncclAllGather(m->u + (size_t)m->tp_rank * m->ffn_local, m->u, m->ffn_local, ncclFloat, m->comm, s);
+                rc = nccl_done(m, ncclGroupEnd(), "ncclAllGather (gate, up)");
+            }
+            if (rc) return rc;
+        }
+        if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
+        if (m->capture && b != 2)  // the residual this launch adds (o: x, down: x1)
+            IAM_CUDA_TRY(cudaMemcpyAsync(m->capture + (size_t)l * capture_layout(c).total +
+                                             (b == 1 ? capture_layout(c).reso : capture_layout(c).resd),
+                                         b == 1 ? m->x : m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+        if ((rc = launch_plan(m, l * 4 + b, pdl, s))) return rc;
+        if (m->capture) {  // this launch's outputs
+            const CaptureLayout CL = capture_layout(c);
+            float* rec = m->capture + (size_t)l * CL.total;
+            if (b == 1) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outo, m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+            if (b == 2) {
+                IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.g, m->g, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
+                IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.u, m->u, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
+            }
+            if (b == 3) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outd, m->x, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    if (m->tp_world > 1) {
+        if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+        rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
+        if (rc) return rc;
+    }
+    return IAM_OK;
+}
+
 // token: token_arg (>= 0), or the previous argmax when token_arg < 0.  pos: pos_arg (>= 0)
 // is written to the device first, else the device value is used.
 int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float* logits, cudaStream_t s,
@@ -798,80 +923,8 @@ int enqueue_step(iam_model_s* m, int token_arg, int pos_arg, float effort, float
     if ((rc = launch_embed(m->embed, c.dim, token_arg, token_arg < 0 ? m->key : nullptr, nullptr, m->x, m->key,
                            m->token_used, s, pdl)))
         return rc;
-    const int gq = c.n_heads / c.n_kv_heads;
-    for (int l = 0; l < c.n_layers; ++l) {
-        if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
-        if ((rc = launch_plan(m, l * 4 + 0, pdl, s))) return rc;
-        if (m->capture) {  // q, k, v of this layer (before attention rotates them)
-            const CaptureLayout CL = capture_layout(c);
-            float* rec = m->capture + (size_t)l * CL.total;
-            const size_t qn = (size_t)c.n_heads * c.head_dim, kvn = (size_t)c.n_kv_heads * c.head_dim;
-            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.q, m->q, qn * 4, cudaMemcpyDeviceToDevice, s));
-            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.k, m->k, kvn * 4, cudaMemcpyDeviceToDevice, s));
-            IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.v, m->v, kvn * 4, cudaMemcpyDeviceToDevice, s));
-        }
-        AttnParams ap{};
-        ap.q = m->q;
-        ap.k = m->k;
-        ap.v = m->v;
-        const size_t layer_kv = (size_t)m->n_kv_local * c.max_ctx * c.head_dim;
-        ap.k_cache = m->k_cache + (size_t)l * layer_kv;
-        ap.v_cache = m->v_cache + (size_t)l * layer_kv;
-        ap.rope = m->rope;
-        ap.pos_dev = m->pos;
-        ap.pos_err = m->pos_err;
-        ap.out = m->att + (size_t)m->tp_rank * m->n_heads_local * c.head_dim;
-        ap.part = m->att_part;
-        ap.ctr = m->att_ctr;
-        ap.n_kv_heads = m->n_kv_local;
-        ap.head_dim = c.head_dim;
-        ap.max_ctx = c.max_ctx;
-        ap.n_split = m->att_split;
-        ap.min_chunk = m->att_min_chunk;
-        if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
-        if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
-        for (int b = 1; b < 4; ++b) {
-            if (m->tp_world > 1 && m->tp_p2p) {  // the exchange in front of launch b (NVLink one-shot)
-                if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-                if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
-                else if (b == 2) rc = tp_allreduce_sum(m->win, woff(m, m->x1), c.dim, s, pdl);
-                else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
-                if (rc) return rc;
-            } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
-                if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-                if (b == 1) rc = nccl_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
-                else if (b == 2) rc = nccl_allreduce_sum(m, m->x1, c.dim, s);
-                else {
-                    if ((rc = nccl_done(m, ncclGroupStart(), "ncclGroupStart"))) return rc;
-                    ncclAllGather(m->g + (size_t)m->tp_rank * m->ffn_local, m->g, m->ffn_local, ncclFloat, m->comm, s);
-                    ncclAllGather(m->u + (size_t)m->tp_rank * m->ffn_local, m->u, m->ffn_local, ncclFloat, m->comm, s);
-                    rc = nccl_done(m, ncclGroupEnd(), "ncclAllGather (gate, up)");
-                }
-                if (rc) return rc;
-            }
-            if ((rc = hook(hk, IAM_KERNEL_BUCKETMUL, s))) return rc;
-            if (m->capture && b != 2)  // the residual this launch adds (o: x, down: x1)
-                IAM_CUDA_TRY(cudaMemcpyAsync(m->capture + (size_t)l * capture_layout(c).total +
-                                                 (b == 1 ? capture_layout(c).reso : capture_layout(c).resd),
-                                             b == 1 ? m->x : m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
-            if ((rc = launch_plan(m, l * 4 + b, pdl, s))) return rc;
-            if (m->capture) {  // this launch's outputs
-                const CaptureLayout CL = capture_layout(c);
-                float* rec = m->capture + (size_t)l * CL.total;
-                if (b == 1) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outo, m->x1, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
-                if (b == 2) {
-                    IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.g, m->g, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
-                    IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.u, m->u, (size_t)c.ffn_dim * 4, cudaMemcpyDeviceToDevice, s));
-                }
-                if (b == 3) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outd, m->x, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
-            }
-        }
-        if (m->tp_world > 1) {
-            if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-            rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
-            if (rc) return rc;
-        }
-    }
+    for (int l = 0; l < c.n_layers; ++l)
+        if ((rc = enqueue_layer(m, l, pdl, s, hk))) return rc;
     LMHeadParams hp{};
     hp.W = m->lm_head;  // this rank's vocabulary rows
     hp.x = m->x;
@@ -1646,6 +1699,59 @@ int iam_model_step_bytes(iam_model_t m, int context, long long* bytes) {
     t += 2LL * m->vocab_local * c.dim;                                          // LM head rows
     *bytes = t;
     return IAM_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ block-level entry points
+
+namespace {
+int block_entry_check(iam_model_s* m, int layer, const void* in, const void* out, float effort, int pos) {
+    if (!m || !in || !out) return fail(IAM_ERR_ARG, "layer entry: null argument");
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail(IAM_ERR_ARG, "layer entry: layer out of range");
+    if (!effort_ok(effort)) return fail(IAM_ERR_ARG, "layer entry: effort must be in (0, 1]");
+    if (pos < 0 || pos >= m->cfg.max_ctx) return fail(IAM_ERR_ARG, "layer entry: pos outside [0, max_ctx)");
+    if (m->tp_world > 1) return fail(IAM_ERR_UNSUPPORTED, "layer entry: one GPU only (call iam_model_forward under TP)");
+    IAM_CUDA_TRY(cudaSetDevice(m->device));
+    return IAM_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int iam_layer_forward(iam_model_t m, int layer, const float* x_dev, int pos, float effort, float* out_dev,
+                      void* stream) {
+    int rc = block_entry_check(m, layer, x_dev, out_dev, effort, pos);
+    if (rc || (rc = build_plans(m, effort))) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    IAM_CUDA_TRY(launch_ex(set_int_kernel, dim3(1), dim3(1), 0, s, false, m->pos, pos));
+    IAM_CUDA_TRY(cudaMemcpyAsync(m->x, x_dev, (size_t)m->cfg.dim * 4, cudaMemcpyDeviceToDevice, s));
+    if ((rc = enqueue_layer(m, layer, false, s, nullptr))) return rc;
+    IAM_CUDA_TRY(cudaMemcpyAsync(out_dev, m->x, (size_t)m->cfg.dim * 4, cudaMemcpyDeviceToDevice, s));
+    m->host_pos = pos;
+    return IAM_OK;
+}
+
+int iam_attention_forward(iam_model_t m, int layer, const float* h_dev, int pos, float effort, float* out_dev,
+                          void* stream) {
+    int rc = block_entry_check(m, layer, h_dev, out_dev, effort, pos);
+    if (rc || (rc = build_plans(m, effort))) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    const iam_model_config& c = m->cfg;
+    IAM_CUDA_TRY(launch_ex(set_int_kernel, dim3(1), dim3(1), 0, s, false, m->pos, pos));
+    if ((rc = launch_plain_plan(m, layer, 0, h_dev, nullptr, s))) return rc;
+    if ((rc = launch_attention(attn_params(m, layer), c.n_heads / c.n_kv_heads, s, false))) return rc;
+    if ((rc = launch_plain_plan(m, layer, 1, m->att, out_dev, s))) return rc;
+    m->host_pos = pos;
+    return IAM_OK;
+}
+
+int iam_feedforward_forward(iam_model_t m, int layer, const float* h_dev, float effort, float* out_dev, void* stream) {
+    int rc = block_entry_check(m, layer, h_dev, out_dev, effort, 0);
+    if (rc || (rc = build_plans(m, effort))) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((rc = launch_plain_plan(m, layer, 2, h_dev, nullptr, s))) return rc;
+    return launch_plain_plan(m, layer, 3, nullptr, out_dev, s);
 }
 
 }  // extern "C"
