@@ -805,10 +805,18 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if args.impl == "reference":  # rank 0 alone times the reference's CPU path: no collective at all
-        res = run_reference(args, rank, world)
+    # stdout carries the one JSON line: whatever the libraries print there (NCCL's version
+    # banner, for one) goes to stderr instead
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(res):
         if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+            os.write(json_fd, (json.dumps(res) + "\n").encode())
+
+    if args.impl == "reference":  # rank 0 alone times the reference's CPU path: no collective at all
+        emit(run_reference(args, rank, world))
         return
     if world > 1:
         import datetime
@@ -822,8 +830,7 @@ def main():
             res = run_prefill(args, rank, world)
         else:
             res = run_bucketmul(args, rank, world)
-        if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+        emit(res)
     finally:
         if world > 1:
             import torch

@@ -659,6 +659,19 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     int* rows_of = reinterpret_cast<int*>(pr.partials + (size_t)R * M);
     if (tile == 0 && tid == 0) rows_of[range] = S;
     debug_stamp(tr, 5);
+    if (b.partials_only) {  // the ranges are summed by the tensor-parallel exchange
+        if (local == 0 && tid == 0) {
+            if (pr.cutoff_out) *pr.cutoff_out = cutoff;
+            if (pr.iters_out) *pr.iters_out = iters;
+        }
+        if (stage && !have_sts && tid == 0) mbar_wait_bounded(&h.bar);
+        if (tr) {
+            debug_stamp(tr, 6);
+            tr[7] = S;
+        }
+        pdl_trigger();
+        return;
+    }
     grid_barrier(b.barrier);  // every partial of the launch is written
     debug_stamp(tr, 11);
     pdl_trigger();  // every CTA of this launch is past the barrier: the successor may start
@@ -781,35 +794,61 @@ size_t bg_smem_bytes(const BGBatch& b) { return g_offsets(bg_range_max(b), b.sta
 
 void bg_choose_shape(BGBatch& b) {
     int widest = 0;
-    for (int i = 0; i < b.nprob; ++i) widest = std::max(widest, b.p[i].cols);
+    for (int i = 0; i < b.nprob; ++i) widest = std::max(widest, b.p[i].full_cols > 0 ? b.p[i].full_cols : b.p[i].cols);
     b.rowl = widest >= 512 ? 1 : 2;
     const int sms = sm_count_current();
+    // input ranges of the whole matrices: one GPU's wave
     double work = 0.0;
-    int tiles[kGMaxProblems];
+    int full_tiles[kGMaxProblems], full_r[kGMaxProblems];
     for (int i = 0; i < b.nprob; ++i) {
-        BGProblem& p = b.p[i];
-        p.vec = vec_cap(p);
-        const int tw = (32 / b.rowl) * p.vec;
-        tiles[i] = (p.cols + tw - 1) / tw;
-        work += (double)p.cols * p.n_in;
+        const BGProblem& p = b.p[i];
+        const int fc = p.full_cols > 0 ? p.full_cols : p.cols, fi = p.full_in > 0 ? p.full_in : p.n_in;
+        full_tiles[i] = (fc + 32 / b.rowl * kVMax - 1) / (32 / b.rowl * kVMax);
+        work += (double)fc * fi;
     }
-    // ranges in proportion to each problem's share of the work, one wave of CTAs in total
     int total = 0;
     for (int i = 0; i < b.nprob; ++i) {
-        BGProblem& p = b.p[i];
-        const double share = work > 0 ? (double)p.cols * p.n_in / work : 1.0;
-        int r = (int)(sms * share / tiles[i]);
-        r = std::max(1, std::min(std::min(r, kMaxRanges), p.n_in));
-        p.n_ranges = r;
-        total += r * tiles[i];
+        const BGProblem& p = b.p[i];
+        const int fc = p.full_cols > 0 ? p.full_cols : p.cols, fi = p.full_in > 0 ? p.full_in : p.n_in;
+        const double share = work > 0 ? (double)fc * fi / work : 1.0;
+        int r = (int)(sms * share / full_tiles[i]);
+        full_r[i] = std::max(1, std::min(std::min(r, kMaxRanges), fi));
+        total += full_r[i] * full_tiles[i];
     }
     while (total > sms) {  // a problem with more tiles than its share of the SMs
         int k = 0;
         for (int i = 1; i < b.nprob; ++i)
-            if (b.p[i].n_ranges * tiles[i] > b.p[k].n_ranges * tiles[k]) k = i;
-        if (b.p[k].n_ranges == 1) break;
-        b.p[k].n_ranges -= 1;
-        total -= tiles[k];
+            if (full_r[i] * full_tiles[i] > full_r[k] * full_tiles[k]) k = i;
+        if (full_r[k] == 1) break;
+        full_r[k] -= 1;
+        total -= full_tiles[k];
+    }
+    // this shard: its ranges, then tiles as wide as the vector loads allow, narrowed while the
+    // launch still fits in one wave
+    total = 0;
+    int tiles[kGMaxProblems];
+    for (int i = 0; i < b.nprob; ++i) {
+        BGProblem& p = b.p[i];
+        const int fi = p.full_in > 0 ? p.full_in : p.n_in;
+        const int rf = p.fixed_ranges > 0 ? p.fixed_ranges : full_r[i];
+        p.n_ranges = std::max(1, (int)((long long)rf * p.n_in / fi));
+        p.vec = vec_cap(p);
+        tiles[i] = (p.cols + (32 / b.rowl) * p.vec - 1) / ((32 / b.rowl) * p.vec);
+        total += tiles[i] * p.n_ranges;
+    }
+    for (bool more = true; more;) {
+        more = false;
+        for (int i = 0; i < b.nprob; ++i) {
+            BGProblem& p = b.p[i];
+            if (p.vec == 1) continue;
+            const int t2 = (p.cols + (32 / b.rowl) * (p.vec / 2) - 1) / ((32 / b.rowl) * (p.vec / 2));
+            if (total + (t2 - tiles[i]) * p.n_ranges > sms) continue;
+            if (t2 == tiles[i]) continue;
+            total += (t2 - tiles[i]) * p.n_ranges;
+            tiles[i] = t2;
+            p.vec /= 2;
+            more = true;
+        }
     }
     // stage each range's stats in shared memory when the packed layout allows it
     b.stage_stats = 1;

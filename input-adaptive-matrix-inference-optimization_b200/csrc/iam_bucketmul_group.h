@@ -44,6 +44,9 @@ struct BGProblem {
     int in_begin;             // first input held (row-parallel shards), else 0
     int n_in;                 // inputs held
     int cols;                 // bucket columns held
+    int full_in;              // inputs of the whole matrix over all ranks (0: n_in)
+    int full_cols;            // bucket columns of the whole matrix over all ranks (0: cols)
+    int fixed_ranges;         // > 0: input ranges of the whole matrix, fixed (must divide full_in)
     int P;                    // probes used by the cutoff: min(in_dim, 4096)
     int target;               // P - quantile
     int vec;                  // columns per lane (1, 2 or 4; bg_choose_shape)
@@ -60,6 +63,8 @@ struct BGBatch {
     int rowl;                 // row lanes per warp: 1 or 2
     int stage_stats;          // bulk-copy each range's packed stats into shared memory first
     int pdl;                  // launched with programmatic stream serialization
+    int partials_only;        // write each range's partial (and its row count) and stop: the
+                              // ranges are summed by the tensor-parallel exchange (tp_gather_reduce)
     unsigned* barrier;        // scratch: 4 words {arrivals, generation, error, -}, zeroed once
     long long* trace;         // optional: kTraceSlots int64 per CTA (blockIdx.x < trace_cap)
     int trace_cap;
@@ -72,10 +77,14 @@ inline size_t bg_scratch_floats(int n_ranges, int cols) {
 // Most input ranges any plan uses (partial scratch can be sized with it).
 constexpr int kMaxRanges = 64;
 
-// Row lanes, columns per lane, input ranges and stats staging of a batch: 1 row lane per
-// warp (32 lanes x 4 columns = 128-column tiles) for matrices of 512 or more bucket columns,
-// else 2 (16 lanes x 4 columns); then as many input ranges per problem (in proportion to its
-// columns) as one wave of one CTA per SM holds.
+// Row lanes, columns per lane, input ranges and stats staging of a batch.  Each output's sum
+// order depends only on the row lanes and the input ranges, and both follow from the whole
+// matrices (full_cols, full_in), so every tensor-parallel shard adds its outputs in the order
+// one GPU does: 1 row lane per warp for matrices of 512 or more bucket columns, else 2; input
+// ranges fixed_ranges, or as many per problem (in proportion to its work) as one wave of one
+// CTA per SM holds on one GPU.  The shard then takes its share of those ranges (row-parallel
+// shards hold whole ranges) and the widest tiles (up to 4 columns per lane) that still fill
+// the SMs.
 void bg_choose_shape(BGBatch& b);
 // Fills n_tiles, range_max and cta_begin of every problem; returns the CTAs of the launch.
 int bg_plan(BGBatch& b);

@@ -88,6 +88,18 @@ struct DenseLayer {
 // column-parallel outputs of the same rank, so no exchange is needed between the two halves).
 inline bool column_parallel(int which) { return which != MO && which != MD; }
 
+// Input ranges of the row-parallel o and down bucketMuls, the same at every tensor-parallel
+// degree (up to kTpMaxWorld) so that each rank holds whole ranges and the ranges' partials add
+// up in the single-GPU order: 32 when in_dim allows, else fewer; 0 when no power of two of at
+// least `world` divides in_dim (the shape is then chosen freely).
+inline int row_parallel_ranges(int in_dim, int world) {
+    for (int r = 32; r >= 1 && r >= world; r /= 2)
+        if (in_dim % r == 0 && r % world == 0 && r % kTpMaxWorld == 0) return r;
+    for (int r = 32; r >= 1 && r >= world; r /= 2)
+        if (in_dim % r == 0 && r % world == 0) return r;
+    return 0;
+}
+
 struct Shard {
     int col0, cols;  // bucket columns held
     int in0, in1;    // inputs held
@@ -315,6 +327,11 @@ int alloc_runtime(iam_model_s* m) {
         // the largest exchange: the o/down all-reduce (dim), the head all-gather, the gate+up
         // all-gather (2 x ffn_local) or the logits all-gather (vocab_local)
         w.mbox_floats = std::max(std::max(c.dim, qn / m->tp_world), std::max(2 * m->ffn_local, m->vocab_local));
+        // the o / down range partials (tp_gather_reduce): ranges per rank x dim
+        for (const int in : {qn, c.ffn_dim}) {
+            const int r = row_parallel_ranges(in, m->tp_world);
+            w.mbox_floats = std::max(w.mbox_floats, std::max(1, r / m->tp_world) * c.dim);
+        }
         w.epoch_off = take(4 * kTpCtas);
         w.err_off = take(4);
         w.mbox_off = take((size_t)2 * m->tp_world * w.mbox_floats * 8);
@@ -748,6 +765,10 @@ int build_plans(iam_model_s* m, float effort) {
                 p.in_begin = mat.in_begin;
                 p.n_in = mat.in_end - mat.in_begin;
                 p.cols = mat.cols;
+                // the whole matrix (the sum order follows from it: identical at every TP degree)
+                p.full_in = mat.in_dim;
+                p.full_cols = mat.out_dim / 16;
+                if (!column_parallel(kMats[bi][i])) p.fixed_ranges = row_parallel_ranges(mat.in_dim, m->tp_world);
                 p.P = sp.P;
                 p.target = sp.target;
                 if (m->capture) {  // diagnostics: the x each launch used and every cutoff
@@ -758,6 +779,8 @@ int build_plans(iam_model_s* m, float effort) {
                     p.cutoff_out = rec + CL.cut + kMats[bi][i];
                 }
             }
+            // under the NVLink exchanges the o and down ranges are summed by tp_gather_reduce
+            b.partials_only = (m->tp_world > 1 && m->tp_p2p && (bi == 1 || bi == 3)) ? 1 : 0;
             bg_choose_shape(b);
         }
     m->plan_effort = effort;
@@ -843,6 +866,20 @@ int launch_plain_plan(iam_model_s* m, int l, int bi, const float* x, float* out,
     return bg_launch(b, s);
 }
 
+// The NVLink exchange after the row-parallel o (bi 1) or down (bi 3) of layer l: the ranges'
+// partials of every rank added in range order plus the residual (x for o, x1 for down) into
+// x1 or x, as one GPU adds them (tp_gather_reduce); the split-CTA kernel's rank sums are
+// all-reduced instead.
+int o_down_exchange(iam_model_s* m, int l, int bi, cudaStream_t s, bool pdl) {
+    const iam_model_config& c = m->cfg;
+    float* out = bi == 1 ? m->x1 : m->x;
+    if (!m->use_group) return tp_allreduce_sum(m->win, woff(m, out), c.dim, s, pdl);
+    const BGBatch& b = m->gplans[(size_t)l * 4 + bi];
+    const BGProblem& p = b.p[0];
+    return tp_gather_reduce(m->win, p.partials, c.dim, p.n_ranges, bi == 1 ? m->x : m->x1, out,
+                            m->sel + l * NMAT + (bi == 1 ? MO : MD), s, pdl);
+}
+
 // The launches of decoder layer l (transformer_layer.hpp:75-122): RMSNorm-fused q/k/v
 // bucketMuls, attention with the RoPE'd fp16 KV append, o (+ the residual), RMSNorm-fused
 // gate/up, SiLU-fused down (+ the residual), with the tensor-parallel exchanges between them.
@@ -868,7 +905,7 @@ int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk
         if (m->tp_world > 1 && m->tp_p2p) {  // the exchange in front of launch b (NVLink one-shot)
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
             if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
-            else if (b == 2) rc = tp_allreduce_sum(m->win, woff(m, m->x1), c.dim, s, pdl);
+            else if (b == 2) rc = o_down_exchange(m, l, 1, s, pdl);
             else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
             if (rc) return rc;
         } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
@@ -902,7 +939,7 @@ int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk
     }
     if (m->tp_world > 1) {
         if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-        rc = m->tp_p2p ? tp_allreduce_sum(m->win, woff(m, m->x), c.dim, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
+        rc = m->tp_p2p ? o_down_exchange(m, l, 3, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
         if (rc) return rc;
     }
     return IAM_OK;

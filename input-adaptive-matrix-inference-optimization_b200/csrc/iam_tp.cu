@@ -109,6 +109,78 @@ __global__ void __launch_bounds__(kTpThreads) tp_allreduce_kernel(TpWindow w, si
     end_epoch(w, c, epoch);
 }
 
+// Each rank holds the partials of r_local consecutive input ranges (ranges rank * r_local ..,
+// [r_local][M] floats, then r_local row counts); every rank receives all of them and adds the
+// R = world * r_local <= kTpMaxRanges partials of each output in range order, then the residual
+// -- the order in which one GPU's bucketMul kernel adds its R ranges -- so the sum is identical
+// on every rank and to the single-GPU one.  A thread takes one output and issues the loads of
+// its R partials together (its own from memory, the peers' from the mailbox), then polls again
+// only for those whose epoch has not arrived (bounded).  The rank's own row count goes to
+// *count_out.
+constexpr int kTpMaxRanges = 32;
+
+__global__ void __launch_bounds__(kTpThreads) tp_gather_reduce_kernel(TpWindow w, const float* part, int M,
+                                                                      int r_local, const float* residual,
+                                                                      float* out, int* count_out) {
+    pdl_wait();
+    __shared__ uint32_t s_epoch;
+    const int c = blockIdx.x;
+    const uint32_t epoch = begin_epoch(w, c, &s_epoch);
+    const int n = r_local * M;  // payload elements (the row counts stay local)
+    const int gt = c * kTpThreads + threadIdx.x, nt = kTpCtas * kTpThreads;
+    for (int e = gt; e < n; e += nt) send(w, epoch, e, part[e]);
+    const int R = r_local * w.world;
+    volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(w.base[w.rank] + w.err_off);
+    for (int i = gt; i < M; i += nt) {
+        float v[kTpMaxRanges];
+        uint32_t pend = 0u;
+#pragma unroll
+        for (int g = 0; g < kTpMaxRanges; ++g) {
+            v[g] = 0.0f;
+            if (g < R) {
+                const int owner = g / r_local, e = (g - owner * r_local) * M + i;
+                if (owner == w.rank) {
+                    v[g] = part[e];
+                } else {
+                    const uint2 x = ld_ll(mbox_of(w, w.rank, epoch, owner) + e);
+                    if (x.y == epoch) v[g] = __uint_as_float(x.x);
+                    else pend |= 1u << g;
+                }
+            }
+        }
+        for (long long polls = 0; pend;) {
+            if (++polls > w.spin_limit || *err != 0u) {  // a peer never sent: flag it, give up
+                *err = 1u;
+                break;
+            }
+            if (polls > 64) __nanosleep(32);
+#pragma unroll
+            for (int g = 0; g < kTpMaxRanges; ++g)
+                if ((pend >> g) & 1u) {
+                    const int owner = g / r_local, e = (g - owner * r_local) * M + i;
+                    const uint2 x = ld_ll(mbox_of(w, w.rank, epoch, owner) + e);
+                    if (x.y == epoch) {
+                        v[g] = __uint_as_float(x.x);
+                        pend &= ~(1u << g);
+                    }
+                }
+        }
+        float acc = 0.0f;
+#pragma unroll
+        for (int g = 0; g < kTpMaxRanges; ++g)
+            if (g < R) acc += v[g];
+        out[i] = residual ? residual[i] + acc : acc;  // add32 (bucketMul.cl:517-520)
+    }
+    if (c == 0 && threadIdx.x == 0 && count_out) {
+        const int* rows = reinterpret_cast<const int*>(part + n);
+        int t = 0;
+        for (int r = 0; r < r_local; ++r) t += rows[r];
+        *count_out = t;
+    }
+    pdl_trigger();
+    end_epoch(w, c, epoch);
+}
+
 // The packed argmax key (64 bits) travels as two elements: high and low words.
 __global__ void __launch_bounds__(kTpThreads) tp_keymax_kernel(TpWindow w, unsigned long long* key) {
     pdl_wait();
@@ -144,6 +216,15 @@ int tp_allgather(const TpWindow& w, size_t off_a, size_t off_b, int chunk, cudaS
 int tp_allreduce_sum(const TpWindow& w, size_t off, int n, cudaStream_t s, bool pdl) {
     if (n > w.mbox_floats) return fail(IAM_ERR_UNSUPPORTED, "tp all-reduce larger than the mailbox");
     IAM_CUDA_TRY(launch_ex(tp_allreduce_kernel, dim3(kTpCtas), dim3(kTpThreads), 0, s, pdl, w, off, n));
+    return IAM_OK;
+}
+
+int tp_gather_reduce(const TpWindow& w, const float* partials, int M, int r_local, const float* residual, float* out,
+                     int* count_out, cudaStream_t s, bool pdl) {
+    if ((long long)r_local * M > w.mbox_floats) return fail(IAM_ERR_UNSUPPORTED, "tp gather-reduce larger than the mailbox");
+    if (r_local < 1 || r_local * w.world > kTpMaxRanges) return fail(IAM_ERR_UNSUPPORTED, "tp gather-reduce: too many ranges");
+    IAM_CUDA_TRY(launch_ex(tp_gather_reduce_kernel, dim3(kTpCtas), dim3(kTpThreads), 0, s, pdl, w, partials, M, r_local,
+                           residual, out, count_out));
     return IAM_OK;
 }
 

@@ -14,7 +14,7 @@
 namespace iam {
 
 constexpr int kTpMaxWorld = 8;
-constexpr int kTpCtas = 8;       // CTAs of every collective launch (one epoch copy each)
+constexpr int kTpCtas = 32;      // CTAs of every collective launch (one epoch copy each)
 constexpr int kTpThreads = 256;
 
 struct TpWindow {
@@ -35,6 +35,12 @@ constexpr long long kTpSpinLimit = 1LL << 21;
 int tp_allgather(const TpWindow& w, size_t off_a, size_t off_b, int chunk, cudaStream_t s, bool pdl);
 // buf[0, n) at window offset off := sum over ranks, added in rank order (identical on all ranks).
 int tp_allreduce_sum(const TpWindow& w, size_t off, int n, cudaStream_t s, bool pdl);
+// out[0, M) := residual (may be null) + the sum of R = world * r_local range partials in range
+// order, rank r holding ranges r * r_local .. (partials [r_local][M] floats, then r_local int row
+// counts, in this rank's memory); identical on every rank and to one GPU's bucketMul sum.
+// *count_out (may be null) := this rank's rows.
+int tp_gather_reduce(const TpWindow& w, const float* partials, int M, int r_local, const float* residual, float* out,
+                     int* count_out, cudaStream_t s, bool pdl);
 // *key := max over ranks (the packed greedy argmax key).
 int tp_keymax(const TpWindow& w, unsigned long long* key, cudaStream_t s, bool pdl);
 
