@@ -263,7 +263,7 @@ def run_bucketmul(args, rank, world):
                    round(sel_frac, 4), "bytes_per_step": int(step_bytes[0])},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
-                     "kernel": "bm_fused_kernel", "bytes_per_launch": int(launch_avg_bytes)},
+                     "kernel": "bg_kernel", "bytes_per_launch": int(launch_avg_bytes)},
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * len(LAYER_SHAPES),
         "clocks": clk.summary(),
