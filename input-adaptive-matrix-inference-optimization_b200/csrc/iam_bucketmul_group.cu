@@ -253,7 +253,89 @@ IAM_DEV void acc_chunk(const uint2* __restrict__ list, int n, int j0, int mw, co
     }
 }
 
-template <int ROWL, int XM>
+// The dense stream of one CTA (tile = dense_rows output rows, range of rin <= 1024 inputs, rin a
+// multiple of 8): a lane holds x and the selection masks of inputs 8*lane + 256c .. + 8 in
+// registers; each warp takes output rows tile_begin + warp + 16j, reads the row's range with
+// 16-byte loads, and adds x[i]*w for the weights whose rank bit is set in mask[i] -- the same
+// weights a bucket-row selection picks (row r of input i holds, in each column group of 16
+// outputs, the weight of rank r).  The weight value is the bucket word: the high 12 bits of the
+// stored word with the output's slot (o mod 16) as the low 4 (bucketMul.cl:419-425).  Per row a
+// lane adds its products in input order, then the warp sums the lanes (xor tree): the sum
+// depends on the range only.  Writes the range's partial of each output.
+IAM_DEV void dense_rows_stream(const BGProblem& pr, const float* xr, const uint16_t* mask, int rin, int i0, int tile,
+                               int M, float* part, int warp, int lane) {
+    constexpr int NCH = 4;
+    float xv[NCH][8];
+    uint32_t mk[NCH][4];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int k0 = 256 * c + 8 * lane;
+        if (k0 < rin) {
+            const float4 a = *reinterpret_cast<const float4*>(xr + k0);
+            const float4 d = *reinterpret_cast<const float4*>(xr + k0 + 4);
+            const uint4 m = *reinterpret_cast<const uint4*>(mask + k0);
+            xv[c][0] = a.x; xv[c][1] = a.y; xv[c][2] = a.z; xv[c][3] = a.w;
+            xv[c][4] = d.x; xv[c][5] = d.y; xv[c][6] = d.z; xv[c][7] = d.w;
+            mk[c][0] = m.x; mk[c][1] = m.y; mk[c][2] = m.z; mk[c][3] = m.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[c][e] = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) mk[c][q] = 0u;
+        }
+    }
+    const int TO = pr.dense_rows;
+    const int o_end = min(M, tile * TO + TO);
+    const size_t ld = (size_t)pr.n_in;
+    const uint16_t* base = pr.dense + (size_t)(i0 - pr.in_begin);
+    // two rows per step (warp rows o and o + 16): both rows' loads are in flight together
+    for (int o = tile * TO + warp; o < o_end; o += 2 * kGW) {
+        const bool two = o + kGW < o_end;
+        const uint4* row0 = reinterpret_cast<const uint4*>(base + (size_t)o * ld);
+        const uint4* row1 = reinterpret_cast<const uint4*>(base + (size_t)(two ? o + kGW : o) * ld);
+        uint4 w0[NCH], w1[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+            if (256 * c + 8 * lane < rin) {
+                w0[c] = __ldg(row0 + 32 * c + lane);
+                w1[c] = __ldg(row1 + 32 * c + lane);
+            }
+        float acc0 = 0.0f, acc1 = 0.0f;
+        const uint32_t slot0 = (uint32_t)(o & 15) * 0x10001u, slot1 = (uint32_t)((o + kGW) & 15) * 0x10001u;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            if (256 * c + 8 * lane >= rin) continue;
+            const uint32_t a[4] = {w0[c].x, w0[c].y, w0[c].z, w0[c].w};
+            const uint32_t d[4] = {w1[c].x, w1[c].y, w1[c].z, w1[c].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t m2 = mk[c][q];  // masks of inputs 2q (low half) and 2q + 1 (high half)
+                const float x0 = xv[c][2 * q], x1 = xv[c][2 * q + 1];
+                {
+                    const uint32_t v = (a[q] & 0xFFF0FFF0u) | slot0;
+                    acc0 = fmaf(((m2 >> (a[q] & 15u)) & 1u) ? x0 : 0.0f, h2f(v & 0xffffu), acc0);
+                    acc0 = fmaf(((m2 >> (16u + ((a[q] >> 16) & 15u))) & 1u) ? x1 : 0.0f, h2f(v >> 16), acc0);
+                }
+                {
+                    const uint32_t v = (d[q] & 0xFFF0FFF0u) | slot1;
+                    acc1 = fmaf(((m2 >> (d[q] & 15u)) & 1u) ? x0 : 0.0f, h2f(v & 0xffffu), acc1);
+                    acc1 = fmaf(((m2 >> (16u + ((d[q] >> 16) & 15u))) & 1u) ? x1 : 0.0f, h2f(v >> 16), acc1);
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, off);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, off);
+        }
+        if (lane == 0) {
+            part[o] = acc0;
+            if (two) part[o + kGW] = acc1;
+        }
+    }
+}
+
+template <int ROWL, int XM, int DN>
 __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBatch b) {
     constexpr int COLL = 32 / ROWL, NSETS = kGW * ROWL;
     static_assert(kChunk % NSETS == 0, "chunks keep the set of every row");
@@ -598,6 +680,11 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     const int S = h.total;
     debug_stamp(tr, 3);
 
+    float* part = pr.partials + (size_t)range * M;
+    if constexpr (DN) {
+        dense_rows_stream(pr, xr, mask, rin, i0, tile, M, part, warp, lane);
+        debug_stamp(tr, 4);
+    } else {
     // ---- 4. accumulation: list position j goes to set j % NSETS = (warp, row lane)
     const int rl = lane / COLL, q = lane % COLL;
     const int col = tile * TW + q * vec;
@@ -641,7 +728,6 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     // lanes' accumulators of one (slot, column) of every warp in turn (conflict free); the row
     // lanes of an output are then added in row-lane order.
     const int kOut = 16 * TW;
-    float* part = pr.partials + (size_t)range * M;
     for (int idx = tid; idx < 32 * 16 * vec; idx += kGT) {  // a multiple of 32: whole warps
         const int ln = idx & 31, pair = idx >> 5;
         const int e = pair % vec, slot = pair / vec;
@@ -655,6 +741,7 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
             s = s + other;
         }
         if (ln < COLL && tile * TW + o / 16 < pr.cols) part[(size_t)tile * kOut + o] = s;
+    }
     }
     int* rows_of = reinterpret_cast<int*>(pr.partials + (size_t)R * M);
     if (tile == 0 && tid == 0) rows_of[range] = S;
@@ -717,28 +804,28 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     }
 }
 
-template <int ROWL, int XM>
+template <int ROWL, int XM, int DN>
 cudaError_t bg_set_attrs() {
     static std::atomic<unsigned long long> done{0};
     return once_per_device(done, [] {
-        return cudaFuncSetAttribute(bg_kernel<ROWL, XM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        return cudaFuncSetAttribute(bg_kernel<ROWL, XM, DN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
 }
 
-template <int ROWL, int XM>
+template <int ROWL, int XM, int DN>
 int bg_launch_t(const BGBatch& b, int ctas, size_t smem, cudaStream_t s) {
-    cudaError_t e = bg_set_attrs<ROWL, XM>();
+    cudaError_t e = bg_set_attrs<ROWL, XM, DN>();
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bg_kernel)");
-    IAM_CUDA_TRY(launch_ex(bg_kernel<ROWL, XM>, dim3((unsigned)ctas), dim3(kGT), smem, s, b.pdl != 0, b));
+    IAM_CUDA_TRY(launch_ex(bg_kernel<ROWL, XM, DN>, dim3((unsigned)ctas), dim3(kGT), smem, s, b.pdl != 0, b));
     return IAM_OK;
 }
 
-template <int ROWL>
+template <int ROWL, int DN>
 int bg_launch_x(const BGBatch& b, int ctas, size_t smem, cudaStream_t s) {
     switch (b.xmode) {
-        case kXRms: return bg_launch_t<ROWL, kXRms>(b, ctas, smem, s);
-        case kXSilu: return bg_launch_t<ROWL, kXSilu>(b, ctas, smem, s);
-        default: return bg_launch_t<ROWL, kXPlain>(b, ctas, smem, s);
+        case kXRms: return bg_launch_t<ROWL, kXRms, DN>(b, ctas, smem, s);
+        case kXSilu: return bg_launch_t<ROWL, kXSilu, DN>(b, ctas, smem, s);
+        default: return bg_launch_t<ROWL, kXPlain, DN>(b, ctas, smem, s);
     }
 }
 
@@ -780,8 +867,12 @@ int bg_plan(BGBatch& b) {
     int begin = 0;
     for (int i = 0; i < b.nprob; ++i) {
         BGProblem& p = b.p[i];
-        const int tw = (32 / b.rowl) * p.vec;
-        p.n_tiles = (p.cols + tw - 1) / tw;
+        if (b.dense) {
+            p.n_tiles = (16 * p.cols + p.dense_rows - 1) / p.dense_rows;
+        } else {
+            const int tw = (32 / b.rowl) * p.vec;
+            p.n_tiles = (p.cols + tw - 1) / tw;
+        }
         p.cta_begin = begin;
         begin += p.n_tiles * p.n_ranges;
     }
@@ -792,7 +883,65 @@ int bg_plan(BGBatch& b) {
 
 size_t bg_smem_bytes(const BGBatch& b) { return g_offsets(bg_range_max(b), b.stage_stats != 0).total; }
 
+// Input ranges of a dense launch over the whole matrix: the fewest that keep a range within
+// 1024 inputs (the stream holds them in registers) in a multiple of 8; a multiple of 8 ranges
+// for row-parallel matrices, so that every tensor-parallel rank holds whole ranges.  0: none.
+int bg_dense_ranges(int full_in, bool row_parallel) {
+    for (int r = 1; r <= kMaxRanges; ++r) {
+        if (full_in % r) continue;
+        const int rin = full_in / r;
+        if (rin > 1024 || rin % 8) continue;
+        if (row_parallel && r % 8) continue;
+        return r;
+    }
+    return 0;
+}
+
+// Dense launches: ranges from the whole matrix (the sum order follows from them only), then
+// tiles of output rows -- CTAs in proportion to each problem's work, one wave in total.
+void bg_choose_shape_dense(BGBatch& b) {
+    const int sms = sm_count_current();
+    b.rowl = 1;
+    double work = 0.0;
+    for (int i = 0; i < b.nprob; ++i) work += 16.0 * b.p[i].cols * b.p[i].n_in;
+    int total = 0;
+    for (int i = 0; i < b.nprob; ++i) {
+        BGProblem& p = b.p[i];
+        const int fi = p.full_in > 0 ? p.full_in : p.n_in;
+        const int rf = bg_dense_ranges(fi, p.fixed_ranges > 0);
+        p.n_ranges = std::max(1, (int)((long long)rf * p.n_in / fi));
+        p.vec = 1;
+        const int M = 16 * p.cols;
+        const double share = work > 0 ? 16.0 * p.cols * p.n_in / work : 1.0;
+        int tiles = std::max(1, (int)(sms * share / p.n_ranges));
+        p.dense_rows = ((M + tiles - 1) / tiles + 15) / 16 * 16;
+        total += ((M + p.dense_rows - 1) / p.dense_rows) * p.n_ranges;
+    }
+    while (total > sms) {  // widen the tiles of the problem with the most CTAs
+        int k = 0, kc = 0;
+        for (int i = 0; i < b.nprob; ++i) {
+            const int c = ((16 * b.p[i].cols + b.p[i].dense_rows - 1) / b.p[i].dense_rows) * b.p[i].n_ranges;
+            if (c > kc) { kc = c; k = i; }
+        }
+        BGProblem& p = b.p[k];
+        const int M = 16 * p.cols;
+        const int t = (M + p.dense_rows - 1) / p.dense_rows;
+        if (t == 1) break;
+        p.dense_rows = ((M + t - 2) / (t - 1) + 15) / 16 * 16;
+        total += (((M + p.dense_rows - 1) / p.dense_rows) - t) * p.n_ranges;
+    }
+    b.stage_stats = 1;
+    for (int i = 0; i < b.nprob; ++i)
+        if (b.p[i].stats_stride != 1 || (reinterpret_cast<uintptr_t>(b.p[i].stats) & 15u) || (b.p[i].row0 % 8))
+            b.stage_stats = 0;
+    if (bg_smem_bytes(b) > 227 * 1024) b.stage_stats = 0;
+}
+
 void bg_choose_shape(BGBatch& b) {
+    if (b.dense) {
+        bg_choose_shape_dense(b);
+        return;
+    }
     int widest = 0;
     for (int i = 0; i < b.nprob; ++i) widest = std::max(widest, b.p[i].full_cols > 0 ? b.p[i].full_cols : b.p[i].cols);
     b.rowl = widest >= 512 ? 1 : 2;
@@ -873,14 +1022,20 @@ int bg_launch(const BGBatch& b0, cudaStream_t s) {
             return fail(IAM_ERR_ARG, "bucketmul: bad input ranges");
         if ((long long)16 * (p.in_begin + p.n_in) * p.cols >= (1LL << 31))
             return fail(IAM_ERR_UNSUPPORTED, "bucketmul: rows * bucket_cols must stay below 2^31 elements");
+        if (b.dense && (!p.dense || (reinterpret_cast<uintptr_t>(p.dense) & 15u) || p.n_in % p.n_ranges ||
+                        (p.n_in / p.n_ranges) % 8 || p.n_in / p.n_ranges > 1024 || p.dense_rows < 16 ||
+                        p.dense_rows % 16))
+            return fail(IAM_ERR_ARG, "bucketmul: dense stream needs aligned rows and ranges of <= 1024 inputs "
+                                     "(a multiple of 8)");
     }
     const int ctas = bg_plan(b);
     if (ctas > sm_count_current())
         return fail(IAM_ERR_UNSUPPORTED, "bucketmul: the launch needs more CTAs than SMs (one wave)");
     const size_t smem = bg_smem_bytes(b);
     if (smem > 227 * 1024) return fail(IAM_ERR_UNSUPPORTED, "bucketmul: an input range too large for shared memory");
-    if (b.rowl == 1) return bg_launch_x<1>(b, ctas, smem, s);
-    return bg_launch_x<2>(b, ctas, smem, s);
+    if (b.dense) return bg_launch_x<1, 1>(b, ctas, smem, s);
+    if (b.rowl == 1) return bg_launch_x<1, 0>(b, ctas, smem, s);
+    return bg_launch_x<2, 0>(b, ctas, smem, s);
 }
 
 }  // namespace iam

@@ -44,6 +44,9 @@ struct BGProblem {
     int in_begin;             // first input held (row-parallel shards), else 0
     int n_in;                 // inputs held
     int cols;                 // bucket columns held
+    const uint16_t* dense;    // dense launches: [16 * cols][n_in] the weights at their output
+                              // positions, low 4 bits = the weight's bucket row (rank) r
+    int dense_rows;           // dense launches: output rows per tile (a multiple of 16)
     int full_in;              // inputs of the whole matrix over all ranks (0: n_in)
     int full_cols;            // bucket columns of the whole matrix over all ranks (0: cols)
     int fixed_ranges;         // > 0: input ranges of the whole matrix, fixed (must divide full_in)
@@ -63,6 +66,8 @@ struct BGBatch {
     int rowl;                 // row lanes per warp: 1 or 2
     int stage_stats;          // bulk-copy each range's packed stats into shared memory first
     int pdl;                  // launched with programmatic stream serialization
+    int dense;                // stream the dense copies (every weight, selected by rank) instead
+                              // of the selected bucket rows: same selection, register accumulators
     int partials_only;        // write each range's partial (and its row count) and stop: the
                               // ranges are summed by the tensor-parallel exchange (tp_gather_reduce)
     unsigned* barrier;        // scratch: 4 words {arrivals, generation, error, -}, zeroed once
@@ -86,6 +91,8 @@ constexpr int kMaxRanges = 64;
 // shards hold whole ranges) and the widest tiles (up to 4 columns per lane) that still fill
 // the SMs.
 void bg_choose_shape(BGBatch& b);
+// Input ranges of a dense launch over a whole matrix of full_in inputs (0: no dense shape).
+int bg_dense_ranges(int full_in, bool row_parallel);
 // Fills n_tiles, range_max and cta_begin of every problem; returns the CTAs of the launch.
 int bg_plan(BGBatch& b);
 size_t bg_smem_bytes(const BGBatch& b);

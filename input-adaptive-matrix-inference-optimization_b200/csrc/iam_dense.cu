@@ -414,7 +414,8 @@ __global__ void __launch_bounds__(256) dense_split_kernel(const float* __restric
 constexpr int kUnpackI = 16, kUnpackC = 32;
 
 __global__ void __launch_bounds__(256) dense_unpack_kernel(const uint16_t* __restrict__ buckets, int in_dim, int cols,
-                                                           uint16_t* __restrict__ w, int ldw, int rpb, int pitch) {
+                                                           uint16_t* __restrict__ w, int ldw, int rpb, int pitch,
+                                                           int tag_rank) {
     __shared__ __align__(16) uint16_t s_out[kUnpackC * 16][kUnpackI];  // [dense row in tile][input]
     const int i0 = blockIdx.x * kUnpackI, c0 = blockIdx.y * kUnpackC;
     for (int e = threadIdx.x; e < kUnpackC * 16 * kUnpackI; e += blockDim.x) (&s_out[0][0])[e] = 0;
@@ -424,7 +425,8 @@ __global__ void __launch_bounds__(256) dense_unpack_kernel(const uint16_t* __res
         const int il = row >> 4;
         if (i0 + il < in_dim && c0 + c < cols) {
             const uint16_t word = buckets[(size_t)(i0 * 16 + row) * cols + c0 + c];
-            s_out[c * 16 + (word & 15)][il] = word;
+            // the packed word, or its value bits with its bucket row (rank) in place of the slot
+            s_out[c * 16 + (word & 15)][il] = tag_rank ? (uint16_t)((word & 0xFFF0u) | (unsigned)(row & 15)) : word;
         }
     }
     __syncthreads();
@@ -555,14 +557,14 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl) {
 }
 
 int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s,
-                 int rows_per_block, int block_pitch) {
+                 int rows_per_block, int block_pitch, bool tag_rank) {
     if (buckets == nullptr || w == nullptr || in_dim <= 0 || cols <= 0 || ldw < in_dim)
         return fail(IAM_ERR_ARG, "dense_unpack: bad arguments");
     if (ldw % 8 != 0 || !aligned16(w)) return fail(IAM_ERR_ARG, "dense_unpack: ldw % 8 and 16-byte alignment");
     if (rows_per_block < 0 || (rows_per_block > 0 && block_pitch < rows_per_block))
         return fail(IAM_ERR_ARG, "dense_unpack: row blocks");
     const dim3 grid((in_dim + kUnpackI - 1) / kUnpackI, (cols + kUnpackC - 1) / kUnpackC);
-    dense_unpack_kernel<<<grid, 256, 0, s>>>(buckets, in_dim, cols, w, ldw, rows_per_block, block_pitch);
+    dense_unpack_kernel<<<grid, 256, 0, s>>>(buckets, in_dim, cols, w, ldw, rows_per_block, block_pitch, tag_rank ? 1 : 0);
     IAM_CUDA_TRY(cudaGetLastError());
     return IAM_OK;
 }

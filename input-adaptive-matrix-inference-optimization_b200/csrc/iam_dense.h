@@ -54,8 +54,10 @@ int dense_gemm(const DenseProblem& p, cudaStream_t s, bool pdl = false);
 // packed word (value with its slot in the low 4 bits) lands at its original position, which
 // is the multiplicand bucketMul uses when every bucket row is selected.
 // rows_per_block > 0 places dense row o at (o / rows_per_block) * block_pitch + o % rows_per_block
-// (used to interleave the gate and up matrices for the SiLU epilogue).
+// (used to interleave the gate and up matrices for the SiLU epilogue).  tag_rank: each weight's
+// low 4 bits hold its bucket row (rank within its group of 16) instead of its slot, which the
+// position already gives (the decode's dense stream selects weights by rank).
 int dense_unpack(const uint16_t* buckets, int in_dim, int cols, uint16_t* w, int ldw, cudaStream_t s,
-                 int rows_per_block = 0, int block_pitch = 0);
+                 int rows_per_block = 0, int block_pitch = 0, bool tag_rank = false);
 
 }  // namespace iam

@@ -68,6 +68,8 @@ struct Matrix {
     int in_dim = 0, out_dim = 0;  // full matrix shape
     int cols = 0;                 // bucket columns held (out/16, or a shard of them)
     int in_begin = 0, in_end = 0; // inputs held (row-parallel shard) -- full range otherwise
+    uint16_t* dense = nullptr;    // [out held][inputs held]: each weight at its output position,
+                                  // its bucket row (rank) in the low 4 bits (high-effort decode)
 };
 
 struct Layer {
@@ -87,6 +89,11 @@ struct DenseLayer {
 // q, k, v, gate, up are column-parallel; o and down row-parallel (their inputs are the
 // column-parallel outputs of the same rank, so no exchange is needed between the two halves).
 inline bool column_parallel(int which) { return which != MO && which != MD; }
+
+// Decode efforts from which the bucketMuls stream dense copies of the matrices (every weight,
+// selected by rank: the same selection) instead of the selected bucket rows: above it the
+// rows read are most of the matrix, and register accumulation beats the slot scatter.
+constexpr float kDenseMinEffort = 0.8f;
 
 // Input ranges of the row-parallel o and down bucketMuls, the same at every tensor-parallel
 // degree (up to kTpMaxWorld) so that each rank holds whole ranges and the ranges' partials add
@@ -214,6 +221,7 @@ struct iam_model_s {
     // attention scratch
     float* att_part = nullptr;
     int* att_ctr = nullptr;
+    float dense_min_effort = kDenseMinEffort;  // decode efforts from here on stream the dense copies
     int att_split = 32, att_min_chunk = kAttnMinChunk, att_lane_min = kAttnLaneMinCtx,
         att_lane_short = kAttnLaneShortMax;
     // launch plans for the current effort
@@ -376,6 +384,7 @@ int alloc_runtime(iam_model_s* m) {
     if (const char* v = getenv("IAM_ATTN_MIN_CHUNK")) m->att_min_chunk = std::max(1, atoi(v));
     if (const char* v = getenv("IAM_ATTN_LANE_MIN_CTX")) m->att_lane_min = std::max(1, atoi(v));
     if (const char* v = getenv("IAM_ATTN_LANE_SHORT_MAX")) m->att_lane_short = std::max(0, atoi(v));
+    if (const char* v = getenv("IAM_DENSE_MIN_EFFORT")) m->dense_min_effort = (float)atof(v);
     if (gq > 4 || (hd != 64 && hd != 128)) {  // outside the tensor-core layout's shapes
         m->att_lane_min = INT_MAX;
         m->att_lane_short = 0;
@@ -769,6 +778,7 @@ int build_plans(iam_model_s* m, float effort) {
                 p.full_in = mat.in_dim;
                 p.full_cols = mat.out_dim / 16;
                 if (!column_parallel(kMats[bi][i])) p.fixed_ranges = row_parallel_ranges(mat.in_dim, m->tp_world);
+                p.dense = mat.dense;
                 p.P = sp.P;
                 p.target = sp.target;
                 if (m->capture) {  // diagnostics: the x each launch used and every cutoff
@@ -781,6 +791,11 @@ int build_plans(iam_model_s* m, float effort) {
             }
             // under the NVLink exchanges the o and down ranges are summed by tp_gather_reduce
             b.partials_only = (m->tp_world > 1 && m->tp_p2p && (bi == 1 || bi == 3)) ? 1 : 0;
+            b.dense = effort >= m->dense_min_effort ? 1 : 0;
+            for (int i = 0; i < b.nprob; ++i) {
+                const BGProblem& p = b.p[i];
+                if (!p.dense || bg_dense_ranges(p.full_in, p.fixed_ranges > 0) == 0) b.dense = 0;
+            }
             bg_choose_shape(b);
         }
     m->plan_effort = effort;
@@ -1116,7 +1131,26 @@ int prefill_chunk(iam_model_s* m, const int* tokens_host, int n, int pos0, cudaS
     return IAM_OK;
 }
 
+// The dense copies the decode streams at efforts >= dense_min_effort (as much memory again as
+// the bucket weights); skipped when that threshold is above 1.
+int build_dense_copies(iam_model_s* m) {
+    if (!(m->dense_min_effort <= 1.0f)) return IAM_OK;
+    for (Layer& L : m->layers)
+        for (Matrix& mat : L.m) {
+            const int n_in = mat.in_end - mat.in_begin;
+            int rc;
+            if ((rc = dalloc(m, &mat.dense, (size_t)16 * mat.cols * n_in))) return rc;
+            if ((rc = dense_unpack(mat.buckets, n_in, mat.cols, mat.dense, n_in, 0, 0, 0, true))) return rc;
+        }
+    return IAM_OK;
+}
+
 int finish_create(iam_model_s* m, iam_model_t* out) {
+    int rc = build_dense_copies(m);
+    if (rc) {
+        free_model(m);
+        return rc;
+    }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         free_model(m);
