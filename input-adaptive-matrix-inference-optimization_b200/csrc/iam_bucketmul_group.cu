@@ -152,25 +152,30 @@ IAM_DEV void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, unsigned 
 IAM_DEV void grid_barrier(unsigned* bar) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        volatile unsigned* vb = bar;
-        const unsigned gen = vb[1];
-        __threadfence();
-        const unsigned arrived = atomicAdd(bar, 1u);
+        // arrival with release semantics (this CTA's partials are visible before the count
+        // moves), generation read with acquire semantics (the others' partials are visible
+        // after it moves)
+        unsigned gen;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
+        unsigned arrived;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(bar) : "memory");
         if (arrived == gridDim.x - 1) {
-            vb[0] = 0u;
-            __threadfence();
-            atomicExch(bar + 1, gen + 1u);
+            asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 1), "r"(gen + 1u) : "memory");
         } else {
             long long n = 0;
-            while (vb[1] == gen) {
-                if (++n > kBarrierPolls || vb[2] != 0u) {
+            for (;;) {
+                unsigned g, err;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+                if (g != gen) break;
+                asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(err) : "l"(bar + 2) : "memory");
+                if (++n > kBarrierPolls || err != 0u) {
                     atomicOr(bar + 2, 1u);
                     break;
                 }
-                __nanosleep(64);
+                if (n > 256) __nanosleep(32);
             }
         }
-        __threadfence();
     }
     __syncthreads();
 }
