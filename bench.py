@@ -488,9 +488,11 @@ def run_decode(args, rank, world):
         "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab},
         # ours per step and rank: embed, key clear, 32 x (4 bucketMul + attention), LM head,
-        # advance; under TP 32 x 4 exchanges + the argmax-key exchange (NVLink one-shot kernels)
+        # advance; under TP 32 x 2 exchange launches + the argmax-key exchange (NVLink one-shot)
+        # (the o / down exchanges run inside their bucketMul launches unless IAM_TP_FUSED=0)
         "gpu_launches": world * args.steps * (2 + 5 * cfg.n_layers + 2 +
-                                              ((4 * cfg.n_layers + 1) if world > 1 and
+                                              (((2 if os.environ.get("IAM_TP_FUSED", "1") != "0" else 4) *
+                                                cfg.n_layers + 1) if world > 1 and
                                                os.environ.get("IAM_TP_COLL", "p2p") != "nccl" else 0)),
         "clocks": clk.summary(),
     }

@@ -60,6 +60,7 @@ struct GHeader {
     float result;
     int it, total, staged, maxbin;
     int blo, bhi, wn;  // bins holding the order statistics around the target, values gathered
+    unsigned fepoch;   // tp_fused: the epoch of this launch's mailbox elements
 };
 
 constexpr size_t a16(size_t n) { return (n + 15) / 16 * 16; }
@@ -258,6 +259,41 @@ IAM_DEV void acc_chunk(const uint2* __restrict__ list, int n, int j0, int mw, co
     }
 }
 
+// Tensor-parallel exchange inside the kernel (tp_fused): element e of this rank's range partials
+// ([local range][M]) is stored into every peer's mailbox as one 8-byte {value bits, epoch} store
+// (seen whole: no fence, no flag); the reduction polls its own mailbox, bounded, until the
+// element of the awaited epoch is there.  Mailbox halves alternate by epoch parity: a rank can
+// only reach epoch e + 2 after every peer has finished the launch of epoch e.
+IAM_DEV uint2* fused_slot(const TpWindow& w, int owner, unsigned epoch, int src) {
+    return reinterpret_cast<uint2*>(w.base[owner] + w.fused_off) +
+           ((size_t)(epoch & 1u) * w.world + src) * (size_t)w.fused_floats;
+}
+
+IAM_DEV void fused_send(const TpWindow& w, unsigned epoch, int e, float v) {
+    for (int p = 0; p < w.world; ++p)
+        if (p != w.rank)
+            asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(fused_slot(w, p, epoch, w.rank) + e),
+                         "r"(__float_as_uint(v)), "r"(epoch)
+                         : "memory");
+}
+
+// Element e of rank src's partials for this launch (bounded wait; on a timeout the window's
+// error word is set and 0 returned, and later waits do not wait).
+IAM_DEV float fused_recv(const TpWindow& w, unsigned epoch, int src, int e) {
+    volatile unsigned* err = reinterpret_cast<volatile unsigned*>(w.base[w.rank] + w.err_off);
+    const uint2* q = fused_slot(w, w.rank, epoch, src) + e;
+    for (long long n = 0;; ++n) {
+        uint2 v;
+        asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(q) : "memory");
+        if (v.y == epoch) return __uint_as_float(v.x);
+        if (n > w.spin_limit || *err != 0u) {
+            *err = 1u;
+            return 0.0f;
+        }
+        if (n > 64) __nanosleep(32);
+    }
+}
+
 // The dense stream of one CTA (tile = dense_rows output rows, range of rin <= 1024 inputs, rin a
 // multiple of 8): a lane holds x and the selection masks of inputs 8*lane + 256c .. + 8 in
 // registers; each warp takes output rows tile_begin + warp + 16j, reads the row's range with
@@ -268,7 +304,8 @@ IAM_DEV void acc_chunk(const uint2* __restrict__ list, int n, int j0, int mw, co
 // lane adds its products in input order, then the warp sums the lanes (xor tree): the sum
 // depends on the range only.  Writes the range's partial of each output.
 IAM_DEV void dense_rows_stream(const BGProblem& pr, const float* xr, const uint16_t* mask, int rin, int i0, int tile,
-                               int M, float* part, int warp, int lane) {
+                               int M, float* part, int warp, int lane, const BGBatch& b, unsigned fepoch,
+                               int range) {
     constexpr int NCH = 4;
     float xv[NCH][8];
     uint32_t mk[NCH][4];
@@ -335,7 +372,11 @@ IAM_DEV void dense_rows_stream(const BGProblem& pr, const float* xr, const uint1
         }
         if (lane == 0) {
             part[o] = acc0;
-            if (two) part[o + kGW] = acc1;
+            if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o, acc0);
+            if (two) {
+                part[o + kGW] = acc1;
+                if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o + kGW, acc1);
+            }
         }
     }
 }
@@ -410,6 +451,8 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     }
     for (int k = tid; k < kNB; k += kGT) hist[k] = 0;
     pdl_wait();  // from here on: x, residuals written by earlier kernels
+    if (b.tp_fused && tid == 0)  // the previous fused launch's epoch, written after its barrier
+        h.fepoch = *reinterpret_cast<const volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) + 1u;
 
     const auto xp = GProvider<XM>::make(pr, h.red);
 
@@ -687,7 +730,7 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
 
     float* part = pr.partials + (size_t)range * M;
     if constexpr (DN) {
-        dense_rows_stream(pr, xr, mask, rin, i0, tile, M, part, warp, lane);
+        dense_rows_stream(pr, xr, mask, rin, i0, tile, M, part, warp, lane, b, h.fepoch, range);
         debug_stamp(tr, 4);
     } else {
     // ---- 4. accumulation: list position j goes to set j % NSETS = (warp, row lane)
@@ -745,7 +788,10 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
             const float other = __shfl_down_sync(0xffffffffu, s, 16);  // row lane 1 of the same column
             s = s + other;
         }
-        if (ln < COLL && tile * TW + o / 16 < pr.cols) part[(size_t)tile * kOut + o] = s;
+        if (ln < COLL && tile * TW + o / 16 < pr.cols) {
+            part[(size_t)tile * kOut + o] = s;
+            if (b.tp_fused) fused_send(b.tp, h.fepoch, range * M + tile * kOut + o, s);
+        }
     }
     }
     int* rows_of = reinterpret_cast<int*>(pr.partials + (size_t)R * M);
@@ -773,17 +819,22 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     const int o0 = (int)((long long)local * M / nc), o1 = (int)((long long)(local + 1) * M / nc);
     const int no = o1 - o0;
     float* red = acc;  // [kRedFloats]: partials staged so that all loads are in flight together
-    const int per_pass = max(1, kRedFloats / R);
+    // tp_fused: the ranges of every rank, rank r holding global ranges r * R .. r * R + R - 1
+    const int RG = b.tp_fused ? R * b.tp.world : R;
+    const int per_pass = max(1, kRedFloats / RG);
     for (int p0 = 0; p0 < no; p0 += per_pass) {
         const int pn = min(per_pass, no - p0);
-        for (int k = tid; k < pn * R; k += kGT) {
-            const int r = k / pn, oo = k - r * pn;
-            red[oo * R + r] = __ldcg(pr.partials + (size_t)r * M + o0 + p0 + oo);
+        for (int k = tid; k < pn * RG; k += kGT) {
+            const int g = k / pn, oo = k - g * pn;
+            const int owner = g / R, lr = g - owner * R;
+            const int e = lr * M + o0 + p0 + oo;
+            red[oo * RG + g] = (!b.tp_fused || owner == b.tp.rank) ? __ldcg(pr.partials + e)
+                                                                    : fused_recv(b.tp, h.fepoch, owner, e);
         }
         __syncthreads();
         for (int oo = tid; oo < pn; oo += kGT) {
             float s = 0.0f;
-            for (int r = 0; r < R; ++r) s += red[oo * R + r];
+            for (int r = 0; r < RG; ++r) s += red[oo * RG + r];
             const int o = o0 + p0 + oo;
             if (pr.residual) s = pr.residual[o] + s;  // add32 (bucketMul.cl:517-520)
             pr.out[o] = s;
@@ -791,6 +842,8 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
         __syncthreads();
     }
     if (local == 0 && tid == 0) {
+        if (b.tp_fused && pi == 0)  // every CTA read the previous epoch before the barrier
+            *reinterpret_cast<volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) = h.fepoch;
         int t = 0;
         for (int r = 0; r < R; ++r) t += __ldcg(rows_of + r);
         if (pr.count_out) *pr.count_out = t;

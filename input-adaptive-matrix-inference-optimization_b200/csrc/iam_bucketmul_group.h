@@ -9,6 +9,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
+#include "iam_tp.h"
 #include <stdint.h>
 
 namespace iam {
@@ -68,6 +70,10 @@ struct BGBatch {
     int pdl;                  // launched with programmatic stream serialization
     int dense;                // stream the dense copies (every weight, selected by rank) instead
                               // of the selected bucket rows: same selection, register accumulators
+    int tp_fused;             // tensor-parallel row-parallel launch (o, down): every range partial
+                              // also goes to each peer's mailbox (tp.fused_off), and the range
+                              // reduction adds the ranges of every rank in range order
+    TpWindow tp;              // tp_fused: the peers' windows
     int partials_only;        // write each range's partial (and its row count) and stop: the
                               // ranges are summed by the tensor-parallel exchange (tp_gather_reduce)
     unsigned* barrier;        // scratch: 4 words {arrivals, generation, error, -}, zeroed once

@@ -244,6 +244,7 @@ struct iam_model_s {
     long long* tp_tmp = nullptr;  // 2 int64 of device scratch for host-side agreements
     // one-shot NVLink collectives (IAM_TP_COLL=nccl: NCCL instead)
     bool tp_p2p = true;
+    bool tp_fused = true;       // o / down exchanges inside the bucketMul kernel (IAM_TP_FUSED=0: a launch after it)
     char* xwin = nullptr;         // this rank's window (exchanged activations, mailbox, flags)
     TpWindow win{};
     std::vector<void*> peer_maps;
@@ -343,6 +344,15 @@ int alloc_runtime(iam_model_s* m) {
         w.epoch_off = take(4 * kTpCtas);
         w.err_off = take(4);
         w.mbox_off = take((size_t)2 * m->tp_world * w.mbox_floats * 8);
+        // the o / down range partials exchanged inside the bucketMul kernel: ranges per rank x dim
+        // (the bucket path's fixed ranges or the dense stream's, whichever is more)
+        w.fused_floats = 1;
+        for (const int in : {qn, c.ffn_dim}) {
+            const int r = std::max(row_parallel_ranges(in, m->tp_world), bg_dense_ranges(in, true));
+            w.fused_floats = std::max(w.fused_floats, std::max(1, r / m->tp_world) * c.dim);
+        }
+        w.fused_off = take((size_t)2 * m->tp_world * w.fused_floats * 8);
+        w.fused_epoch_off = take(4);
         if ((rc = dalloc(m, &m->xwin, off))) return rc;
         IAM_CUDA_TRY(cudaMemset(m->xwin, 0, off));
         w.base[m->tp_rank] = m->xwin;
@@ -789,8 +799,15 @@ int build_plans(iam_model_s* m, float effort) {
                     p.cutoff_out = rec + CL.cut + kMats[bi][i];
                 }
             }
-            // under the NVLink exchanges the o and down ranges are summed by tp_gather_reduce
-            b.partials_only = (m->tp_world > 1 && m->tp_p2p && (bi == 1 || bi == 3)) ? 1 : 0;
+            // under the NVLink exchanges the o and down ranges of every rank are summed inside the
+            // kernel (tp_fused; IAM_TP_FUSED=0: by a tp_gather_reduce launch after it)
+            const bool rowp = m->tp_world > 1 && m->tp_p2p && m->use_group && (bi == 1 || bi == 3);
+            b.tp_fused = (rowp && m->tp_fused) ? 1 : 0;
+            b.partials_only = (rowp && !m->tp_fused) ? 1 : 0;
+            if (b.tp_fused) {
+                b.tp = m->win;
+                b.p[0].residual = bi == 1 ? m->x : m->x1;  // every rank adds it: every rank sums all ranges
+            }
             b.dense = effort >= m->dense_min_effort ? 1 : 0;
             for (int i = 0; i < b.nprob; ++i) {
                 const BGProblem& p = b.p[i];
@@ -889,6 +906,7 @@ int o_down_exchange(iam_model_s* m, int l, int bi, cudaStream_t s, bool pdl) {
     const iam_model_config& c = m->cfg;
     float* out = bi == 1 ? m->x1 : m->x;
     if (!m->use_group) return tp_allreduce_sum(m->win, woff(m, out), c.dim, s, pdl);
+    if (m->gplans[(size_t)l * 4 + bi].tp_fused) return IAM_OK;  // done inside the kernel
     const BGBatch& b = m->gplans[(size_t)l * 4 + bi];
     const BGProblem& p = b.p[0];
     return tp_gather_reduce(m->win, p.partials, c.dim, p.n_ranges, bi == 1 ? m->x : m->x1, out,
@@ -917,12 +935,16 @@ int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk
     if ((rc = hook(hk, IAM_KERNEL_ATTENTION, s))) return rc;
     if ((rc = launch_attention(ap, gq, s, pdl))) return rc;
     for (int b = 1; b < 4; ++b) {
-        if (m->tp_world > 1 && m->tp_p2p) {  // the exchange in front of launch b (NVLink one-shot)
-            if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
-            if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
-            else if (b == 2) rc = o_down_exchange(m, l, 1, s, pdl);
-            else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
-            if (rc) return rc;
+        if (m->tp_world > 1 && m->tp_p2p) {
+            // the exchange in front of launch b (NVLink one-shot); none after a fused o launch,
+            // which summed every rank's ranges itself
+            if (!(b == 2 && m->gplans[(size_t)l * 4 + 1].tp_fused)) {
+                if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
+                if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
+                else if (b == 2) rc = o_down_exchange(m, l, 1, s, pdl);
+                else rc = tp_allgather(m->win, woff(m, m->g), woff(m, m->u), m->ffn_local, s, pdl);
+                if (rc) return rc;
+            }
         } else if (m->tp_world > 1) {  // the exchange in front of launch b (NCCL)
             if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
             if (b == 1) rc = nccl_allgather(m, m->att, (size_t)m->n_heads_local * c.head_dim, s);
@@ -952,7 +974,7 @@ int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk
             if (b == 3) IAM_CUDA_TRY(cudaMemcpyAsync(rec + CL.outd, m->x, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
         }
     }
-    if (m->tp_world > 1) {
+    if (m->tp_world > 1 && !(m->tp_p2p && m->gplans[(size_t)l * 4 + 3].tp_fused)) {  // (down's: inside it)
         if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
         rc = m->tp_p2p ? o_down_exchange(m, l, 3, s, pdl) : nccl_allreduce_sum(m, m->x, c.dim, s);
         if (rc) return rc;
@@ -1176,6 +1198,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int ran
     if (const char* v = getenv("IAM_BM_KERNEL")) m->use_group = std::string(v) != "split";
     if (const char* v = getenv("IAM_TP_TIMEOUT_S")) m->tp_timeout_s = atof(v);
     if (const char* v = getenv("IAM_TP_COLL")) m->tp_p2p = std::string(v) != "nccl";
+    if (const char* v = getenv("IAM_TP_FUSED")) m->tp_fused = std::string(v) != "0";
     m->n_heads_local = cfg->n_heads / world;
     m->n_kv_local = cfg->n_kv_heads / world;
     m->ffn_local = cfg->ffn_dim / world;

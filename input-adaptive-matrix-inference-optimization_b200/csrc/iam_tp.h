@@ -25,6 +25,10 @@ struct TpWindow {
     size_t mbox_off;          // uint2 [2][world][mbox_floats]: {value bits, epoch} from rank r
     int mbox_floats;          // elements per mailbox slot
     long long spin_limit;     // polls of one element before a wait gives up (kTpSpinLimit by default)
+    // the mailbox of the exchanges done inside the bucketMul kernel (the o / down range
+    // partials): uint2 [2][world][fused_floats], and the epoch of the last such launch (u32)
+    size_t fused_off, fused_epoch_off;
+    int fused_floats;
 };
 
 // Default poll bound of a wait (~1 s on a B200 with the back-off of the poll loop).
