@@ -346,6 +346,13 @@ def decode_config(args, cfg, world):
             "l2": "inputs larger than L2: 13.9 GB of bucket weights streamed per token"}
 
 
+def tp_exchanges_per_layer():
+    """Exchange launches per decoder layer under the NVLink tensor-parallel path."""
+    if os.environ.get("IAM_TP_FUSED", "1") == "0":
+        return 4
+    return 2 if os.environ.get("IAM_TP_PUSH", "1") == "0" else 0
+
+
 def run_decode(args, rank, world):
     import torch
     iam = load_pkg()
@@ -488,11 +495,12 @@ def run_decode(args, rank, world):
         "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab},
         # ours per step and rank: embed, key clear, 32 x (4 bucketMul + attention), LM head,
-        # advance; under TP 32 x 2 exchange launches + the argmax-key exchange (NVLink one-shot)
-        # (the o / down exchanges run inside their bucketMul launches unless IAM_TP_FUSED=0)
+        # advance; under TP the argmax-key exchange (NVLink one-shot) and, per layer, no
+        # exchange launch (the o / down partials are exchanged inside their bucketMul launches,
+        # heads and gate/up slices pushed by their producers), 2 with IAM_TP_PUSH=0, 4 with
+        # IAM_TP_FUSED=0
         "gpu_launches": world * args.steps * (2 + 5 * cfg.n_layers + 2 +
-                                              (((2 if os.environ.get("IAM_TP_FUSED", "1") != "0" else 4) *
-                                                cfg.n_layers + 1) if world > 1 and
+                                              ((tp_exchanges_per_layer() * cfg.n_layers + 1) if world > 1 and
                                                os.environ.get("IAM_TP_COLL", "p2p") != "nccl" else 0)),
         "clocks": clk.summary(),
     }

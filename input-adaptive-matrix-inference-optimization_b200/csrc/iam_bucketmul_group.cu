@@ -34,6 +34,7 @@
 #include "iam_bucketmul.cuh"
 #include "iam_bucketmul_group.h"
 #include "iam_bucketmul_launch.h"
+#include "iam_tp_push.cuh"
 
 namespace iam {
 
@@ -85,24 +86,91 @@ __host__ __device__ inline GOffsets g_offsets(int range_max, bool stage) {
     return o;
 }
 
+// The inputs other ranks made, when they are pushed (tp_wait): read from this rank's mailbox of
+// that kind, polled until they carry the launch's epoch.  w == nullptr: every input is local.
+struct PullIn {
+    const TpWindow* w;
+    int kind, lo, hi;  // this rank's inputs [lo, hi)
+    unsigned epoch;
+    IAM_DEV bool remote(int i) const { return w && (i < lo || i >= hi); }
+    IAM_DEV bool local8(int i) const { return !w || (i >= lo && i + 8 <= hi); }
+    IAM_DEV float get(size_t idx) const { return tp_push_recv(*w, kind, idx, epoch); }
+    // elements idx .. idx + 7 (idx even): all eight loads in flight, then a poll of any late one
+    IAM_DEV void get8(size_t idx, float* o) const {
+        const uint4* q = reinterpret_cast<const uint4*>(tp_push_mbox(*w, w->rank, kind) + idx);
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[k].x), "=r"(v[k].y), "=r"(v[k].z), "=r"(v[k].w)
+                         : "l"(q + k)
+                         : "memory");
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            o[2 * k] = v[k].y == epoch ? __uint_as_float(v[k].x) : get(idx + 2 * k);
+            o[2 * k + 1] = v[k].w == epoch ? __uint_as_float(v[k].z) : get(idx + 2 * k + 1);
+        }
+    }
+};
+
+struct GXPlain {
+    static constexpr bool kVectorizable = true;
+    XPlain base;
+    PullIn in;
+    IAM_DEV float operator()(int i) const { return in.remote(i) ? in.get((size_t)i) : base(i); }
+    IAM_DEV bool aligned16() const { return base.aligned16(); }
+    IAM_DEV void load8(int i, float* o) const {
+        if (in.local8(i)) base.load8(i, o);
+        else if (!in.remote(i) || !in.remote(i + 7)) {  // straddles this rank's inputs
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = (*this)(i + e);
+        } else {
+            in.get8((size_t)i, o);
+        }
+    }
+};
+
+struct GXSilu {
+    static constexpr bool kVectorizable = true;
+    XSilu base;
+    PullIn in;
+    IAM_DEV float operator()(int i) const {
+        return in.remote(i) ? XSilu::f(in.get((size_t)i), in.get((size_t)in.w->pmb_ffn + i)) : base(i);
+    }
+    IAM_DEV bool aligned16() const { return base.aligned16(); }
+    IAM_DEV void load8(int i, float* o) const {
+        if (in.local8(i)) base.load8(i, o);
+        else if (!in.remote(i) || !in.remote(i + 7)) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = (*this)(i + e);
+        } else {
+            float g[8], u[8];
+            in.get8((size_t)i, g);
+            in.get8((size_t)in.w->pmb_ffn + i, u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = XSilu::f(g[e], u[e]);
+        }
+    }
+};
+
 template <int XM>
 struct GProvider;
 template <>
 struct GProvider<kXPlain> {
-    using T = XPlain;
-    static IAM_DEV T make(const BGProblem& p, float*) { return XPlain{p.x}; }
+    using T = GXPlain;
+    static IAM_DEV T make(const BGProblem& p, float*, const PullIn& in) { return GXPlain{XPlain{p.x}, in}; }
 };
 template <>
 struct GProvider<kXRms> {
     using T = XRms;
-    static IAM_DEV T make(const BGProblem& p, float* red) {
+    static IAM_DEV T make(const BGProblem& p, float* red, const PullIn&) {
         return XRms{p.x, p.gain, block_rms_scale<kGT>(p.x, p.norm_n, p.norm_eps, red)};
     }
 };
 template <>
 struct GProvider<kXSilu> {
-    using T = XSilu;
-    static IAM_DEV T make(const BGProblem& p, float*) { return XSilu{p.x, p.x2}; }
+    using T = GXSilu;
+    static IAM_DEV T make(const BGProblem& p, float*, const PullIn& in) { return GXSilu{XSilu{p.x, p.x2}, in}; }
 };
 
 // Bin of v: monotone non-decreasing in v (a fixed subtraction and a multiplication by a
@@ -453,8 +521,13 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     pdl_wait();  // from here on: x, residuals written by earlier kernels
     if (b.tp_fused && tid == 0)  // the previous fused launch's epoch, written after its barrier
         h.fepoch = *reinterpret_cast<const volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) + 1u;
+    // pushed inputs: this launch's epoch (the kind's consumed count + 1, read before the barrier)
+    const unsigned push_epoch =
+        b.tp_push ? tp_push_epoch(b.tp, b.tp_push - 1) : (b.tp_wait ? tp_push_epoch(b.tp, b.tp_wait - 1) : 0u);
+    PullIn pin{nullptr, 0, 0, 0, 0u};
+    if (b.tp_wait) pin = PullIn{&b.tp, b.tp_wait - 1, pr.in_begin, pr.in_begin + pr.n_in, push_epoch};
 
-    const auto xp = GProvider<XM>::make(pr, h.red);
+    const auto xp = GProvider<XM>::make(pr, h.red, pin);
 
     // ---- 1. cutoff values: thread t owns x[8t, 8t + 8)
     float v[kVPT];
@@ -838,12 +911,15 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
             const int o = o0 + p0 + oo;
             if (pr.residual) s = pr.residual[o] + s;  // add32 (bucketMul.cl:517-520)
             pr.out[o] = s;
+            if (b.tp_push && pr.out_begin + o < b.push_limit)
+                tp_push_send(b.tp, b.tp_push - 1, (size_t)pi * b.tp.pmb_ffn + pr.out_begin + o, s, push_epoch);
         }
         __syncthreads();
     }
     if (local == 0 && tid == 0) {
         if (b.tp_fused && pi == 0)  // every CTA read the previous epoch before the barrier
             *reinterpret_cast<volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) = h.fepoch;
+        if (b.tp_wait && pi == 0) tp_push_consumed(b.tp, b.tp_wait - 1, push_epoch);  // (likewise)
         int t = 0;
         for (int r = 0; r < R; ++r) t += __ldcg(rows_of + r);
         if (pr.count_out) *pr.count_out = t;
@@ -1086,6 +1162,8 @@ int bg_launch(const BGBatch& b0, cudaStream_t s) {
             return fail(IAM_ERR_ARG, "bucketmul: dense stream needs aligned rows and ranges of <= 1024 inputs "
                                      "(a multiple of 8)");
     }
+    if ((b.tp_push || b.tp_wait) && (b.partials_only || b.tp.world < 2 || (b.tp_push && b.tp_wait)))
+        return fail(IAM_ERR_ARG, "bucketmul: pushed inputs or outputs need the range reduction and a peer window");
     const int ctas = bg_plan(b);
     if (ctas > sm_count_current())
         return fail(IAM_ERR_UNSUPPORTED, "bucketmul: the launch needs more CTAs than SMs (one wave)");

@@ -59,6 +59,7 @@ struct BGProblem {
     int range_max;            // most inputs in one range (bg_plan)
     int n_tiles;              // column tiles (bg_plan)
     int cta_begin;            // first CTA of this problem in the launch (bg_plan)
+    int out_begin;            // global index of out[0] (column-parallel shards; tp_push)
 };
 
 struct BGBatch {
@@ -73,7 +74,12 @@ struct BGBatch {
     int tp_fused;             // tensor-parallel row-parallel launch (o, down): every range partial
                               // also goes to each peer's mailbox (tp.fused_off), and the range
                               // reduction adds the ranges of every rank in range order
-    TpWindow tp;              // tp_fused: the peers' windows
+    TpWindow tp;              // tp_fused / tp_push / tp_wait: the peers' windows
+    int tp_push;              // 1 + kind: outputs at global index out_begin + o below push_limit
+    int push_limit;           // also go to every peer's mailbox of that kind (iam_tp_push.cuh),
+                              // problem i at offset i * tp.pmb_ffn; 0: none
+    int tp_wait;              // 1 + kind: x outside this rank's inputs [in_begin, in_begin + n_in)
+                              // is read from this rank's mailbox of that kind (x2 at + pmb_ffn)
     int partials_only;        // write each range's partial (and its row count) and stop: the
                               // ranges are summed by the tensor-parallel exchange (tp_gather_reduce)
     unsigned* barrier;        // scratch: 4 words {arrivals, generation, error, -}, zeroed once

@@ -13,6 +13,7 @@
 
 #include "iam_bucketmul.cuh"
 #include "iam_layers.h"
+#include "iam_tp_push.cuh"
 
 namespace iam {
 
@@ -534,13 +535,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
     }
     __syncthreads();
     float* stat = p.part + ((size_t)(kvh * p.n_split + s) * GQ) * (HD + 2);
+    const unsigned push_epoch = p.tp_push ? tp_push_epoch(p.tp, kTpPushHeads) : 0u;
     for (int idx = tid; idx < GQ * HD; idx += kAttnThreads) {
         const int j = idx / HD, d = idx % HD;
         const float M = sM[j], L = sL[j];
         float O = 0.0f;
         for (int h = 0; h < nslots; ++h) O = fmaf(cm[h * GQ + j], co[(h * GQ + j) * HD + d], O);
         if (active == 1) {
-            p.out[(size_t)(kvh * GQ + j) * HD + d] = __fdiv_rn(O, L);
+            const int gi = (kvh * GQ + j) * HD + d;
+            p.out[gi] = __fdiv_rn(O, L);
+            if (p.tp_push && p.push_begin + gi < p.push_limit)
+                tp_push_send(p.tp, kTpPushHeads, (size_t)(p.push_begin + gi), __fdiv_rn(O, L), push_epoch);
         } else {
             if (d == 0) {
                 stat[j * (HD + 2)] = M;
@@ -596,7 +601,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnParams p
             float O = 0.0f;
 #pragma unroll 8
             for (int r = 0; r < active; ++r) O = fmaf(wgt[j * p.n_split + r], part_at(r * PER + j * (HD + 2) + 2 + d), O);
-            p.out[(size_t)(kvh * GQ + j) * HD + d] = O;
+            const int gi = (kvh * GQ + j) * HD + d;
+            p.out[gi] = O;
+            if (p.tp_push && p.push_begin + gi < p.push_limit)
+                tp_push_send(p.tp, kTpPushHeads, (size_t)(p.push_begin + gi), O, push_epoch);
         }
     };
     if (staged) combine([&](int i) { return co[i]; });

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "iam_tp.h"
+
 namespace iam {
 
 constexpr int kAttnThreads = 256;   // 16 half-warps
@@ -29,6 +31,10 @@ struct AttnParams {
     int min_chunk;         // context tokens per CTA at least
     int lane_min_ctx;      // contexts of this many tokens or more take the tensor-core layout,
     int lane_short_max;    // and so do contexts of at most this many (in one chunk per KV head)
+    int tp_push;           // tensor parallel: head outputs at global index push_begin + i below
+    int push_begin;        // push_limit also go to every peer's mailbox (kTpPushHeads)
+    int push_limit;
+    TpWindow tp;
 };
 
 struct LMHeadParams {

@@ -245,6 +245,7 @@ struct iam_model_s {
     // one-shot NVLink collectives (IAM_TP_COLL=nccl: NCCL instead)
     bool tp_p2p = true;
     bool tp_fused = true;       // o / down exchanges inside the bucketMul kernel (IAM_TP_FUSED=0: a launch after it)
+    bool tp_push = true;        // heads and gate/up slices pushed by their producers (IAM_TP_PUSH=0: all-gathers)
     char* xwin = nullptr;         // this rank's window (exchanged activations, mailbox, flags)
     TpWindow win{};
     std::vector<void*> peer_maps;
@@ -306,6 +307,12 @@ std::vector<float> rope_table(const iam_model_config& c) {
     return t;
 }
 
+// Tensor-parallel inputs of o and down pushed by their producing kernels (NVLink exchanges,
+// the range kernel with its exchange inside, IAM_TP_PUSH unset or not 0).
+bool push_mode(const iam_model_s* m) {
+    return m->tp_world > 1 && m->tp_p2p && m->use_group && m->tp_fused && m->tp_push;
+}
+
 int alloc_runtime(iam_model_s* m) {
     const iam_model_config& c = m->cfg;
     const int hd = c.head_dim;
@@ -353,6 +360,11 @@ int alloc_runtime(iam_model_s* m) {
         }
         w.fused_off = take((size_t)2 * m->tp_world * w.fused_floats * 8);
         w.fused_epoch_off = take(4);
+        w.xin_off = take(4 * kTpPushKinds);
+        // pushed inputs (iam_tp_push.cuh): every head, and gate / up (the cutoff prefix of down)
+        w.pmb_ffn = c.ffn_dim;
+        w.pmb_off[kTpPushHeads] = take((size_t)qn * 8);
+        w.pmb_off[kTpPushFfn] = take((size_t)2 * w.pmb_ffn * 8);
         if ((rc = dalloc(m, &m->xwin, off))) return rc;
         IAM_CUDA_TRY(cudaMemset(m->xwin, 0, off));
         w.base[m->tp_rank] = m->xwin;
@@ -814,6 +826,19 @@ int build_plans(iam_model_s* m, float effort) {
                 if (!p.dense || bg_dense_ranges(p.full_in, p.fixed_ranges > 0) == 0) b.dense = 0;
             }
             bg_choose_shape(b);
+            // the heads and the gate/up values of every rank that o and down read for their
+            // cutoff (the first P inputs), pushed by the attention and gate/up launches into every
+            // peer's mailbox; o and down read the ones other ranks made from their own mailbox
+            if (push_mode(m) && bi >= 1) {
+                b.tp = m->win;
+                if (bi == 1) b.tp_wait = 1 + kTpPushHeads;
+                if (bi == 3) b.tp_wait = 1 + kTpPushFfn;
+                if (bi == 2) {
+                    b.tp_push = 1 + kTpPushFfn;
+                    b.push_limit = m->plans[(size_t)l * 4 + 3].p[0].P;  // down's cutoff prefix
+                    for (int i = 0; i < b.nprob; ++i) b.p[i].out_begin = m->tp_rank * m->ffn_local;
+                }
+            }
         }
     m->plan_effort = effort;
     return IAM_OK;
@@ -872,6 +897,12 @@ AttnParams attn_params(iam_model_s* m, int l) {
     ap.min_chunk = m->att_min_chunk;
     ap.lane_min_ctx = m->att_lane_min;
     ap.lane_short_max = m->att_lane_short;
+    if (push_mode(m)) {  // every head goes to the peers (o's cutoff reads them all)
+        ap.tp_push = 1;
+        ap.tp = m->win;
+        ap.push_begin = m->tp_rank * m->n_heads_local * c.head_dim;
+        ap.push_limit = c.n_heads * c.head_dim;
+    }
     return ap;
 }
 
@@ -937,8 +968,8 @@ int enqueue_layer(iam_model_s* m, int l, bool pdl, cudaStream_t s, StepHooks* hk
     for (int b = 1; b < 4; ++b) {
         if (m->tp_world > 1 && m->tp_p2p) {
             // the exchange in front of launch b (NVLink one-shot); none after a fused o launch,
-            // which summed every rank's ranges itself
-            if (!(b == 2 && m->gplans[(size_t)l * 4 + 1].tp_fused)) {
+            // which summed every rank's ranges itself, and none of the pushed heads and slices
+            if (!(b == 2 && m->gplans[(size_t)l * 4 + 1].tp_fused) && !(b != 2 && push_mode(m))) {
                 if ((rc = hook(hk, IAM_KERNEL_COLLECTIVE, s))) return rc;
                 if (b == 1) rc = tp_allgather(m->win, woff(m, m->att), (size_t)-1, m->n_heads_local * c.head_dim, s, pdl);
                 else if (b == 2) rc = o_down_exchange(m, l, 1, s, pdl);
@@ -1199,6 +1230,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int ran
     if (const char* v = getenv("IAM_TP_TIMEOUT_S")) m->tp_timeout_s = atof(v);
     if (const char* v = getenv("IAM_TP_COLL")) m->tp_p2p = std::string(v) != "nccl";
     if (const char* v = getenv("IAM_TP_FUSED")) m->tp_fused = std::string(v) != "0";
+    if (const char* v = getenv("IAM_TP_PUSH")) m->tp_push = std::string(v) != "0";
     m->n_heads_local = cfg->n_heads / world;
     m->n_kv_local = cfg->n_kv_heads / world;
     m->ffn_local = cfg->ffn_dim / world;

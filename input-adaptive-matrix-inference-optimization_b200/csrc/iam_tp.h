@@ -29,7 +29,16 @@ struct TpWindow {
     // partials): uint2 [2][world][fused_floats], and the epoch of the last such launch (u32)
     size_t fused_off, fused_epoch_off;
     int fused_floats;
+    // inputs pushed by their producing kernels (iam_tp_push.cuh): u32 [kTpPushKinds] epochs
+    // consumed so far, and per kind a mailbox of uint2 {value bits, epoch}: the heads
+    // [n_heads * head_dim], the gate/up values [2][pmb_ffn] (gate, then up)
+    size_t xin_off;
+    size_t pmb_off[2];
+    int pmb_ffn;
 };
+
+// Kinds of pushed activations: the attention heads (o's input), the gate/up slices (down's).
+constexpr int kTpPushHeads = 0, kTpPushFfn = 1, kTpPushKinds = 2;
 
 // Default poll bound of a wait (~1 s on a B200 with the back-off of the poll loop).
 constexpr long long kTpSpinLimit = 1LL << 21;
