@@ -161,17 +161,15 @@ __device__ float block_find_cutoff(const XP& xp, const uint16_t* __restrict__ pr
 
 // Every provider also offers load8 (8 consecutive values, 16-byte aligned) for the cutoff's
 // vector loads; kVectorizable says whether that path is worth taking.
-// x = a plain fp32 vector.  XPlain and XSilu read their activations through L2 (__ldcg), not
-// the read-only path: under tensor parallelism a peer stores them into this GPU's memory while
-// the launch runs (before its arrival wait), so they are not read-only for the kernel's life.
+// x = a plain fp32 vector.
 struct XPlain {
     static constexpr bool kVectorizable = true;
     const float* x;
-    IAM_DEV float operator()(int i) const { return __ldcg(x + i); }
+    IAM_DEV float operator()(int i) const { return __ldg(x + i); }
     IAM_DEV bool aligned16() const { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; }
     IAM_DEV void load8(int i, float* o) const {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(x + i));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(x + i + 4));
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x + i));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(x + i + 4));
         o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
         o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
     }
@@ -210,15 +208,15 @@ struct XSilu {
     const float* gate;
     const float* up;
     static IAM_DEV float f(float gv, float uv) { return __fdiv_rn(__fmul_rn(uv, gv), __fadd_rn(1.0f, expf(-gv))); }
-    IAM_DEV float operator()(int i) const { return f(__ldcg(gate + i), __ldcg(up + i)); }
+    IAM_DEV float operator()(int i) const { return f(__ldg(gate + i), __ldg(up + i)); }
     IAM_DEV bool aligned16() const {
         return ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up)) & 15u) == 0;
     }
     IAM_DEV void load8(int i, float* o) const {
-        const float4 g0 = __ldcg(reinterpret_cast<const float4*>(gate + i));
-        const float4 g1 = __ldcg(reinterpret_cast<const float4*>(gate + i + 4));
-        const float4 u0 = __ldcg(reinterpret_cast<const float4*>(up + i));
-        const float4 u1 = __ldcg(reinterpret_cast<const float4*>(up + i + 4));
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + i));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + i + 4));
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(up + i));
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(up + i + 4));
         const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll

@@ -113,14 +113,24 @@ struct PullIn {
     }
 };
 
+// Tensor-parallel x: the local inputs through L2 (__ldcg), not the read-only path -- a peer
+// stores this GPU's pushed inputs while the launch runs, so x is not read-only for the
+// kernel's life -- and the others from the mailbox.
+IAM_DEV void ldcg8(const float* p, float* o) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
 struct GXPlain {
     static constexpr bool kVectorizable = true;
-    XPlain base;
+    const float* x;
     PullIn in;
-    IAM_DEV float operator()(int i) const { return in.remote(i) ? in.get((size_t)i) : base(i); }
-    IAM_DEV bool aligned16() const { return base.aligned16(); }
+    IAM_DEV float operator()(int i) const { return in.remote(i) ? in.get((size_t)i) : __ldcg(x + i); }
+    IAM_DEV bool aligned16() const { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; }
     IAM_DEV void load8(int i, float* o) const {
-        if (in.local8(i)) base.load8(i, o);
+        if (in.local8(i)) ldcg8(x + i, o);
         else if (!in.remote(i) || !in.remote(i + 7)) {  // straddles this rank's inputs
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (*this)(i + e);
@@ -132,45 +142,58 @@ struct GXPlain {
 
 struct GXSilu {
     static constexpr bool kVectorizable = true;
-    XSilu base;
+    const float* gate;
+    const float* up;
     PullIn in;
     IAM_DEV float operator()(int i) const {
-        return in.remote(i) ? XSilu::f(in.get((size_t)i), in.get((size_t)in.w->pmb_ffn + i)) : base(i);
+        return in.remote(i) ? XSilu::f(in.get((size_t)i), in.get((size_t)in.w->pmb_ffn + i))
+                            : XSilu::f(__ldcg(gate + i), __ldcg(up + i));
     }
-    IAM_DEV bool aligned16() const { return base.aligned16(); }
+    IAM_DEV bool aligned16() const {
+        return ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up)) & 15u) == 0;
+    }
     IAM_DEV void load8(int i, float* o) const {
-        if (in.local8(i)) base.load8(i, o);
-        else if (!in.remote(i) || !in.remote(i + 7)) {
+        float g[8], u[8];
+        if (in.local8(i)) {
+            ldcg8(gate + i, g);
+            ldcg8(up + i, u);
+        } else if (!in.remote(i) || !in.remote(i + 7)) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (*this)(i + e);
+            return;
         } else {
-            float g[8], u[8];
             in.get8((size_t)i, g);
             in.get8((size_t)in.w->pmb_ffn + i, u);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = XSilu::f(g[e], u[e]);
         }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = XSilu::f(g[e], u[e]);
     }
 };
 
-template <int XM>
+// x of a launch; TPX (a tensor-parallel launch) adds the reads of pushed inputs
+template <int XM, int TPX>
 struct GProvider;
 template <>
-struct GProvider<kXPlain> {
-    using T = GXPlain;
-    static IAM_DEV T make(const BGProblem& p, float*, const PullIn& in) { return GXPlain{XPlain{p.x}, in}; }
+struct GProvider<kXPlain, 0> {
+    static IAM_DEV XPlain make(const BGProblem& p, float*, const PullIn&) { return XPlain{p.x}; }
 };
 template <>
-struct GProvider<kXRms> {
-    using T = XRms;
-    static IAM_DEV T make(const BGProblem& p, float* red, const PullIn&) {
+struct GProvider<kXPlain, 1> {
+    static IAM_DEV GXPlain make(const BGProblem& p, float*, const PullIn& in) { return GXPlain{p.x, in}; }
+};
+template <int TPX>
+struct GProvider<kXRms, TPX> {
+    static IAM_DEV XRms make(const BGProblem& p, float* red, const PullIn&) {
         return XRms{p.x, p.gain, block_rms_scale<kGT>(p.x, p.norm_n, p.norm_eps, red)};
     }
 };
 template <>
-struct GProvider<kXSilu> {
-    using T = GXSilu;
-    static IAM_DEV T make(const BGProblem& p, float*, const PullIn& in) { return GXSilu{XSilu{p.x, p.x2}, in}; }
+struct GProvider<kXSilu, 0> {
+    static IAM_DEV XSilu make(const BGProblem& p, float*, const PullIn&) { return XSilu{p.x, p.x2}; }
+};
+template <>
+struct GProvider<kXSilu, 1> {
+    static IAM_DEV GXSilu make(const BGProblem& p, float*, const PullIn& in) { return GXSilu{p.x, p.x2, in}; }
 };
 
 // Bin of v: monotone non-decreasing in v (a fixed subtraction and a multiplication by a
@@ -371,6 +394,7 @@ IAM_DEV float fused_recv(const TpWindow& w, unsigned epoch, int src, int e) {
 // stored word with the output's slot (o mod 16) as the low 4 (bucketMul.cl:419-425).  Per row a
 // lane adds its products in input order, then the warp sums the lanes (xor tree): the sum
 // depends on the range only.  Writes the range's partial of each output.
+template <int TPX>
 IAM_DEV void dense_rows_stream(const BGProblem& pr, const float* xr, const uint16_t* mask, int rin, int i0, int tile,
                                int M, float* part, int warp, int lane, const BGBatch& b, unsigned fepoch,
                                int range) {
@@ -440,16 +464,20 @@ IAM_DEV void dense_rows_stream(const BGProblem& pr, const float* xr, const uint1
         }
         if (lane == 0) {
             part[o] = acc0;
-            if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o, acc0);
+            if constexpr (TPX) {
+                if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o, acc0);
+            }
             if (two) {
                 part[o + kGW] = acc1;
-                if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o + kGW, acc1);
+                if constexpr (TPX) {
+                    if (b.tp_fused) fused_send(b.tp, fepoch, range * M + o + kGW, acc1);
+                }
             }
         }
     }
 }
 
-template <int ROWL, int XM, int DN>
+template <int ROWL, int XM, int DN, int TPX>
 __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBatch b) {
     constexpr int COLL = 32 / ROWL, NSETS = kGW * ROWL;
     static_assert(kChunk % NSETS == 0, "chunks keep the set of every row");
@@ -519,15 +547,18 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     }
     for (int k = tid; k < kNB; k += kGT) hist[k] = 0;
     pdl_wait();  // from here on: x, residuals written by earlier kernels
-    if (b.tp_fused && tid == 0)  // the previous fused launch's epoch, written after its barrier
-        h.fepoch = *reinterpret_cast<const volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) + 1u;
-    // pushed inputs: this launch's epoch (the kind's consumed count + 1, read before the barrier)
-    const unsigned push_epoch =
-        b.tp_push ? tp_push_epoch(b.tp, b.tp_push - 1) : (b.tp_wait ? tp_push_epoch(b.tp, b.tp_wait - 1) : 0u);
+    unsigned push_epoch = 0u;
     PullIn pin{nullptr, 0, 0, 0, 0u};
-    if (b.tp_wait) pin = PullIn{&b.tp, b.tp_wait - 1, pr.in_begin, pr.in_begin + pr.n_in, push_epoch};
+    if constexpr (TPX) {
+        if (b.tp_fused && tid == 0)  // the previous fused launch's epoch, written after its barrier
+            h.fepoch = *reinterpret_cast<const volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) + 1u;
+        // pushed inputs: this launch's epoch (the kind's consumed count + 1, read before the barrier)
+        push_epoch =
+            b.tp_push ? tp_push_epoch(b.tp, b.tp_push - 1) : (b.tp_wait ? tp_push_epoch(b.tp, b.tp_wait - 1) : 0u);
+        if (b.tp_wait) pin = PullIn{&b.tp, b.tp_wait - 1, pr.in_begin, pr.in_begin + pr.n_in, push_epoch};
+    }
 
-    const auto xp = GProvider<XM>::make(pr, h.red, pin);
+    const auto xp = GProvider<XM, TPX>::make(pr, h.red, pin);
 
     // ---- 1. cutoff values: thread t owns x[8t, 8t + 8)
     float v[kVPT];
@@ -803,7 +834,7 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
 
     float* part = pr.partials + (size_t)range * M;
     if constexpr (DN) {
-        dense_rows_stream(pr, xr, mask, rin, i0, tile, M, part, warp, lane, b, h.fepoch, range);
+        dense_rows_stream<TPX>(pr, xr, mask, rin, i0, tile, M, part, warp, lane, b, h.fepoch, range);
         debug_stamp(tr, 4);
     } else {
     // ---- 4. accumulation: list position j goes to set j % NSETS = (warp, row lane)
@@ -863,7 +894,9 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
         }
         if (ln < COLL && tile * TW + o / 16 < pr.cols) {
             part[(size_t)tile * kOut + o] = s;
-            if (b.tp_fused) fused_send(b.tp, h.fepoch, range * M + tile * kOut + o, s);
+            if constexpr (TPX) {
+                if (b.tp_fused) fused_send(b.tp, h.fepoch, range * M + tile * kOut + o, s);
+            }
         }
     }
     }
@@ -892,34 +925,61 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     const int o0 = (int)((long long)local * M / nc), o1 = (int)((long long)(local + 1) * M / nc);
     const int no = o1 - o0;
     float* red = acc;  // [kRedFloats]: partials staged so that all loads are in flight together
-    // tp_fused: the ranges of every rank, rank r holding global ranges r * R .. r * R + R - 1
-    const int RG = b.tp_fused ? R * b.tp.world : R;
-    const int per_pass = max(1, kRedFloats / RG);
-    for (int p0 = 0; p0 < no; p0 += per_pass) {
-        const int pn = min(per_pass, no - p0);
-        for (int k = tid; k < pn * RG; k += kGT) {
-            const int g = k / pn, oo = k - g * pn;
-            const int owner = g / R, lr = g - owner * R;
-            const int e = lr * M + o0 + p0 + oo;
-            red[oo * RG + g] = (!b.tp_fused || owner == b.tp.rank) ? __ldcg(pr.partials + e)
-                                                                    : fused_recv(b.tp, h.fepoch, owner, e);
+    if constexpr (!TPX) {
+        const int per_pass = max(1, kRedFloats / R);
+        for (int p0 = 0; p0 < no; p0 += per_pass) {
+            const int pn = min(per_pass, no - p0);
+            for (int k = tid; k < pn * R; k += kGT) {
+                const int r = k / pn, oo = k - r * pn;
+                red[oo * R + r] = __ldcg(pr.partials + (size_t)r * M + o0 + p0 + oo);
+            }
+            __syncthreads();
+            for (int oo = tid; oo < pn; oo += kGT) {
+                float s = 0.0f;
+                for (int r = 0; r < R; ++r) s += red[oo * R + r];
+                const int o = o0 + p0 + oo;
+                if (pr.residual) s = pr.residual[o] + s;  // add32 (bucketMul.cl:517-520)
+                pr.out[o] = s;
+            }
+            __syncthreads();
         }
-        __syncthreads();
-        for (int oo = tid; oo < pn; oo += kGT) {
-            float s = 0.0f;
-            for (int r = 0; r < RG; ++r) s += red[oo * RG + r];
-            const int o = o0 + p0 + oo;
-            if (pr.residual) s = pr.residual[o] + s;  // add32 (bucketMul.cl:517-520)
-            pr.out[o] = s;
-            if (b.tp_push && pr.out_begin + o < b.push_limit)
-                tp_push_send(b.tp, b.tp_push - 1, (size_t)pi * b.tp.pmb_ffn + pr.out_begin + o, s, push_epoch);
+    } else {
+        // tp_fused: the ranges of every rank, rank r holding global ranges r * R .. r * R + R - 1
+        // (this rank's from its partials, the others' from its mailbox, all loads first)
+        const int RG = b.tp_fused ? R * b.tp.world : R;
+        const int own = b.tp_fused ? b.tp.rank : 0;
+        const int per_pass = max(1, kRedFloats / RG);
+        for (int p0 = 0; p0 < no; p0 += per_pass) {
+            const int pn = min(per_pass, no - p0);
+            for (int k = tid; k < pn * R; k += kGT) {
+                const int r = k / pn, oo = k - r * pn;
+                red[oo * RG + own * R + r] = __ldcg(pr.partials + (size_t)r * M + o0 + p0 + oo);
+            }
+            if (b.tp_fused)
+                for (int k = tid; k < pn * RG; k += kGT) {
+                    const int g = k / pn, oo = k - g * pn;
+                    const int owner = g / R;
+                    if (owner != own) red[oo * RG + g] = fused_recv(b.tp, h.fepoch, owner, (g - owner * R) * M + o0 + p0 + oo);
+                }
+            __syncthreads();
+            for (int oo = tid; oo < pn; oo += kGT) {
+                float s = 0.0f;
+                for (int r = 0; r < RG; ++r) s += red[oo * RG + r];
+                const int o = o0 + p0 + oo;
+                if (pr.residual) s = pr.residual[o] + s;  // add32 (bucketMul.cl:517-520)
+                pr.out[o] = s;
+                if (b.tp_push && pr.out_begin + o < b.push_limit)
+                    tp_push_send(b.tp, b.tp_push - 1, (size_t)pi * b.tp.pmb_ffn + pr.out_begin + o, s, push_epoch);
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
     if (local == 0 && tid == 0) {
-        if (b.tp_fused && pi == 0)  // every CTA read the previous epoch before the barrier
-            *reinterpret_cast<volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) = h.fepoch;
-        if (b.tp_wait && pi == 0) tp_push_consumed(b.tp, b.tp_wait - 1, push_epoch);  // (likewise)
+        if constexpr (TPX) {
+            if (b.tp_fused && pi == 0)  // every CTA read the previous epoch before the barrier
+                *reinterpret_cast<volatile unsigned*>(b.tp.base[b.tp.rank] + b.tp.fused_epoch_off) = h.fepoch;
+            if (b.tp_wait && pi == 0) tp_push_consumed(b.tp, b.tp_wait - 1, push_epoch);  // (likewise)
+        }
         int t = 0;
         for (int r = 0; r < R; ++r) t += __ldcg(rows_of + r);
         if (pr.count_out) *pr.count_out = t;
@@ -938,29 +998,38 @@ __global__ void __launch_bounds__(kGT, 1) bg_kernel(const __grid_constant__ BGBa
     }
 }
 
-template <int ROWL, int XM, int DN>
+template <int ROWL, int XM, int DN, int TPX>
 cudaError_t bg_set_attrs() {
     static std::atomic<unsigned long long> done{0};
     return once_per_device(done, [] {
-        return cudaFuncSetAttribute(bg_kernel<ROWL, XM, DN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        return cudaFuncSetAttribute(bg_kernel<ROWL, XM, DN, TPX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024);
     });
 }
 
-template <int ROWL, int XM, int DN>
+template <int ROWL, int XM, int DN, int TPX>
 int bg_launch_t(const BGBatch& b, int ctas, size_t smem, cudaStream_t s) {
-    cudaError_t e = bg_set_attrs<ROWL, XM, DN>();
+    cudaError_t e = bg_set_attrs<ROWL, XM, DN, TPX>();
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bg_kernel)");
-    IAM_CUDA_TRY(launch_ex(bg_kernel<ROWL, XM, DN>, dim3((unsigned)ctas), dim3(kGT), smem, s, b.pdl != 0, b));
+    IAM_CUDA_TRY(launch_ex(bg_kernel<ROWL, XM, DN, TPX>, dim3((unsigned)ctas), dim3(kGT), smem, s, b.pdl != 0, b));
     return IAM_OK;
+}
+
+// The tensor-parallel exchanges (tp_fused, tp_push, tp_wait) live in their own instantiation:
+// a one-GPU launch compiles none of their code.
+template <int ROWL, int DN, int TPX>
+int bg_launch_xt(const BGBatch& b, int ctas, size_t smem, cudaStream_t s) {
+    switch (b.xmode) {
+        case kXRms: return bg_launch_t<ROWL, kXRms, DN, TPX>(b, ctas, smem, s);
+        case kXSilu: return bg_launch_t<ROWL, kXSilu, DN, TPX>(b, ctas, smem, s);
+        default: return bg_launch_t<ROWL, kXPlain, DN, TPX>(b, ctas, smem, s);
+    }
 }
 
 template <int ROWL, int DN>
 int bg_launch_x(const BGBatch& b, int ctas, size_t smem, cudaStream_t s) {
-    switch (b.xmode) {
-        case kXRms: return bg_launch_t<ROWL, kXRms, DN>(b, ctas, smem, s);
-        case kXSilu: return bg_launch_t<ROWL, kXSilu, DN>(b, ctas, smem, s);
-        default: return bg_launch_t<ROWL, kXPlain, DN>(b, ctas, smem, s);
-    }
+    if (b.tp_fused || b.tp_push || b.tp_wait) return bg_launch_xt<ROWL, DN, 1>(b, ctas, smem, s);
+    return bg_launch_xt<ROWL, DN, 0>(b, ctas, smem, s);
 }
 
 int bg_range_max(const BGBatch& b) {
