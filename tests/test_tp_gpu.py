@@ -1,7 +1,9 @@
 """Tensor-parallel decode on 2 GPUs (IAM_TP_TEST_WORLD=4 or 8 for more; one process per GPU,
 the library's NVLink exchanges) against the single-GPU model built from the same seed: the
 sharded weights are slices of the same bucketized matrices.  Skipped when the box has fewer
-GPUs than ranks.
+GPUs than ranks.  The default step exchanges everything inside its kernels; the second test
+runs the small model with the exchange launches put back (IAM_TP_PUSH=0: all-gathers of the
+heads and of gate/up; IAM_TP_FUSED=0: also the gather-reduce launches after o and down).
 """
 import datetime
 import os
@@ -68,8 +70,12 @@ def _teacher_forced(model, torch, cfg_d, effort, kv_prefix, seq):
     return np.stack(outs), np.stack(sels)  # logits [steps, vocab], counts [steps, layers, 7]
 
 
-def _rank_main(rank, world, port, outdir):
+CASES = (("small", SMALL, 3, (0.25, 0.5, 1.0), 0), ("mistral1", MISTRAL_1L, 11, (0.25,), 1024))
+
+
+def _rank_main(rank, world, port, outdir, env=None, cases=CASES):
     import sys
+    os.environ.update(env or {})  # read when a model is created
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import torch
@@ -80,8 +86,7 @@ def _rank_main(rank, world, port, outdir):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=180))
     res = {}
-    for name, cfg_d, seed, efforts, prefix in (("small", SMALL, 3, (0.25, 0.5, 1.0), 0),
-                                               ("mistral1", MISTRAL_1L, 11, (0.25,), 1024)):
+    for name, cfg_d, seed, efforts, prefix in cases:
         cfg = iam.ModelConfig.make(**cfg_d)
         seqs = {}
         if rank == 0:  # the unsharded model, same seed: its greedy tokens and logits
@@ -111,15 +116,16 @@ def rel_err(a, ref):
     return float(np.max(np.abs(a - ref)) / max(np.sqrt(np.mean(ref * ref)), 1e-30))
 
 
-def test_tp_matches_single_gpu(iam, cuda):
+def _check_identical(world, env=None, cases=CASES):
     import torch
     import torch.multiprocessing as mp
-    world = WORLD
     if torch.cuda.device_count() < world:
         pytest.skip(f"tensor-parallel test needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_rank_main, args=(world, _free_port(), d), nprocs=world, join=True, start_method="spawn")
+        mp.start_processes(_rank_main, args=(world, _free_port(), d, env, cases), nprocs=world, join=True,
+                           start_method="spawn")
         res = [np.load(os.path.join(d, f"rank{r}.npy"), allow_pickle=True)[0] for r in range(world)]
+    tag = " ".join(f"{k}={v}" for k, v in (env or {}).items())
     r0 = res[0]
     for (name, kind, eff), (toks_tp, logits_tp, sel_tp) in r0.items():
         if kind != "tp":
@@ -131,7 +137,7 @@ def test_tp_matches_single_gpu(iam, cuda):
         ntok = int(np.argmax(toks_tp != toks_1)) if (toks_tp != toks_1).any() else len(toks_1)
         nsel = int(np.all(sel == sel_1, axis=(1, 2)).sum())
         nlog = int(sum(np.array_equal(a.view(np.uint32), b.view(np.uint32)) for a, b in zip(logits_tp, logits_1)))
-        print(f"tp{world} {name} effort {eff}: {nlog}/{len(logits_1)} steps with bit-identical logits, "
+        print(f"tp{world}{' ' + tag if tag else ''} {name} effort {eff}: {nlog}/{len(logits_1)} steps with bit-identical logits, "
               f"{nsel}/{len(sel_1)} with identical selections; free-running greedy tokens equal for "
               f"{ntok}/{len(toks_1)}")
         assert np.array_equal(toks_tp, toks_1), (name, eff, toks_tp, toks_1)
@@ -143,3 +149,12 @@ def test_tp_matches_single_gpu(iam, cuda):
             assert np.array_equal(l_r, logits_tp), (name, eff)
             assert np.array_equal(t_r, toks_tp), (name, eff)
             assert np.array_equal(s_r[:, :, :3], sel_tp[:, :, :3]), (name, eff)
+
+
+def test_tp_matches_single_gpu(iam, cuda):
+    _check_identical(WORLD)
+
+
+@pytest.mark.parametrize("env", [{"IAM_TP_PUSH": "0"}, {"IAM_TP_FUSED": "0"}], ids=["allgather", "gather_reduce"])
+def test_tp_exchange_launches_match_single_gpu(iam, cuda, env):
+    _check_identical(WORLD, env, cases=(("small", SMALL, 3, (0.25, 1.0), 0),))
