@@ -9,7 +9,8 @@ independent numpy restatement of bucketMul.cl:68-214 (cutoff), :351-386 (dispatc
 :392-447 (accumulation): the reference's OpenCL cannot execute here, so those values are a
 second restatement the C oracle is cross-checked against, not an executed reference.
 
-Usage:  python tests/golden/make_golden.py [--reference /path/to/reference]
+Usage:  python tests/golden/make_golden.py --reference <reference checkout>
+        (or IAM_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py)
 The fixtures are small .npz files; nothing here is needed at test time except them.
 """
 import argparse
@@ -164,8 +165,11 @@ def torch_tie_order(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("IAM_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("IAM_REFERENCE_DIR"),
+                    help="the reference checkout (default: $IAM_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set IAM_REFERENCE_DIR")
     ref = load_reference(args.reference)
     packing_kat(ref)
     torch_tie_order(ref)
