@@ -241,7 +241,7 @@ struct iam_model_s {
     int* gen_tokens = nullptr;
     std::vector<void*> allocs;
     int n_heads_local = 0, n_kv_local = 0, ffn_local = 0;
-    long long* tp_tmp = nullptr;  // 2 int64 of device scratch for host-side agreements
+    long long* tp_tmp = nullptr;  // 4 int64 of device scratch for host-side agreements
     // one-shot NVLink collectives (IAM_TP_COLL=nccl: NCCL instead)
     bool tp_p2p = true;
     bool tp_fused = true;       // o / down exchanges inside the bucketMul kernel (IAM_TP_FUSED=0: a launch after it)
@@ -511,15 +511,29 @@ int tp_map_peers(iam_model_s* m) {
 
 // Every rank of the group learns whether all ranks got here with rc == IAM_OK (a rank that
 // failed to build still takes part, so no rank waits on it in a later collective).
+// The settings every rank of a group must share: which exchanges run and where (a rank that
+// launched a different sequence of exchanges, or a different range layout, would wait for
+// peers that never send).
+long long tp_settings(const iam_model_s* m) {
+    uint32_t dense_bits;
+    std::memcpy(&dense_bits, &m->dense_min_effort, sizeof(dense_bits));
+    return ((long long)dense_bits << 8) | (m->tp_p2p ? 1 : 0) | (m->tp_fused ? 2 : 0) | (m->tp_push ? 4 : 0) |
+           (m->use_group ? 8 : 0);
+}
+
 int tp_agree(iam_model_s* m, int rc) {
     if (m->tp_world == 1) return rc;
-    long long h[2] = {rc != IAM_OK ? 1 : 0, 0};
+    const long long mine = tp_settings(m);
+    long long h[4] = {rc != IAM_OK ? 1 : 0, mine, -mine, 0};  // max of each: any failure, settings range
     IAM_CUDA_TRY(cudaMemcpy(m->tp_tmp, h, sizeof(h), cudaMemcpyHostToDevice));
-    int r2 = nccl_done(m, ncclAllReduce(m->tp_tmp, m->tp_tmp, 1, ncclInt64, ncclMax, m->comm, 0), "status all-reduce");
+    int r2 = nccl_done(m, ncclAllReduce(m->tp_tmp, m->tp_tmp, 3, ncclInt64, ncclMax, m->comm, 0), "status all-reduce");
     if (r2) return r2;
     IAM_CUDA_TRY(cudaMemcpy(h, m->tp_tmp, sizeof(h), cudaMemcpyDeviceToHost));
     if (rc) return rc;
     if (h[0]) return fail(IAM_ERR_UNSUPPORTED, "tensor parallel: another rank failed to build its shard");
+    if (h[1] != mine || -h[2] != mine)
+        return fail(IAM_ERR_ARG, "tensor parallel: the ranks were started with different exchange settings "
+                                 "(IAM_TP_COLL, IAM_TP_FUSED, IAM_TP_PUSH, IAM_BM_KERNEL, IAM_DENSE_MIN_EFFORT)");
     return IAM_OK;
 }
 
@@ -1238,7 +1252,7 @@ int init_common(iam_model_s* m, const iam_model_config* cfg, int device, int ran
     m->vocab0 = rank * m->vocab_local;
     if (world > 1) {
         if (!nccl_id) return fail(IAM_ERR_ARG, "tensor parallel: null NCCL id");
-        if ((rc = dalloc(m, &m->tp_tmp, 2))) return rc;
+        if ((rc = dalloc(m, &m->tp_tmp, 4))) return rc;
         ncclUniqueId id;
         std::memcpy(&id, nccl_id, sizeof(id));
         ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;

@@ -158,3 +158,43 @@ def test_tp_matches_single_gpu(iam, cuda):
 @pytest.mark.parametrize("env", [{"IAM_TP_PUSH": "0"}, {"IAM_TP_FUSED": "0"}], ids=["allgather", "gather_reduce"])
 def test_tp_exchange_launches_match_single_gpu(iam, cuda, env):
     _check_identical(WORLD, env, cases=(("small", SMALL, 3, (0.25, 1.0), 0),))
+
+
+def _mismatch_main(rank, world, port, outdir):
+    import sys
+    if rank == world - 1:
+        os.environ["IAM_TP_PUSH"] = "0"  # this rank alone: the exchange launches put back
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import torch
+    import torch.distributed as dist
+    from conftest import load_pkg
+    iam = load_pkg()
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=180))
+    uid = [iam.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    try:
+        iam.Model.random(iam.ModelConfig.make(**SMALL), seed=3, device=rank, tp=(rank, world, uid[0])).close()
+        code = 0
+    except iam.IamError as e:
+        code = e.code
+    with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
+        f.write(str(code))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_tp_mismatched_settings_refused(iam, cuda):
+    """Ranks started with different exchange settings would launch different exchange
+    sequences and wait on each other; model creation refuses them on every rank instead."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"tensor-parallel test needs {WORLD} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_mismatch_main, args=(WORLD, _free_port(), d), nprocs=WORLD, join=True,
+                           start_method="spawn")
+        codes = [int(open(os.path.join(d, f"rank{r}.txt")).read()) for r in range(WORLD)]
+    assert codes == [iam.IAM_ERR_ARG] * WORLD, codes
