@@ -1213,11 +1213,6 @@ int build_dense_copies(iam_model_s* m) {
 }
 
 int finish_create(iam_model_s* m, iam_model_t* out) {
-    int rc = build_dense_copies(m);
-    if (rc) {
-        free_model(m);
-        return rc;
-    }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         free_model(m);
@@ -1310,6 +1305,7 @@ int create_random(iam_model_t* out, const iam_model_config* cfg, unsigned long l
     cudaFree(wtmp);
     cudaFree(btmp);
     if (!rc) rc = alloc_runtime(m);
+    if (!rc) rc = build_dense_copies(m);  // before the agreement: a rank that fails here stops every rank
     rc = tp_agree(m, rc);
     if (!rc) rc = tp_agree(m, tp_map_peers(m));
     if (rc) {
@@ -1353,6 +1349,7 @@ int load_model(iam_model_t* out, const char* weights_dir, const iam_model_config
         }
     }
     if (!rc) rc = alloc_runtime(m);
+    if (!rc) rc = build_dense_copies(m);  // before the agreement: a rank that fails here stops every rank
     rc = tp_agree(m, rc);
     if (!rc) rc = tp_agree(m, tp_map_peers(m));
     if (rc) {
